@@ -1,0 +1,235 @@
+// Host side of the tcgen05 GEMM: tensor maps, tile/split selection, split-K
+// reduction.  Exposed to Python through ops.cpp.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+#include "status.h"
+
+namespace mb {
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(p != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, cols] matrix with leading dimension ld
+// (elements); box = 64 columns (128 B, the swizzle span) x box_rows rows.
+CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+template <int BN, int STAGES, bool DUAL>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, cudaStream_t st) {
+  using L = GemmSmem<BN, STAGES, DUAL>;
+  auto k = gemm_tc_kernel<BN, STAGES, DUAL>;
+  static bool attr = false;  // per instantiation
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    attr = true;
+  }
+  k<<<grid, 192, L::kBytes, st>>>(ta, tb, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Dispatch on the N tile.  DUAL keeps 4 accumulators of BN columns in TMEM,
+// so it stops at BN = 128.
+static void dispatch(int bn, bool dual, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid,
+                     cudaStream_t st) {
+  if (dual) {
+    switch (bn) {
+      case 16: return launch<16, 6, true>(ta, tb, a, grid, st);
+      case 32: return launch<32, 6, true>(ta, tb, a, grid, st);
+      case 64: return launch<64, 5, true>(ta, tb, a, grid, st);
+      default: return launch<128, 4, true>(ta, tb, a, grid, st);
+    }
+  }
+  switch (bn) {
+    case 16: return launch<16, 8, false>(ta, tb, a, grid, st);
+    case 32: return launch<32, 8, false>(ta, tb, a, grid, st);
+    case 64: return launch<64, 6, false>(ta, tb, a, grid, st);
+    case 128: return launch<128, 5, false>(ta, tb, a, grid, st);
+    default: return launch<256, 4, false>(ta, tb, a, grid, st);
+  }
+}
+
+static int pick_bn(int64_t rows, bool dual) {
+  int cap = dual ? 128 : 256;
+  int bn = 16;
+  while (bn < rows && bn < cap) bn *= 2;
+  return bn;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, c10::cuda::current_device()));
+  return n;
+}
+
+// split-K reduction: out = bf16(sum_s ws[s] (+ residual))
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t n,
+                                     const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out) {
+  int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= n) return;
+  float4 acc = *reinterpret_cast<const float4*>(ws + i);
+  for (int s = 1; s < splits; ++s) {
+    float4 v = *reinterpret_cast<const float4*>(ws + (int64_t)s * n + i);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if (residual) {
+    acc.x += __bfloat162float(residual[i]);
+    acc.y += __bfloat162float(residual[i + 1]);
+    acc.z += __bfloat162float(residual[i + 2]);
+    acc.w += __bfloat162float(residual[i + 3]);
+  }
+  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+  reinterpret_cast<__nv_bfloat162*>(out + i)[0] = lo;
+  reinterpret_cast<__nv_bfloat162*>(out + i)[1] = hi;
+}
+
+// y[T, N] = x[T, K] @ w[N, K]^T (+ residual).  `workspace` (fp32, may be
+// empty) enables split-K for decode shapes that would otherwise leave SMs idle.
+void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,
+            const c10::optional<at::Tensor>& workspace, int64_t splits_req) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && y.is_cuda());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && y.is_contiguous());
+  const int64_t T = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && y.size(0) == T && y.size(1) == N);
+  TORCH_CHECK(K % 8 == 0, "K must be a multiple of 8");
+  if (T == 0) return;
+  const __nv_bfloat16* res = nullptr;
+  if (residual && residual->defined()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == y.sizes());
+    res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  GemmArgs a{};
+  a.K = (int)K;
+  a.groups = 1;
+  a.ldc = (int)N;
+  a.out_rows = (int)T;
+  a.status = status_ptr(x.device().index());
+  a.residual = res;
+  const bool swap = (T <= 256) && (N % 128 == 0);
+  if (swap) {
+    const int bn = pick_bn(T, false);
+    auto ta = make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), 128);
+    auto tb = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
+    a.a_rows = (int)N;
+    a.b_rows = (int)T;
+    a.swap = 1;
+    const int m_tiles = (int)(N / 128);
+    const int kb = (int)((K + 63) / 64);
+    int splits = (int)splits_req;
+    if (splits <= 0) {
+      splits = 1;
+      while (m_tiles * splits * 2 <= num_sms() && splits * 2 <= kb / 4) splits *= 2;
+    }
+    bool use_ws = splits > 1 && workspace && workspace->defined() &&
+                  workspace->numel() >= (int64_t)splits * T * N && (T * N) % 4 == 0;
+    if (!use_ws) splits = 1;
+    a.splits = splits;
+    if (splits > 1) {
+      a.mode = kEpiPartialF32;
+      a.out = workspace->data_ptr();
+      a.residual = nullptr;
+    } else {
+      a.mode = kEpiStore;
+      a.out = y.data_ptr();
+    }
+    dispatch(bn, false, ta, tb, a, dim3(m_tiles, 1, splits), st);
+    if (splits > 1) {
+      int64_t n = T * N;
+      int threads = 256;
+      int64_t blocks = (n / 4 + threads - 1) / threads;
+      splitk_reduce_kernel<<<blocks, threads, 0, st>>>(workspace->data_ptr<float>(), splits, n, res,
+                                                     reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+    }
+  } else {
+    // Normal orientation: 128 activation rows x BN weight rows per tile.
+    const int bn = N >= 256 ? 256 : pick_bn(N, false);
+    auto ta = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), 128);
+    auto tb = make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), bn);
+    a.a_rows = (int)((T + 127) / 128 * 128);
+    a.b_rows = (int)N;
+    a.swap = 0;
+    a.splits = 1;
+    a.mode = kEpiStore;
+    a.out = y.data_ptr();
+    const int m_tiles = (int)((T + 127) / 128);
+    const int n_tiles = (int)((N + bn - 1) / bn);
+    // Each CTA walks N tiles with stride gridDim.y; cap the grid near a few
+    // waves so TMEM double-buffering overlaps epilogue and MMA.
+    int ny = n_tiles;
+    const int target = num_sms() * 2;
+    while ((int64_t)m_tiles * ny > target && ny > 1) ny = (ny + 1) / 2;
+    dispatch(bn, false, ta, tb, a, dim3(m_tiles, ny, 1), st);
+  }
+}
+
+// Grouped (MoE) GEMM, swap orientation.  w: [G * rows_per_group, K] (experts
+// stacked), x: [R, K] tokens sorted by group, offs: [G+1] int32 on device.
+// SwiGLU mode: each group holds [gate; up] rows (2*I) and y gets I columns.
+void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
+                    int64_t groups, bool swiglu, int64_t max_rows_per_group) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(offs.scalar_type() == at::kInt && offs.numel() == groups + 1);
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && y.is_contiguous());
+  const int64_t R = x.size(0), K = x.size(1);
+  const int64_t rows_pg = w.size(0) / groups;
+  TORCH_CHECK(rows_pg * groups == w.size(0) && w.size(1) == K);
+  const int64_t n_out = swiglu ? rows_pg / 2 : rows_pg;
+  TORCH_CHECK(n_out % 128 == 0, "grouped GEMM needs output features % 128 == 0");
+  TORCH_CHECK(y.size(0) == R && y.size(1) == n_out);
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int bn = pick_bn(std::max<int64_t>(1, max_rows_per_group), swiglu);
+  auto ta = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, 128);
+  auto tb = make_tmap_bf16(x.data_ptr(), R, K, K, bn);
+  GemmArgs a{};
+  a.K = (int)K;
+  a.a_rows = (int)rows_pg;
+  a.a_up_offset = swiglu ? (int)n_out : 0;
+  a.b_offs = offs.data_ptr<int>();
+  a.groups = (int)groups;
+  a.splits = 1;
+  a.swap = 1;
+  a.mode = swiglu ? kEpiSwiGLU : kEpiStore;
+  a.out = y.data_ptr();
+  a.ldc = (int)n_out;
+  a.out_rows = (int)R;
+  a.status = status_ptr(x.device().index());
+  const int m_tiles = (int)(n_out / 128);
+  // gridDim.y splits a group's token tiles across CTAs when groups are large.
+  int ny = (int)std::max<int64_t>(1, std::min<int64_t>((max_rows_per_group + bn - 1) / bn, 8));
+  dispatch(bn, swiglu, ta, tb, a, dim3(m_tiles, ny, groups), st);
+}
+
+}  // namespace mb

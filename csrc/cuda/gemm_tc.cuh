@@ -1,0 +1,254 @@
+// bf16 GEMM on 5th-generation tensor cores (tcgen05 + TMEM), TMA-fed.
+//
+//   D[i, j] = sum_k A[i, k] * B[j, k]        (both operands K-major, bf16)
+//
+// A is the "M side" (128 rows per tile, one TMEM lane per row) and B the
+// "N side" (BN rows per tile, one TMEM column per row).  Linear layers run in
+// one of two orientations:
+//   * swap   : A = weight [out, in], B = activations [tokens, in].  Decode and
+//              MoE shapes have few tokens, so the 128-row MMA dimension is
+//              filled by weight rows and the token count only sets BN.
+//   * normal : A = activations, B = weight (large-M prefill).
+// Grouped mode (MoE experts): group g uses A rows [g*a_group_rows, ...) and
+// B rows [offs[g], offs[g+1]) where offs lives in device memory, so the
+// schedule needs no host synchronisation and is CUDA-graph safe.
+//
+// CTA = 6 warps: warp 0 issues TMA loads, warp 1 allocates TMEM and issues
+// tcgen05.mma from one elected lane, warps 2-5 drain TMEM accumulators
+// (double-buffered, so the epilogue of tile t overlaps the MMAs of t+1).
+// Replaces the reference's FP32 SIMT matmul/linear kernels
+// (pio/plugins/cuda/c_src/tensor_ops_cuda.cu:290-329).
+#pragma once
+#include "common.cuh"
+
+namespace mb {
+
+enum EpiMode : int {
+  kEpiStore = 0,      // bf16 store of D (optionally + bf16 residual)
+  kEpiSwiGLU = 1,     // dual accumulator: silu(D_gate) * D_up
+  kEpiPartialF32 = 2, // fp32 split-K partial to a workspace
+};
+
+struct GemmArgs {
+  int K;                 // reduction length
+  int a_rows;            // rows of A per group (multiple of 128)
+  int a_up_offset;       // SwiGLU: row offset of the "up" half inside a group
+  int b_rows;            // dense mode: rows of B; grouped mode: unused
+  const int* b_offs;     // grouped mode: [groups+1] row offsets into B (device)
+  int groups;
+  int splits;            // split-K factor
+  int swap;              // 1: out[j, i] ; 0: out[i, j]
+  int mode;              // EpiMode
+  void* out;             // bf16 [tokens, ldc] or f32 [splits, tokens, ldc]
+  const __nv_bfloat16* residual;  // optional, same layout as out
+  int ldc;
+  int out_rows;          // tokens (rows of out) for the split-K workspace stride
+  int* status;
+};
+
+template <int BN, int STAGES, bool DUAL>
+struct GemmSmem {
+  static constexpr int kABytes = 128 * 64 * 2;
+  static constexpr int kBBytes = BN * 64 * 2;
+  static constexpr int kStageBytes = kABytes * (DUAL ? 2 : 1) + kBBytes;
+  static constexpr int kBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int STAGES, bool DUAL>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   GemmArgs args) {
+  using L = GemmSmem<BN, STAGES, DUAL>;
+  constexpr int kAcc = DUAL ? 2 * BN : BN;          // TMEM columns per buffer
+  constexpr int kTmemCols = (2 * kAcc <= 32) ? 32 : (2 * kAcc <= 64) ? 64 : (2 * kAcc <= 128) ? 128
+                            : (2 * kAcc <= 256) ? 256 : 512;
+  static_assert(2 * kAcc <= 512, "TMEM overflow");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;   // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tile = blockIdx.x;
+  const int g = blockIdx.z / args.splits;
+  const int split = blockIdx.z % args.splits;
+
+  // Work of this CTA: N tiles nt = blockIdx.y + r*gridDim.y of group g, over
+  // this split's K-block range.
+  int b0, cnt;
+  if (args.b_offs) {
+    b0 = __ldg(args.b_offs + g);
+    cnt = __ldg(args.b_offs + g + 1) - b0;
+  } else {
+    b0 = 0;
+    cnt = args.b_rows;
+  }
+  const int n_tiles = (cnt + BN - 1) / BN;
+  const int my_tiles = n_tiles > (int)blockIdx.y ? (n_tiles - 1 - (int)blockIdx.y) / (int)gridDim.y + 1 : 0;
+  const int kb_total = (args.K + 63) / 64;
+  const int kb_per = (kb_total + args.splits - 1) / args.splits;
+  const int kb_lo = split * kb_per;
+  const int kb_hi = min(kb_total, kb_lo + kb_per);
+  const int kbs = max(0, kb_hi - kb_lo);
+  const int a_row0 = g * args.a_rows + m_tile * 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (my_tiles > 0 && kbs > 0) {
+    if (warp == 0) {
+      // ------------------------------------------------ TMA producer
+      if (elect_one_sync()) {
+        int it = 0;
+        bool ok = true;
+        for (int t = 0; t < my_tiles && ok; ++t) {
+          const int nt = blockIdx.y + t * gridDim.y;
+          for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, args.status)) { ok = false; break; }
+            uint8_t* st = smem + s * L::kStageBytes;
+            mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+            tma_load_2d(st, &tmA, &full[s], kb * 64, a_row0);
+            if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], kb * 64, a_row0 + args.a_up_offset);
+            tma_load_2d(st + L::kABytes * (DUAL ? 2 : 1), &tmB, &full[s], kb * 64, b0 + nt * BN);
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = make_idesc_bf16(128, BN);
+      if (elect_one_sync()) {
+        int it = 0;
+        bool ok = true;
+        for (int t = 0; t < my_tiles && ok; ++t) {
+          const int buf = t & 1;
+          if (!mbar_wait(&tempty[buf], ((t >> 1) & 1) ^ 1, args.status)) break;
+          tc_fence_after();
+          const uint32_t d0 = tmem_base + buf * kAcc;
+          for (int kb = 0; kb < kbs; ++kb, ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
+            if (!mbar_wait(&full[s], ph, args.status)) { ok = false; break; }
+            tc_fence_after();
+            uint8_t* st = smem + s * L::kStageBytes;
+            const uint32_t a_addr = smem_u32(st);
+            const uint32_t b_addr = smem_u32(st + L::kABytes * (DUAL ? 2 : 1));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bd = make_sdesc_k128(b_addr + kk * 32);
+              tc_mma_bf16(d0, make_sdesc_k128(a_addr + kk * 32), bd, idesc, (kb | kk) != 0);
+              if (DUAL) tc_mma_bf16(d0 + BN, make_sdesc_k128(a_addr + L::kABytes + kk * 32), bd, idesc, (kb | kk) != 0);
+            }
+            tc_commit(&empty[s]);
+          }
+          tc_commit(&tfull[buf]);
+        }
+      }
+    } else {
+      // ------------------------------------------------ epilogue (warps 2-5)
+      const int lane_base = (warp & 3) * 32;
+      const int i = lane_base + lane;             // accumulator row (TMEM lane)
+      for (int t = 0; t < my_tiles; ++t) {
+        const int buf = t & 1;
+        const int nt = blockIdx.y + t * gridDim.y;
+        if (!mbar_wait(&tfull[buf], (t >> 1) & 1, args.status)) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kAcc;
+        const int arow = m_tile * 128 + i;        // row of A inside the group
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(taddr + c0, v);
+          if (DUAL) {
+            float u[16];
+            tmem_ld16(taddr + BN + c0, u);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] = silu(v[q]) * u[q];
+          }
+          const int jbase = nt * BN + c0;         // B row inside the group
+          if (args.swap) {
+            // out[(b0 + j), arow]: lanes of a warp write consecutive columns.
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const int j = jbase + q;
+              if (j < cnt) {
+                const size_t o = (size_t)(b0 + j) * args.ldc + arow;
+                if (args.mode == kEpiPartialF32) {
+                  reinterpret_cast<float*>(args.out)[(size_t)split * args.out_rows * args.ldc + o] = v[q];
+                } else {
+                  float r = args.residual ? __bfloat162float(args.residual[o]) : 0.f;
+                  reinterpret_cast<__nv_bfloat16*>(args.out)[o] = __float2bfloat16(v[q] + r);
+                }
+              }
+            }
+          } else {
+            // out[arow, j]: 16 consecutive columns per thread.
+            const int grow = g * args.a_rows + arow;
+            if (grow < args.out_rows) {
+              const size_t o = (size_t)grow * args.ldc + jbase;
+              if (args.mode == kEpiPartialF32) {
+                float* dst = reinterpret_cast<float*>(args.out) + (size_t)split * args.out_rows * args.ldc + o;
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (jbase + q < cnt) dst[q] = v[q];
+              } else if (jbase + 16 <= cnt && (args.ldc & 7) == 0) {
+                __align__(16) __nv_bfloat16 h[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                  float r = args.residual ? __bfloat162float(args.residual[o + q]) : 0.f;
+                  h[q] = __float2bfloat16(v[q] + r);
+                }
+                uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) + o);
+                d[0] = reinterpret_cast<uint4*>(h)[0];
+                d[1] = reinterpret_cast<uint4*>(h)[1];
+              } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (jbase + q < cnt) {
+                    float r = args.residual ? __bfloat162float(args.residual[o + q]) : 0.f;
+                    reinterpret_cast<__nv_bfloat16*>(args.out)[o + q] = __float2bfloat16(v[q] + r);
+                  }
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace mb

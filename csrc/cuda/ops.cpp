@@ -1,0 +1,47 @@
+// Python bindings of the sm_100a kernels (module mod_b200._C).
+#include <torch/extension.h>
+#include "status.h"
+
+namespace mb {
+void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,
+            const c10::optional<at::Tensor>& workspace, int64_t splits);
+void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y, int64_t groups,
+                    bool swiglu, int64_t max_rows_per_group);
+void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
+             double eps);
+void rope_qknorm(const at::Tensor& qkv, const c10::optional<at::Tensor>& q_w, const c10::optional<at::Tensor>& k_w,
+                 const at::Tensor& positions, const at::Tensor& inv_freq, const c10::optional<at::Tensor>& slots,
+                 at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t D,
+                 int64_t rot_dim, double eps);
+void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                 const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
+                 const c10::optional<at::Tensor>& workspace, double scale);
+void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids, at::Tensor& wts,
+               at::Tensor& counts, at::Tensor& offs, at::Tensor& cursor);
+void moe_permute(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& offs, at::Tensor& cursor,
+                 at::Tensor& pos, at::Tensor& xs);
+void moe_combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& wts,
+                 const c10::optional<at::Tensor>& residual, at::Tensor& out);
+void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
+void swiglu(const at::Tensor& gu, at::Tensor& out);
+void argmax(const at::Tensor& logits, at::Tensor& out_idx, const c10::optional<at::Tensor>& out_val,
+            int64_t index_offset);
+void verify_tokens(const at::Tensor& draft, const at::Tensor& target, at::Tensor& out);
+}  // namespace mb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "mod_b200 sm_100a kernels";
+  m.def("linear", &mb::linear);
+  m.def("grouped_linear", &mb::grouped_linear);
+  m.def("rmsnorm", &mb::rmsnorm);
+  m.def("rope_qknorm", &mb::rope_qknorm);
+  m.def("attn_decode", &mb::attn_decode);
+  m.def("moe_route", &mb::moe_route);
+  m.def("moe_permute", &mb::moe_permute);
+  m.def("moe_combine", &mb::moe_combine);
+  m.def("embed", &mb::embed);
+  m.def("swiglu", &mb::swiglu);
+  m.def("argmax", &mb::argmax);
+  m.def("verify_tokens", &mb::verify_tokens);
+  m.def("read_and_clear_status", &mb::read_and_clear_status);
+}

@@ -1,0 +1,134 @@
+"""LLMEngine: the public serving API.
+
+    eng = LLMEngine.from_preset("qwen3-30b-a3b", backend="native")
+    outs = eng.generate([[1, 2, 3]], SamplingParams(max_new_tokens=32))
+
+``add_request`` / ``step`` / ``has_unfinished`` give the incremental form a
+serving loop or the streaming front-end uses; ``generate`` drives them to
+completion.  The reference's per-plugin ``generate_text`` /
+``BatchManager.add_request/step`` (``pio/models/qwen3_0_6b/plugin.py:139-152``,
+``pio/common/managers/batch_manager.py:9-84``) map onto this.
+"""
+from __future__ import annotations
+
+import logging
+import time
+from typing import Dict, List, Optional, Sequence as Seq, Union
+
+import torch
+
+from ..config.models import ModelConfig
+from ..config.presets import get_preset
+from ..models.backend import make_backend
+from ..models.decoder import DecoderLM
+from ..models.weights import ModelWeights, random_weights
+from .block_manager import BlockManager
+from .kv_cache import KVCache, StateCache
+from .runner import ModelRunner
+from .scheduler import Scheduler
+from .sequence import SamplingParams, Sequence, SeqStatus
+
+log = logging.getLogger("mod_b200.engine")
+
+
+class LLMEngine:
+    def __init__(self, cfg: ModelConfig, weights: Optional[ModelWeights] = None, backend: str = "native",
+                 device: Union[str, torch.device] = "cuda", max_batch: int = 128, max_model_len: int = 4096,
+                 num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
+                 max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if weights is None and model is None:
+            weights = random_weights(cfg, device=self.device, seed=seed)
+        self.backend = make_backend(backend)
+        self.model = model if model is not None else DecoderLM(cfg, weights, self.backend)
+        bs = 16
+        if num_blocks is None:
+            num_blocks = self._auto_blocks(kv_mem_fraction, max_batch, max_model_len, kv_heads)
+        self.kv = KVCache(cfg, num_blocks, self.device, dtype=self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
+        has_delta = any(cfg.layer_type(i) == "linear_attention" for i in range(cfg.num_hidden_layers))
+        self.states = StateCache(cfg, max_batch + 1, self.device) if has_delta else None
+        self.blocks = BlockManager(num_blocks, bs, max_seqs=max_batch)
+        self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens)
+        self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
+                                  use_graphs=use_graphs, device=self.device)
+        self.seqs: Dict[int, Sequence] = {}
+        self.last_step: Dict[str, float] = {}
+
+    @classmethod
+    def from_preset(cls, name: str, **kw) -> "LLMEngine":
+        return cls(get_preset(name), **kw)
+
+    def _auto_blocks(self, frac, max_batch, max_model_len, kv_heads) -> int:
+        per_block = KVCache.bytes_per_block(self.cfg, num_kv_heads=kv_heads or self.model.Hkv)
+        want = max_batch * ((max_model_len + 15) // 16) + max_batch
+        if self.device.type != "cuda" or per_block == 0:
+            return max(want, 16)
+        free, _ = torch.cuda.mem_get_info(self.device)
+        cap = int(free * frac) // per_block
+        return max(16, min(want, cap))
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt: Seq[int], params: Optional[SamplingParams] = None, images=None,
+                    callback=None) -> int:
+        seq = Sequence(prompt=list(int(t) for t in prompt), params=params or SamplingParams())
+        seq.images, seq.callback = images, callback
+        self.seqs[seq.req_id] = seq
+        self.scheduler.add(seq)
+        return seq.req_id
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    def step(self) -> List[Sequence]:
+        """Runs one prefill or decode step; returns sequences that finished in it."""
+        sched = self.scheduler.schedule()
+        if not sched.seqs:
+            return []
+        t0 = time.perf_counter()
+        try:
+            if sched.is_decode:
+                toks = self.runner.decode(sched.seqs)
+            else:
+                toks = self.runner.prefill(sched.seqs, sched.query_lens, self._embeds(sched))
+        except Exception as e:  # fail the step's requests, keep serving others
+            log.error("step failed: %s", e)
+            for s in sched.seqs:
+                s.error = repr(e)
+                self.scheduler.finish(s, SeqStatus.FAILED)
+            return list(sched.seqs)
+        now = time.perf_counter()
+        self.last_step = {"kind": 1.0 if sched.is_decode else 0.0, "seconds": now - t0, "batch": len(sched.seqs)}
+        done = []
+        for s, t in zip(sched.seqs, toks):
+            if s.t_first_token is None:
+                s.t_first_token = now
+            s.output.append(int(t))
+            if s.callback is not None:
+                s.callback(s, int(t))
+            if s.finished_by(int(t)):
+                s.t_finish = now
+                self.scheduler.finish(s)
+                done.append(s)
+        return done
+
+    def _embeds(self, sched):
+        hook = getattr(self.model, "prefill_embeds", None)
+        return hook(sched) if hook is not None else None
+
+    def generate(self, prompts: List[Seq[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
+        ids = [self.add_request(p, params) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        out = []
+        for i in ids:
+            s = self.seqs.pop(i)
+            if s.status == SeqStatus.FAILED:
+                raise RuntimeError(f"request {i} failed: {s.error}")
+            out.append(s.output)
+        return out
+
+    def stats(self) -> Dict[str, float]:
+        return {"free_blocks": self.blocks.num_free, "running": len(self.scheduler.running),
+                "waiting": len(self.scheduler.waiting), "preempted": self.scheduler.num_preempted,
+                "h2d_bytes_last_step": self.runner.h2d_bytes, "d2h_bytes_last_step": self.runner.d2h_bytes}

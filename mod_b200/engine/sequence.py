@@ -1,0 +1,70 @@
+"""Requests and sampling parameters.
+
+Mirrors the reference's request lifecycle in ``BatchManager``
+(``pio/common/managers/batch_manager.py:9-84``: add_request / step / status,
+FAILED on exception) but for a continuous batcher.
+"""
+from __future__ import annotations
+
+import enum
+import itertools
+import time
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+
+class SeqStatus(enum.Enum):
+    WAITING = "waiting"
+    RUNNING = "running"
+    FINISHED = "finished"
+    FAILED = "failed"
+
+
+@dataclass
+class SamplingParams:
+    max_new_tokens: int = 16
+    temperature: float = 0.0          # 0 -> greedy
+    top_p: float = 1.0
+    top_k: int = 0
+    eos_token_id: Optional[int] = None
+    ignore_eos: bool = False
+    seed: Optional[int] = None
+
+
+_ids = itertools.count()
+
+
+@dataclass
+class Sequence:
+    prompt: List[int]
+    params: SamplingParams = field(default_factory=SamplingParams)
+    req_id: int = field(default_factory=lambda: next(_ids))
+    output: List[int] = field(default_factory=list)
+    status: SeqStatus = SeqStatus.WAITING
+    blocks: List[int] = field(default_factory=list)
+    state_slot: int = -1
+    num_cached: int = 0               # tokens whose KV is in the cache
+    error: Optional[str] = None
+    t_arrival: float = field(default_factory=time.perf_counter)
+    t_first_token: Optional[float] = None
+    t_finish: Optional[float] = None
+    images: Optional[object] = None   # pixel tensor for vision-language prompts
+    callback: Optional[object] = None  # streaming: callback(seq, token)
+
+    @property
+    def all_tokens(self) -> List[int]:
+        return self.prompt + self.output
+
+    @property
+    def length(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    def finished_by(self, token: int) -> bool:
+        p = self.params
+        if not p.ignore_eos and p.eos_token_id is not None and token == p.eos_token_id:
+            return True
+        return len(self.output) >= p.max_new_tokens
+
+    @property
+    def ttft(self) -> Optional[float]:
+        return None if self.t_first_token is None else self.t_first_token - self.t_arrival

@@ -1,0 +1,168 @@
+"""Op backends the model layers call.
+
+* :class:`NativeBackend`  - the product path: sm_100a kernels from ``mod_b200._C``.
+* :class:`TorchBackend`   - the baseline: PyTorch ops, cuBLAS GEMMs (``torch.matmul``),
+  SDPA attention.  Also runs on CPU, where it backs the CPU tests.
+
+Both take and return bf16 tensors and the same buffer conventions, so a model
+switches paths with one constructor argument.  The reference's equivalent is
+the ctypes ``Tensor`` method table (``pio/core/engine/backend.py:332-654``).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from ..ops import reference as R
+
+
+class TorchBackend:
+    name = "torch"
+
+    def linear(self, x, w, bias=None, residual=None, out=None):
+        y = R.linear(x, w, residual=residual)
+        if bias is not None:
+            y = y + bias
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+    def rmsnorm(self, x, w, eps, residual=None):
+        return R.rmsnorm(x, w, eps, residual=residual)
+
+    def swiglu_mlp(self, x, gate_up, down, residual=None):
+        h = R.swiglu(R.linear(x, gate_up))
+        return R.linear(h, down, residual=residual)
+
+    def rope_qknorm(self, qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps):
+        return R.rope_qknorm(qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps)
+
+    def attn_decode(self, q, k_cache, v_cache, block_tables, ctx_lens, splits=1):
+        return R.attn_decode_batched(q, k_cache, v_cache, block_tables, ctx_lens)
+
+    def attn_prefill(self, q, k, v):
+        return R.attn_prefill(q, k, v)
+
+    def moe(self, x, mo, top_k, renorm, inter, residual=None):
+        """Full routed-expert block on all experts held by this process."""
+        logits = R.linear(x, mo.router)
+        ids, wts = R.moe_route(logits, top_k, renorm)
+        E = mo.e_hi - mo.e_lo
+        out = R.moe_experts(x, ids - mo.e_lo, wts, mo.w13, mo.w2, E, inter)
+        if mo.shared is not None:
+            sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down).float()
+            out = out + torch.sigmoid(R.linear(x, mo.shared_gate).float()) * sh
+        if residual is not None:
+            out = out + residual.float()
+        return out.to(x.dtype)
+
+    def embed(self, ids, table):
+        return R.embed(ids, table)
+
+    def argmax(self, logits):
+        return R.argmax(logits)
+
+
+class NativeBackend:
+    """sm_100a kernels.  Scratch tensors come from the caching allocator, so a
+    captured CUDA graph owns them through its private memory pool."""
+
+    name = "native"
+
+    def __init__(self):
+        from ..ops import native as N
+        from ..ops import load_extension
+
+        load_extension()
+        self.N = N
+        self._one_group = {}
+
+    def _offs1(self, T, device):
+        # built by a kernel (no host copy), so it is legal inside graph capture
+        return torch.arange(2, dtype=torch.int32, device=device) * T
+
+    def linear(self, x, w, bias=None, residual=None, out=None):
+        T = x.reshape(-1, x.shape[-1]).shape[0]
+        ws = None
+        if T <= 256 and w.shape[0] % 128 == 0:
+            # split-K workspace for skinny (decode) shapes
+            ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=x.device)
+        y = self.N.linear(x, w, out=out, residual=residual, workspace=ws)
+        if bias is not None:
+            y += bias
+        return y
+
+    def rmsnorm(self, x, w, eps, residual=None):
+        return self.N.rmsnorm(x, w, eps, residual=residual)
+
+    def swiglu_mlp(self, x, gate_up, down, residual=None):
+        x2 = x.reshape(-1, x.shape[-1])
+        T = x2.shape[0]
+        I = gate_up.shape[0] // 2
+        if I % 128 == 0:
+            offs = self._offs1(T, x.device)
+            h = self.N.grouped_linear(x2, gate_up, offs, 1, True, T)
+        else:
+            h = self.N.swiglu(self.linear(x2, gate_up))
+        return self.linear(h, down, residual=residual)
+
+    def rope_qknorm(self, qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps):
+        return self.N.rope_qknorm(qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot,
+                                  eps)
+
+    def attn_decode(self, q, k_cache, v_cache, block_tables, ctx_lens, splits=1):
+        B, Hq, D = q.shape
+        ws = None
+        if splits > 1:
+            ws = torch.empty(B * Hq * splits * (D + 1), dtype=torch.float32, device=q.device)
+        return self.N.attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws)
+
+    def attn_prefill(self, q, k, v):
+        # causal prefill attention; replaced by the tcgen05 flash kernel when built
+        return R.attn_prefill(q, k, v)
+
+    def moe(self, x, mo, top_k, renorm, inter, residual=None):
+        N = self.N
+        T, H = x.shape
+        E = mo.router.shape[0]
+        dev = x.device
+        logits = self.linear(x, mo.router)
+        ids = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+        wts = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+        counts = torch.empty(E, dtype=torch.int32, device=dev)
+        offs = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        cursor = torch.empty(E, dtype=torch.int32, device=dev)
+        N.moe_route(logits, top_k, renorm, ids, wts, counts, offs, cursor)
+        pos = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+        xs = torch.empty(T * top_k, H, dtype=x.dtype, device=dev)
+        N.moe_permute(x, ids, offs, cursor, pos, xs)
+        exp_rows = max(1, (T * top_k) // E)
+        max_rows = min(T * top_k, 4 * exp_rows)
+        h = N.grouped_linear(xs, mo.w13, offs, E, True, max_rows)
+        y = N.grouped_linear(h, mo.w2, offs, E, False, max_rows)
+        out = torch.empty_like(x)
+        if mo.shared is not None:
+            sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down)
+            # [T, 1] gate: a GEMV too narrow for a tensor-core tile
+            g = torch.sigmoid((x.float() @ mo.shared_gate.float().t()))
+            res2 = (sh.float() * g + (residual.float() if residual is not None else 0)).to(x.dtype)
+            return N.moe_combine(y, pos, wts, res2, out)
+        return N.moe_combine(y, pos, wts, residual, out)
+
+    def embed(self, ids, table):
+        return self.N.embed(ids, table)
+
+    def argmax(self, logits):
+        return self.N.argmax(logits.contiguous())
+
+
+def make_backend(name: str):
+    if name == "native":
+        return NativeBackend()
+    if name in ("torch", "baseline", "reference"):
+        return TorchBackend()
+    raise ValueError(f"unknown backend {name!r}")

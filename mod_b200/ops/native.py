@@ -1,0 +1,104 @@
+"""Thin, allocation-explicit wrappers around the sm_100a kernels.
+
+Every function takes its output buffers as arguments (or allocates them once
+with the caching allocator when ``out`` is omitted), so the whole decode step
+can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import load_extension
+
+
+def _C():
+    return load_extension()
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+           residual: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+           splits: int = 0) -> torch.Tensor:
+    """``out = x @ w.T (+ residual)``; tcgen05 GEMM.  ``splits=0`` picks split-K automatically."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if out is None:
+        out = torch.empty(x2.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    _C().linear(x2, w, out.view(x2.shape[0], w.shape[0]),
+                None if residual is None else residual.reshape(x2.shape[0], w.shape[0]), workspace, splits)
+    return out
+
+
+def grouped_linear(xs: torch.Tensor, w: torch.Tensor, offs: torch.Tensor, groups: int, swiglu: bool,
+                   max_rows_per_group: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    rows_pg = w.shape[0] // groups
+    n_out = rows_pg // 2 if swiglu else rows_pg
+    if out is None:
+        out = torch.empty(xs.shape[0], n_out, dtype=xs.dtype, device=xs.device)
+    _C().grouped_linear(xs, w, offs, out, groups, swiglu, max_rows_per_group)
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    _C().rmsnorm(x, residual, w, out, eps)
+    return out
+
+
+def rope_qknorm(qkv, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot_dim, eps):
+    _C().rope_qknorm(qkv, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot_dim, eps)
+    return q_out
+
+
+def attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits: int = 1, workspace=None,
+                scale: Optional[float] = None):
+    if out is None:
+        out = torch.empty_like(q)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    _C().attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, splits, workspace, scale)
+    return out
+
+
+def moe_route(logits, top_k, renorm, ids, wts, counts, offs, cursor):
+    _C().moe_route(logits, top_k, renorm, ids, wts, counts, offs, cursor)
+
+
+def moe_permute(x, ids, offs, cursor, pos, xs):
+    _C().moe_permute(x, ids, offs, cursor, pos, xs)
+
+
+def moe_combine(y, pos, wts, residual, out):
+    _C().moe_combine(y, pos, wts, residual, out)
+    return out
+
+
+def embed(ids, table, out=None, vocab_start: int = 0):
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    _C().embed(ids, table, out, vocab_start)
+    return out
+
+
+def swiglu(gu, out=None):
+    if out is None:
+        out = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, dtype=gu.dtype, device=gu.device)
+    _C().swiglu(gu, out)
+    return out
+
+
+def argmax(logits, out=None, out_val=None, index_offset: int = 0):
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
+    _C().argmax(logits, out, out_val, index_offset)
+    return out
+
+
+def verify_tokens(draft, target, out=None):
+    if out is None:
+        out = torch.empty(draft.shape[0], dtype=torch.int32, device=draft.device)
+    _C().verify_tokens(draft, target, out)
+    return out

@@ -1,0 +1,204 @@
+"""sm_100a kernels vs PyTorch fp32 references of the same op (bf16 tolerances)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _N():
+    from mod_b200.ops import check_status, native
+
+    return native, check_status
+
+
+def _close(a, b, rtol=2e-2, atol=2e-2):
+    torch.testing.assert_close(a.float(), b.float(), rtol=rtol, atol=atol)
+
+
+def _rand(*shape, scale=1.0, dev="cuda"):
+    return (torch.randn(*shape, device=dev) * scale).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("T,K,N", [(1, 256, 128), (7, 512, 384), (64, 2048, 5120), (128, 2048, 2048),
+                                   (200, 768, 256), (256, 4096, 1024)])
+def test_linear_swap_orientation(cuda, T, K, N):
+    native, check = _N()
+    torch.manual_seed(0)
+    x, w = _rand(T, K), _rand(N, K, scale=0.05)
+    ref = x.float() @ w.float().t()
+    y = native.linear(x, w)
+    check()
+    _close(y, ref)
+    ws = torch.empty(8 * T * N, device=cuda, dtype=torch.float32)
+    for splits in (2, 4):
+        y2 = native.linear(x, w, workspace=ws, splits=splits)
+        check()
+        _close(y2, ref)
+
+
+@pytest.mark.parametrize("T,K,N", [(300, 512, 384), (1024, 1024, 1000), (4096, 2048, 2048), (129, 256, 16)])
+def test_linear_normal_orientation(cuda, T, K, N):
+    native, check = _N()
+    torch.manual_seed(1)
+    x, w = _rand(T, K), _rand(N, K, scale=0.05)
+    y = native.linear(x, w)
+    check()
+    _close(y, x.float() @ w.float().t())
+
+
+def test_linear_residual(cuda):
+    native, check = _N()
+    x, w, r = _rand(32, 1024), _rand(512, 1024, scale=0.05), _rand(32, 512)
+    y = native.linear(x, w, residual=r)
+    check()
+    _close(y, x.float() @ w.float().t() + r.float())
+    ws = torch.empty(8 * 32 * 512, device=cuda, dtype=torch.float32)
+    y = native.linear(x, w, residual=r, workspace=ws, splits=4)
+    _close(y, x.float() @ w.float().t() + r.float())
+
+
+@pytest.mark.parametrize("E,I,H,T,k", [(8, 128, 256, 16, 2), (16, 768, 2048, 128, 8), (128, 768, 2048, 128, 8),
+                                       (4, 256, 512, 700, 2)])
+def test_grouped_swiglu_and_down(cuda, E, I, H, T, k):
+    native, check = _N()
+    torch.manual_seed(2)
+    counts = torch.randint(0, 2 * T * k // E + 1, (E,))
+    counts[0] = 0  # an empty expert
+    R = int(counts.sum())
+    offs = torch.zeros(E + 1, dtype=torch.int32)
+    offs[1:] = counts.cumsum(0)
+    xs = _rand(R, H)
+    w13 = _rand(E * 2 * I, H, scale=0.05)
+    w2 = _rand(E * H, I, scale=0.05)
+    h = native.grouped_linear(xs, w13, offs.cuda(), E, True, int(counts.max()))
+    y = native.grouped_linear(h, w2, offs.cuda(), E, False, int(counts.max()))
+    check()
+    href = torch.empty(R, I)
+    yref = torch.empty(R, H)
+    for e in range(E):
+        a, b = int(offs[e]), int(offs[e + 1])
+        if a == b:
+            continue
+        gu = xs[a:b].float().cpu() @ w13[e * 2 * I:(e + 1) * 2 * I].float().cpu().t()
+        hh = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+        href[a:b] = hh
+        yref[a:b] = hh.bfloat16().float() @ w2[e * H:(e + 1) * H].float().cpu().t()
+    _close(h.cpu(), href)
+    _close(y.cpu(), yref)
+
+
+# ------------------------------------------------------------------------ norms / rope
+@pytest.mark.parametrize("H", [256, 1024, 2048, 4096, 1000])
+def test_rmsnorm(cuda, H):
+    native, check = _N()
+    from mod_b200.ops import reference as R
+
+    x, w, r = _rand(37, H), _rand(H), _rand(37, H)
+    _close(native.rmsnorm(x, w, 1e-6), R.rmsnorm(x.float(), w.float(), 1e-6))
+    r2 = r.clone()
+    out = native.rmsnorm(x, w, 1e-6, residual=r2)
+    check()
+    rr = (r.float() + x.float())
+    _close(r2, rr)
+    _close(out, R.rmsnorm(rr, w.float(), 1e-6))
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,rot,qk", [(32, 4, 128, 128, True), (16, 2, 256, 64, True), (4, 2, 128, 128, False)])
+def test_rope_qknorm_paged_write(cuda, Hq, Hkv, D, rot, qk):
+    native, check = _N()
+    from mod_b200.ops import reference as R
+
+    T, nb = 40, 8
+    qkv = _rand(T, (Hq + 2 * Hkv) * D)
+    qw = _rand(D) if qk else None
+    kw = _rand(D) if qk else None
+    pos = torch.randint(0, 5000, (T,), device=cuda, dtype=torch.int32)
+    slots = torch.randperm(nb * 16, device=cuda)[:T].int()
+    slots[3] = -1
+    invf = R.inv_freq(rot, 1e6, device=cuda)
+    outs = []
+    for impl in (native.rope_qknorm, R.rope_qknorm):
+        q = torch.empty(T, Hq, D, device=cuda, dtype=torch.bfloat16)
+        kc = torch.zeros(nb, Hkv, 16, D, device=cuda, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        impl(qkv, qw, kw, pos, invf, slots, q, kc, vc, Hq, Hkv, D, rot, 1e-6)
+        outs.append((q, kc, vc))
+    check()
+    for a, b in zip(*outs):
+        _close(a, b, rtol=2e-2, atol=3e-2)
+
+
+# ------------------------------------------------------------------------ attention
+@pytest.mark.parametrize("B,Hq,Hkv,D,splits", [(4, 32, 4, 128, 1), (3, 32, 4, 128, 4), (5, 16, 2, 256, 2),
+                                               (2, 16, 8, 128, 1), (6, 8, 8, 64, 3)])
+def test_attn_decode(cuda, B, Hq, Hkv, D, splits):
+    native, check = _N()
+    from mod_b200.ops import reference as R
+
+    torch.manual_seed(3)
+    nb = 64
+    kc, vc = _rand(nb, Hkv, 16, D), _rand(nb, Hkv, 16, D)
+    lens = torch.tensor([1, 17, 100, 255, 33, 64][:B], dtype=torch.int32)
+    maxb = 16
+    bt = torch.stack([torch.randperm(nb)[:maxb] for _ in range(B)]).int()
+    q = _rand(B, Hq, D)
+    ws = torch.empty(B * Hq * splits * (D + 1), device=cuda, dtype=torch.float32)
+    o = native.attn_decode(q, kc, vc, bt.cuda(), lens.cuda(), splits=splits, workspace=ws)
+    check()
+    ref = R.attn_decode(q.float(), kc.float(), vc.float(), bt.cuda(), lens)
+    _close(o, ref)
+
+
+# ------------------------------------------------------------------------ MoE routing
+def test_moe_route_permute_combine(cuda):
+    native, check = _N()
+    from mod_b200.ops import reference as R
+
+    torch.manual_seed(4)
+    T, E, K, H = 50, 128, 8, 256
+    logits = _rand(T, E)
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    wts = torch.empty(T, K, dtype=torch.float32, device=cuda)
+    counts = torch.empty(E, dtype=torch.int32, device=cuda)
+    offs = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+    cursor = torch.empty(E, dtype=torch.int32, device=cuda)
+    native.moe_route(logits, K, True, ids, wts, counts, offs, cursor)
+    check()
+    rid, rw = R.moe_route(logits.float(), K, True)
+    assert torch.equal(ids.sort(-1).values, rid.sort(-1).values)
+    _close(wts.gather(1, ids.argsort(-1).long()), rw.gather(1, rid.argsort(-1).long()), rtol=1e-3, atol=1e-4)
+    assert int(offs[-1]) == T * K
+    x = _rand(T, H)
+    pos = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    xs = torch.empty(T * K, H, dtype=torch.bfloat16, device=cuda)
+    native.moe_permute(x, ids, offs, cursor, pos, xs)
+    assert torch.equal(xs[pos.long().flatten()], x.repeat_interleave(K, 0))
+    # rows of each expert segment belong to that expert
+    seg = torch.bucketize(pos.long().flatten(), offs[1:].long(), right=True)
+    assert torch.equal(seg.int(), ids.flatten())
+    y = _rand(T * K, H)
+    res = _rand(T, H)
+    out = torch.empty_like(x)
+    native.moe_combine(y, pos, wts, res, out)
+    ref = (y[pos.long()].float() * wts[..., None]).sum(1) + res.float()
+    _close(out, ref)
+
+
+def test_embed_argmax_verify(cuda):
+    native, check = _N()
+    table = _rand(1000, 256)
+    ids = torch.tensor([0, 5, 999, 123], device=cuda)
+    assert torch.equal(native.embed(ids, table), table[ids])
+    part = native.embed(ids, table[500:], vocab_start=500)
+    assert torch.equal(part[2], table[999]) and torch.all(part[0] == 0)
+    logits = _rand(7, 151936)
+    logits[3, 77] = 100.0
+    idx = native.argmax(logits)
+    assert torch.equal(idx, logits.float().argmax(-1))
+    d = torch.tensor([[1, 2, 3, 4], [1, 2, 3, 4]], device=cuda)
+    t = torch.tensor([[1, 2, 9, 4], [1, 2, 3, 4]], device=cuda)
+    assert native.verify_tokens(d, t).tolist() == [2, 4]
+    check()

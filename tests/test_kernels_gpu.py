@@ -14,7 +14,9 @@ def _N():
 
 
 def _close(a, b, rtol=2e-2, atol=2e-2):
-    torch.testing.assert_close(a.float(), b.float(), rtol=rtol, atol=atol)
+    # bf16 outputs: absolute slack scales with the tensor's magnitude
+    scale = max(1.0, b.float().abs().max().item())
+    torch.testing.assert_close(a.float(), b.float(), rtol=rtol, atol=atol * scale)
 
 
 def _rand(*shape, scale=1.0, dev="cuda"):

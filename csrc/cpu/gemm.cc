@@ -1,0 +1,96 @@
+// fp32 GEMM  y[M, N] = x[M, K] * w[N, K]^T  (both operands K-contiguous).
+//
+// Register-blocked dot-product kernel: a 4 x 4 tile of outputs keeps 16 AVX2
+// accumulators of 8 lanes each along K; the 8 loads per k-step (4 rows of x,
+// 4 rows of w) feed 16 FMAs.  OpenMP splits the tile grid; the single-row
+// case (decode GEMV, weight-bandwidth bound) splits N.
+#include <immintrin.h>
+#include <omp.h>
+#include <algorithm>
+#include "cpu_ops.h"
+
+namespace mbcpu {
+
+static inline float hsum(__m256 v) {
+  __m128 lo = _mm256_castps256_ps128(v), hi = _mm256_extractf128_ps(v, 1);
+  lo = _mm_add_ps(lo, hi);
+  lo = _mm_hadd_ps(lo, lo);
+  lo = _mm_hadd_ps(lo, lo);
+  return _mm_cvtss_f32(lo);
+}
+
+// rows [m0, m0+mr) x cols [n0, n0+nr), mr, nr <= 4
+static void tile(const float* x, const float* w, float* y, int64_t K, int64_t N, int64_t m0, int mr, int64_t n0,
+                 int nr) {
+  __m256 acc[4][4];
+  for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 4; ++j) acc[i][j] = _mm256_setzero_ps();
+  const float* xr[4];
+  const float* wr[4];
+  for (int i = 0; i < 4; ++i) xr[i] = x + (m0 + (i < mr ? i : 0)) * K;
+  for (int j = 0; j < 4; ++j) wr[j] = w + (n0 + (j < nr ? j : 0)) * K;
+  int64_t k = 0;
+  for (; k + 8 <= K; k += 8) {
+    __m256 xv[4], wv[4];
+    for (int i = 0; i < 4; ++i) xv[i] = _mm256_loadu_ps(xr[i] + k);
+    for (int j = 0; j < 4; ++j) wv[j] = _mm256_loadu_ps(wr[j] + k);
+    for (int i = 0; i < 4; ++i)
+      for (int j = 0; j < 4; ++j) acc[i][j] = _mm256_fmadd_ps(xv[i], wv[j], acc[i][j]);
+  }
+  for (int i = 0; i < mr; ++i)
+    for (int j = 0; j < nr; ++j) {
+      float s = hsum(acc[i][j]);
+      for (int64_t kk = k; kk < K; ++kk) s += xr[i][kk] * wr[j][kk];
+      y[(m0 + i) * N + n0 + j] = s;
+    }
+}
+
+static void gemv(const float* x, const float* w, float* y, int64_t K, int64_t N) {
+#pragma omp parallel for schedule(static)
+  for (int64_t n0 = 0; n0 < N; n0 += 4) {
+    const int nr = (int)std::min<int64_t>(4, N - n0);
+    __m256 a0[4], a1[4];
+    for (int j = 0; j < 4; ++j) a0[j] = a1[j] = _mm256_setzero_ps();
+    const float* wr[4];
+    for (int j = 0; j < 4; ++j) wr[j] = w + (n0 + (j < nr ? j : 0)) * K;
+    int64_t k = 0;
+    for (; k + 16 <= K; k += 16) {
+      const __m256 x0 = _mm256_loadu_ps(x + k), x1 = _mm256_loadu_ps(x + k + 8);
+      for (int j = 0; j < 4; ++j) {
+        a0[j] = _mm256_fmadd_ps(x0, _mm256_loadu_ps(wr[j] + k), a0[j]);
+        a1[j] = _mm256_fmadd_ps(x1, _mm256_loadu_ps(wr[j] + k + 8), a1[j]);
+      }
+    }
+    for (int j = 0; j < nr; ++j) {
+      float s = hsum(_mm256_add_ps(a0[j], a1[j]));
+      for (int64_t kk = k; kk < K; ++kk) s += x[kk] * wr[j][kk];
+      y[n0 + j] = s;
+    }
+  }
+}
+
+void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && w.scalar_type() == at::kFloat && y.scalar_type() == at::kFloat);
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && y.is_contiguous());
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && y.size(0) == M && y.size(1) == N);
+  const float* px = x.data_ptr<float>();
+  const float* pw = w.data_ptr<float>();
+  float* py = y.data_ptr<float>();
+  if (M == 1) {
+    gemv(px, pw, py, K, N);
+    return;
+  }
+  const int64_t MB = 64, NB = 64;
+  const int64_t mt = (M + MB - 1) / MB, nt = (N + NB - 1) / NB;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+  for (int64_t bi = 0; bi < mt; ++bi)
+    for (int64_t bj = 0; bj < nt; ++bj) {
+      const int64_t m_end = std::min(M, (bi + 1) * MB), n_end = std::min(N, (bj + 1) * NB);
+      for (int64_t n0 = bj * NB; n0 < n_end; n0 += 4)
+        for (int64_t m0 = bi * MB; m0 < m_end; m0 += 4)
+          tile(px, pw, py, K, N, m0, (int)std::min<int64_t>(4, m_end - m0), n0, (int)std::min<int64_t>(4, n_end - n0));
+    }
+}
+
+}  // namespace mbcpu

@@ -1,7 +1,7 @@
 // Paged decode attention with GQA packing and split-KV.
 //
 // q        [B, Hq, D]           one query token per sequence
-// k/v cache[num_blocks, Hkv, BS, D]   BS = 16 (block size)
+// k cache  [num_blocks, Hkv, BS, D], v cache [num_blocks, Hkv, D, BS], BS = 16
 // block_tables [B, max_blocks] int32, context_lens [B] int32
 // out      [B, Hq, D]
 //

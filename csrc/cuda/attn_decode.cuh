@@ -52,10 +52,14 @@ __global__ void __launch_bounds__(kWarps * 32)
     const uint4* kp = reinterpret_cast<const uint4*>(kc + base + tok * D + half * HD);
 #pragma unroll
     for (int i = 0; i < HD / 8; ++i) kr[i] = kp[i];
-    using VT = typename std::conditional<E == 2, unsigned int, typename std::conditional<E == 4, uint2, uint4>::type>::type;
-    VT vr[BS];
+    // V block is [D, BS]: this lane's E dims are E rows of 16 tokens (32 B each)
+    uint4 vr[E][2];
 #pragma unroll
-    for (int t = 0; t < BS; ++t) vr[t] = *reinterpret_cast<const VT*>(vc + base + t * D + lane * E);
+    for (int e = 0; e < E; ++e) {
+      const uint4* vp = reinterpret_cast<const uint4*>(vc + base + (size_t)(lane * E + e) * BS);
+      vr[e][0] = vp[0];
+      vr[e][1] = vp[1];
+    }
 
     float s[G];
 #pragma unroll
@@ -92,10 +96,10 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
 #pragma unroll
     for (int t = 0; t < BS; ++t) {
-      const __nv_bfloat16* vh = reinterpret_cast<const __nv_bfloat16*>(&vr[t]);
       float vf[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) vf[e] = __bfloat162float(vh[e]);
+      for (int e = 0; e < E; ++e)
+        vf[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&vr[e][t >> 3])[t & 7]);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float pt = __shfl_sync(0xffffffffu, s[g], t);

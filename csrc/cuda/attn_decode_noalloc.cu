@@ -87,7 +87,7 @@ __attribute__((visibility("default"))) size_t mb_attn_decode_noalloc_max_scratch
 
 // Paged decode attention, split-KV, with no allocation.
 //   q          [B, Hq, D] bf16           out  [B, Hq, D] bf16
-//   k/v cache  [num_blocks, Hkv, 16, D] bf16
+//   k cache [num_blocks, Hkv, 16, D], v cache [num_blocks, Hkv, D, 16] bf16
 //   block_tables [B, max_blocks] int32,  ctx_lens [B] int32
 // All pointers are device pointers owned by the caller; `stream` is a
 // cudaStream_t (0 = legacy default stream).  Returns 0 on success, 1 for bad

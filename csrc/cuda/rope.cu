@@ -3,7 +3,7 @@
 // Input is the packed QKV projection [T, (Hq + 2*Hkv) * D].  For every token:
 //   q_h  <- rope(rmsnorm(q_h) * q_w)      -> q_out [T, Hq, D]
 //   k_h  <- rope(rmsnorm(k_h) * k_w)      -> k_cache[block, h, off, :]
-//   v_h                                   -> v_cache[block, h, off, :]
+//   v_h                                   -> v_cache[block, h, :, off]
 // with (block, off) = divmod(slot_mapping[t], block_size).  RoPE is the
 // rotate-half (NeoX) form on the first `rot_dim` dimensions (rot_dim < D gives
 // the partial rotary of Qwen3-Next attention).  Angles are computed on the fly
@@ -42,13 +42,19 @@ __global__ void rope_qknorm_kernel(const __nv_bfloat16* __restrict__ qkv, const 
     const bool is_q = h < Hq;
     const bool is_k = !is_q && h < Hq + Hkv;
     __nv_bfloat16* dst;
+    int dstride = 1;  // element stride of the destination along D
     if (is_q) {
       dst = q_out + ((size_t)t * Hq + h) * D;
     } else {
       if (slot < 0) continue;
       const int hk = is_k ? h - Hq : h - Hq - Hkv;
       const size_t blk = slot / block_size, off = slot % block_size;
-      dst = (is_k ? k_cache : v_cache) + ((blk * Hkv + hk) * block_size + off) * D;
+      if (is_k) {
+        dst = k_cache + ((blk * Hkv + hk) * block_size + off) * D;
+      } else {  // V is stored [blk, Hkv, D, block_size]
+        dst = v_cache + ((blk * Hkv + hk) * D) * block_size + off;
+        dstride = block_size;
+      }
     }
     if (is_q || is_k) {
       const __nv_bfloat16* nw = is_q ? qw : kw;
@@ -82,7 +88,7 @@ __global__ void rope_qknorm_kernel(const __nv_bfloat16* __restrict__ qkv, const 
       __syncwarp();
     }
 #pragma unroll
-    for (int e = 0; e < E; ++e) dst[lane * E + e] = __float2bfloat16(v[e]);
+    for (int e = 0; e < E; ++e) dst[(size_t)(lane * E + e) * dstride] = __float2bfloat16(v[e]);
   }
 }
 
@@ -97,6 +103,7 @@ void rope_qknorm(const at::Tensor& qkv, const c10::optional<at::Tensor>& q_w, co
   TORCH_CHECK(qkv.size(1) >= (Hq + 2 * Hkv) * D && positions.numel() == T);
   TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == T * Hq * D);
   TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.size(1) == Hkv && k_cache.size(3) == D);
+  TORCH_CHECK(v_cache.size(1) == Hkv && v_cache.size(2) == D && v_cache.size(3) == k_cache.size(2), "V cache must be [blocks, Hkv, D, block_size]");
   if (slots && slots->defined()) TORCH_CHECK(slots->scalar_type() == at::kInt && slots->numel() == T);
   if (T == 0) return;
   c10::cuda::CUDAGuard guard(qkv.device());

@@ -1,6 +1,8 @@
 """Paged KV cache and recurrent-state cache.
 
-KV layout per full-attention layer: ``[num_blocks, Hkv, block_size, D]``,
+KV layout per full-attention layer: K ``[num_blocks, Hkv, block_size, D]`` and
+V ``[num_blocks, Hkv, D, block_size]`` (transposed inside a block, so the
+tensor-core P.V product reads it K-major, one 16-token block per MMA),
 block_size 16.  A (block, head) tile is one contiguous 4 KiB run at D = 128,
 which the decode kernel reads with 16-byte vector loads.  The reference keeps
 a static ``[B, Smax, Hkv, D]`` cache per layer filled by ``set_slice``
@@ -31,7 +33,7 @@ class KVCache:
             if cfg.layer_type(i) == "full_attention":
                 self.layer_index[i] = len(self.k)
                 self.k.append(torch.zeros(num_blocks, hkv, block_size, cfg.head_dim, device=device, dtype=dtype))
-                self.v.append(torch.zeros(num_blocks, hkv, block_size, cfg.head_dim, device=device, dtype=dtype))
+                self.v.append(torch.zeros(num_blocks, hkv, cfg.head_dim, block_size, device=device, dtype=dtype))
 
     def layer(self, i: int):
         j = self.layer_index[i]

@@ -160,9 +160,85 @@ class NativeBackend:
         return self.N.argmax(logits.contiguous())
 
 
+class CpuBackend(TorchBackend):
+    """C++/OpenMP CPU backend (``mod_b200._cpu``), fp32.  Plumbing and host
+    reference path; the reference's equivalent is its C CPU library
+    (``pio/plugins/cpu/c_src/tensor_ops.c``)."""
+
+    name = "cpu"
+
+    def __init__(self, threads: Optional[int] = None):
+        import importlib
+
+        self.C = importlib.import_module("mod_b200._cpu")
+        if threads:
+            self.C.set_num_threads(threads)
+
+    def linear(self, x, w, bias=None, residual=None, out=None):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        y = torch.empty(x2.shape[0], w.shape[0], dtype=torch.float32)
+        self.C.linear(x2, w, y)
+        if bias is not None:
+            y += bias
+        if residual is not None:
+            y += residual.reshape(y.shape)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+    def rmsnorm(self, x, w, eps, residual=None):
+        out = torch.empty_like(x)
+        self.C.rmsnorm(x.contiguous(), residual, w, out, eps)
+        return out
+
+    def swiglu_mlp(self, x, gate_up, down, residual=None):
+        gu = self.linear(x, gate_up)
+        h = torch.empty(gu.shape[0], gu.shape[1] // 2)
+        self.C.swiglu(gu, h)
+        return self.linear(h, down, residual=residual)
+
+    def rope_qknorm(self, qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps):
+        self.C.rope_qknorm(qkv.contiguous(), q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D,
+                           rot, eps)
+        return q_out
+
+    def attn_paged(self, q, k_cache, v_cache, fb):
+        out = torch.empty_like(q)
+        if fb.is_decode:
+            qlens = torch.ones(q.shape[0], dtype=torch.int32)
+        else:
+            qlens = torch.tensor(fb.query_lens, dtype=torch.int32)
+        self.C.attn_paged(q, k_cache, v_cache, fb.block_tables, fb.ctx_lens, qlens, out, 1.0 / math.sqrt(q.shape[-1]))
+        return out
+
+    def moe(self, x, mo, top_k, renorm, inter, residual=None):
+        logits = self.linear(x, mo.router)
+        T = x.shape[0]
+        ids = torch.empty(T, top_k, dtype=torch.int32)
+        wts = torch.empty(T, top_k)
+        self.C.moe_route(logits, top_k, renorm, ids, wts)
+        out = torch.zeros_like(x) if residual is None else residual.clone()
+        self.C.moe_experts(x.contiguous(), ids, wts, mo.w13, mo.w2, mo.e_lo, mo.e_hi - mo.e_lo, out)
+        if mo.shared is not None:
+            sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down)
+            out += torch.sigmoid(x @ mo.shared_gate.t()) * sh
+        return out
+
+    def embed(self, ids, table):
+        out = torch.empty(ids.numel(), table.shape[1])
+        self.C.embed(ids.contiguous(), table, out)
+        return out
+
+    def argmax(self, logits):
+        return self.C.argmax(logits.float().contiguous())
+
+
 def make_backend(name: str):
     if name == "native":
         return NativeBackend()
+    if name == "cpu":
+        return CpuBackend()
     if name in ("torch", "baseline", "reference"):
         return TorchBackend()
     raise ValueError(f"unknown backend {name!r}")

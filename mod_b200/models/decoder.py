@@ -52,7 +52,9 @@ class DecoderLM:
         q = torch.empty(T, Hq, D, dtype=x.dtype, device=x.device)
         be.rope_qknorm(qkv, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc, vc, Hq, Hkv,
                        D, cfg.rotary_dim, cfg.rms_norm_eps)
-        if fb.is_decode:
+        if hasattr(be, "attn_paged"):
+            o = be.attn_paged(q, kc, vc, fb)
+        elif fb.is_decode:
             o = be.attn_decode(q, kc, vc, fb.block_tables, fb.ctx_lens, fb.attn_splits)
         else:
             o = torch.empty_like(q)
@@ -60,7 +62,7 @@ class DecoderLM:
             for b, ql in enumerate(fb.query_lens):
                 n = fb.ctx_lens_host[b]
                 k = R.gather_kv(kc, fb.block_tables[b], n)
-                v = R.gather_kv(vc, fb.block_tables[b], n)
+                v = R.gather_v(vc, fb.block_tables[b], n)
                 qb = q[start:start + ql]
                 if ql == n:
                     o[start:start + ql] = be.attn_prefill(qb, k, v)

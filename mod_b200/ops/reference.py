@@ -76,7 +76,7 @@ def rope_qknorm(qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, 
         s = slots[valid].long()
         blk, off = s // bs, s % bs
         k_cache[blk, :, off, :] = k[valid]
-        v_cache[blk, :, off, :] = v[valid]
+        v_cache[blk, :, :, off] = v[valid]          # V blocks are [Hkv, D, BS]
     return q_out
 
 
@@ -86,6 +86,14 @@ def gather_kv(cache: torch.Tensor, block_table: torch.Tensor, n: int) -> torch.T
     nb = (n + bs - 1) // bs
     blocks = cache[block_table[:nb].long()]                # [nb, Hkv, BS, D]
     return blocks.permute(0, 2, 1, 3).reshape(nb * bs, cache.shape[1], cache.shape[3])[:n]
+
+
+def gather_v(cache: torch.Tensor, block_table: torch.Tensor, n: int) -> torch.Tensor:
+    """[num_blocks, Hkv, D, BS] + table -> [n, Hkv, D] for one sequence."""
+    bs = cache.shape[3]
+    nb = (n + bs - 1) // bs
+    blocks = cache[block_table[:nb].long()]                # [nb, Hkv, D, BS]
+    return blocks.permute(0, 3, 1, 2).reshape(nb * bs, cache.shape[1], cache.shape[2])[:n]
 
 
 def attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits=1, workspace=None, scale=None):
@@ -100,7 +108,7 @@ def attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits=1,
     for b in range(B):
         n = int(lens[b])
         k = gather_kv(k_cache, block_tables[b], n).float()    # [n, Hkv, D]
-        v = gather_kv(v_cache, block_tables[b], n).float()
+        v = gather_v(v_cache, block_tables[b], n).float()
         qb = q[b].float().view(Hkv, G, D)
         s = torch.einsum("hgd,nhd->hgn", qb, k) * scale
         p = torch.softmax(s, dim=-1)
@@ -115,9 +123,9 @@ def attn_decode_batched(q, k_cache, v_cache, block_tables, ctx_lens, out=None, s
     Hkv, bs = k_cache.shape[1], k_cache.shape[2]
     maxb = block_tables.shape[1]
     k = k_cache[block_tables.long()]                          # [B, maxb, Hkv, BS, D]
-    v = v_cache[block_tables.long()]
+    v = v_cache[block_tables.long()]                          # [B, maxb, Hkv, D, BS]
     k = k.permute(0, 2, 1, 3, 4).reshape(B, Hkv, maxb * bs, D)
-    v = v.permute(0, 2, 1, 3, 4).reshape(B, Hkv, maxb * bs, D)
+    v = v.permute(0, 2, 1, 4, 3).reshape(B, Hkv, maxb * bs, D)
     mask = torch.arange(maxb * bs, device=q.device)[None, :] < ctx_lens[:, None]
     o = F.scaled_dot_product_attention(q[:, :, None, :], k, v, attn_mask=mask[:, None, None, :],
                                        scale=scale, enable_gqa=True)

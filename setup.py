@@ -17,6 +17,9 @@ os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"  # keep torch from adding other -ge
 from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+import torch  # noqa: E402
+
+TORCH_LIB = os.path.join(os.path.dirname(torch.__file__), "lib")
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",
@@ -45,7 +48,8 @@ def cpu_ext():
         sources=srcs,
         include_dirs=[os.path.join(ROOT, "csrc", "cpu"), os.path.join(ROOT, "csrc", "io")],
         extra_compile_args=CXX_FLAGS + ["-fopenmp", "-march=x86-64-v3"],
-        extra_link_args=["-fopenmp"],
+        # link the OpenMP runtime torch already ships, so one process has one runtime
+        extra_link_args=["-L" + TORCH_LIB, "-l:libgomp.so.1", "-Wl,-rpath," + TORCH_LIB],
     )
 
 

@@ -57,3 +57,15 @@ def test_kv_cache_lengths_after_prefill_and_decode():
     assert eng.seqs[rid].num_cached == 5
     eng.step()
     assert eng.seqs[rid].num_cached == 6
+
+
+@pytest.mark.parametrize("name", ["tiny-dense", "tiny-moe", "tiny-glm", "tiny-next"])
+def test_cpu_cxx_backend_matches_oracle(name):
+    pytest.importorskip("mod_b200._cpu")
+    cfg = get_preset(name)
+    w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=0)
+    eng = LLMEngine(cfg, weights=w, backend="cpu", device="cpu", max_batch=4, max_model_len=64)
+    prompts = _prompts(cfg.vocab_size, (5, 9, 3))
+    outs = eng.generate(prompts, SamplingParams(max_new_tokens=6))
+    ref = [oracle.greedy_generate(cfg, w, torch.tensor([p]), 6)[0].tolist() for p in prompts]
+    assert outs == ref

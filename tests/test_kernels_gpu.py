@@ -125,7 +125,7 @@ def test_rope_qknorm_paged_write(cuda, Hq, Hkv, D, rot, qk):
     for impl in (native.rope_qknorm, R.rope_qknorm):
         q = torch.empty(T, Hq, D, device=cuda, dtype=torch.bfloat16)
         kc = torch.zeros(nb, Hkv, 16, D, device=cuda, dtype=torch.bfloat16)
-        vc = torch.zeros_like(kc)
+        vc = torch.zeros(nb, Hkv, D, 16, device=cuda, dtype=torch.bfloat16)
         impl(qkv, qw, kw, pos, invf, slots, q, kc, vc, Hq, Hkv, D, rot, 1e-6)
         outs.append((q, kc, vc))
     check()
@@ -142,7 +142,7 @@ def test_attn_decode(cuda, B, Hq, Hkv, D, splits):
 
     torch.manual_seed(3)
     nb = 64
-    kc, vc = _rand(nb, Hkv, 16, D), _rand(nb, Hkv, 16, D)
+    kc, vc = _rand(nb, Hkv, 16, D), _rand(nb, Hkv, D, 16)
     lens = torch.tensor([1, 17, 100, 255, 33, 64][:B], dtype=torch.int32)
     maxb = 16
     bt = torch.stack([torch.randperm(nb)[:maxb] for _ in range(B)]).int()

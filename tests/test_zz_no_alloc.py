@@ -43,7 +43,7 @@ def test_noalloc_matches_torch_entry_point_twice(cuda):
     scale = 1.0 / math.sqrt(D)
     for call in range(2):  # two calls in a row: the shared scratch keeps the previous call's contents
         kc = (torch.randn(nb, Hkv, 16, D, device=cuda)).bfloat16()
-        vc = (torch.randn(nb, Hkv, 16, D, device=cuda)).bfloat16()
+        vc = (torch.randn(nb, Hkv, D, 16, device=cuda)).bfloat16()
         q = torch.randn(B, Hq, D, device=cuda).bfloat16()
         bt = torch.stack([torch.randperm(nb)[:maxb] for _ in range(B)]).int().to(cuda)
         ctx = torch.tensor([1, 40, 255, 17, 100, 200][:B], dtype=torch.int32, device=cuda) - call
@@ -68,6 +68,7 @@ def test_noalloc_rejects_oversized_request(cuda):
     bt = torch.zeros(B, 1, device=cuda, dtype=torch.int32)
     ctx = torch.ones(B, device=cuda, dtype=torch.int32)
     out = torch.empty_like(q)
-    rc = _call(lib, q, kc, kc, bt, ctx, out, int(splits), 0.1)
+    vc = torch.zeros(2, Hkv, D, 16, device=cuda, dtype=torch.bfloat16)
+    rc = _call(lib, q, kc, vc, bt, ctx, out, int(splits), 0.1)
     assert rc == 2
     assert b"maximum" in lib.mb_noalloc_last_error()

@@ -20,6 +20,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "attn_decode.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -57,7 +58,7 @@ void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tenso
   const int mbk = (int)block_tables.size(1);
 #define MB_ATT(DD, GG)                                                                                         \
   if (D == DD && G == GG) {                                                                                    \
-    attn_decode_kernel<DD, GG><<<grid, kWarps * 32, 0, st>>>(pq, pk, pv, block_tables.data_ptr<int>(),         \
+    launch_k(attn_decode_kernel<DD, GG>, grid, kWarps * 32, 0, st, pq, pk, pv, block_tables.data_ptr<int>(),         \
                                                             ctx_lens.data_ptr<int>(), pout, po, pl, Hkv, mbk,  \
                                                             (int)splits, sl2);                                 \
     launched = true;                                                                                           \
@@ -70,9 +71,9 @@ void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tenso
   TORCH_CHECK(launched, "attn_decode: unsupported head_dim/group ", D, "/", G);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (splits > 1) {
-    if (D == 128) attn_combine_kernel<128><<<B * Hq, 128, 0, st>>>(po, pl, pout, (int)splits);
-    else if (D == 256) attn_combine_kernel<256><<<B * Hq, 128, 0, st>>>(po, pl, pout, (int)splits);
-    else attn_combine_kernel<64><<<B * Hq, 64, 0, st>>>(po, pl, pout, (int)splits);
+    if (D == 128) launch_k(attn_combine_kernel<128>, B * Hq, 128, 0, st, po, pl, pout, (int)splits);
+    else if (D == 256) launch_k(attn_combine_kernel<256>, B * Hq, 128, 0, st, po, pl, pout, (int)splits);
+    else launch_k(attn_combine_kernel<64>, B * Hq, 64, 0, st, po, pl, pout, (int)splits);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

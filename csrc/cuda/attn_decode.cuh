@@ -15,6 +15,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                        const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_tables,
                        const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out, float* __restrict__ part_o,
                        float* __restrict__ part_lse, int Hkv, int max_blocks, int splits, float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int BS = 16;
   constexpr int E = D / 32;      // P.V dims per lane
   constexpr int HD = D / 2;      // Q.K dims per lane
@@ -149,6 +151,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 template <int D>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                     __nv_bfloat16* __restrict__ out, int splits) {
+  pdl_wait();
+  pdl_trigger();
   const size_t bh = blockIdx.x;
   float mx = -INFINITY;
   for (int s = 0; s < splits; ++s) mx = fmaxf(mx, part_lse[bh * splits + s]);

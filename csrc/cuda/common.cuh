@@ -193,3 +193,15 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
 }  // namespace mb
+
+namespace mb {
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with the PDL attribute may
+// start while its predecessor in the stream is still running.  It must call
+// pdl_wait() before reading anything the predecessor writes or writing
+// anything the predecessor reads; work that touches only immutable data
+// (weights, shared-memory set-up, TMEM allocation) can go before it.
+// pdl_trigger() lets the next kernel begin launching early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+}  // namespace mb

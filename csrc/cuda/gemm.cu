@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "gemm_tc.cuh"
+#include "launch.cuh"
 #include "status.h"
 
 namespace mb {
@@ -42,6 +43,23 @@ CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t
   return m;
 }
 
+// General 2-D map: [rows, cols] of `dt` with row pitch ld_bytes; box = box_cols x box_rows.
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows, int64_t cols, int64_t ld_bytes,
+                         int box_cols, int box_rows, CUtensorMapSwizzle sw) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(ld_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
 template <int BN, int STAGES, bool DUAL>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, cudaStream_t st) {
   using L = GemmSmem<BN, STAGES, DUAL>;
@@ -51,7 +69,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
     C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     attr = true;
   }
-  k<<<grid, 192, L::kBytes, st>>>(ta, tb, a);
+  launch_k(k, grid, 192, L::kBytes, st, ta, tb, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -59,19 +77,21 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
 // so it stops at BN = 128.
 static void dispatch(int bn, bool dual, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid,
                      cudaStream_t st) {
+  // Stage counts keep shared memory near 110 KB where possible, so two CTAs
+  // share an SM and one CTA's prologue/epilogue overlaps the other's loads.
   if (dual) {
     switch (bn) {
-      case 16: return launch<16, 6, true>(ta, tb, a, grid, st);
-      case 32: return launch<32, 6, true>(ta, tb, a, grid, st);
-      case 64: return launch<64, 5, true>(ta, tb, a, grid, st);
+      case 16: return launch<16, 3, true>(ta, tb, a, grid, st);
+      case 32: return launch<32, 3, true>(ta, tb, a, grid, st);
+      case 64: return launch<64, 4, true>(ta, tb, a, grid, st);
       default: return launch<128, 4, true>(ta, tb, a, grid, st);
     }
   }
   switch (bn) {
-    case 16: return launch<16, 8, false>(ta, tb, a, grid, st);
-    case 32: return launch<32, 8, false>(ta, tb, a, grid, st);
-    case 64: return launch<64, 6, false>(ta, tb, a, grid, st);
-    case 128: return launch<128, 5, false>(ta, tb, a, grid, st);
+    case 16: return launch<16, 6, false>(ta, tb, a, grid, st);
+    case 32: return launch<32, 5, false>(ta, tb, a, grid, st);
+    case 64: return launch<64, 4, false>(ta, tb, a, grid, st);
+    case 128: return launch<128, 3, false>(ta, tb, a, grid, st);
     default: return launch<256, 4, false>(ta, tb, a, grid, st);
   }
 }
@@ -92,6 +112,8 @@ static int num_sms() {
 // split-K reduction: out = bf16(sum_s ws[s] (+ residual))
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t n,
                                      const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i >= n) return;
   float4 acc = *reinterpret_cast<const float4*>(ws + i);
@@ -113,7 +135,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 // y[T, N] = x[T, K] @ w[N, K]^T (+ residual).  `workspace` (fp32, may be
 // empty) enables split-K for decode shapes that would otherwise leave SMs idle.
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,
-            const c10::optional<at::Tensor>& workspace, int64_t splits_req) {
+            const c10::optional<at::Tensor>& workspace, int64_t splits_req, int64_t orient) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && y.is_cuda());
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16);
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && y.is_contiguous());
@@ -135,7 +157,9 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::
   a.out_rows = (int)T;
   a.status = status_ptr(x.device().index());
   a.residual = res;
-  const bool swap = (T <= 256) && (N % 128 == 0);
+  // orient: -1 automatic, 0 normal (activations on the 128-row side), 1 swap
+  const bool swap = orient == 1 || (orient < 0 && T <= 256 && N % 128 == 0);
+  TORCH_CHECK(!swap || (T <= 256 && N % 128 == 0), "swap orientation needs T <= 256 and N % 128 == 0");
   if (swap) {
     const int bn = pick_bn(T, false);
     auto ta = make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), 128);
@@ -167,7 +191,7 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::
       int64_t n = T * N;
       int threads = 256;
       int64_t blocks = (n / 4 + threads - 1) / threads;
-      splitk_reduce_kernel<<<blocks, threads, 0, st>>>(workspace->data_ptr<float>(), splits, n, res,
+      launch_k(splitk_reduce_kernel, blocks, threads, 0, st, workspace->data_ptr<float>(), splits, n, res,
                                                      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
       C10_CUDA_KERNEL_LAUNCH_CHECK();
     }

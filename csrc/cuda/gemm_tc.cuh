@@ -77,12 +77,21 @@ __global__ void __launch_bounds__(192, 1)
   const int g = blockIdx.z / args.splits;
   const int split = blockIdx.z % args.splits;
 
+  // Dependent launch: every thread waits for the previous kernel before it
+  // touches activations, group offsets or outputs.  The producer of a dense
+  // GEMM (no device-side offsets) first prefetches weight tiles, which no
+  // earlier kernel writes.
+  const bool dense = args.b_offs == nullptr;
+  if (!(warp == 0 && dense)) {
+    pdl_wait();
+    pdl_trigger();
+  }
   // Work of this CTA: N tiles nt = blockIdx.y + r*gridDim.y of group g, over
   // this split's K-block range.
   int b0, cnt;
-  if (args.b_offs) {
-    b0 = __ldg(args.b_offs + g);
-    cnt = __ldg(args.b_offs + g + 1) - b0;
+  if (!dense) {
+    b0 = args.b_offs[g];
+    cnt = args.b_offs[g + 1] - b0;
   } else {
     b0 = 0;
     cnt = args.b_rows;
@@ -123,16 +132,35 @@ __global__ void __launch_bounds__(192, 1)
   if (my_tiles > 0 && kbs > 0) {
     if (warp == 0) {
       // ------------------------------------------------ TMA producer
-      if (elect_one_sync()) {
+      const bool leader = elect_one_sync();
+      // weight tiles of the first stages, issued before the dependency wait
+      const int pre = dense ? min(STAGES, kbs) : 0;
+      if (leader) {
+        for (int s = 0; s < pre; ++s) {
+          uint8_t* st = smem + s * L::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+          tma_load_2d(st, &tmA, &full[s], (kb_lo + s) * 64, a_row0);
+          if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], (kb_lo + s) * 64, a_row0 + args.a_up_offset);
+        }
+      }
+      if (dense) {
+        pdl_wait();
+        pdl_trigger();
+      }
+      if (leader) {
         int it = 0;
         bool ok = true;
         for (int t = 0; t < my_tiles && ok; ++t) {
           const int nt = blockIdx.y + t * gridDim.y;
           for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
             const int s = it % STAGES;
+            uint8_t* st = smem + s * L::kStageBytes;
+            if (it < pre) {  // weights already in flight: add the activation tile
+              tma_load_2d(st + L::kABytes * (DUAL ? 2 : 1), &tmB, &full[s], kb * 64, b0 + nt * BN);
+              continue;
+            }
             const uint32_t ph = (it / STAGES) & 1;
             if (!mbar_wait(&empty[s], ph ^ 1, args.status)) { ok = false; break; }
-            uint8_t* st = smem + s * L::kStageBytes;
             mbar_arrive_expect_tx(&full[s], L::kStageBytes);
             tma_load_2d(st, &tmA, &full[s], kb * 64, a_row0);
             if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], kb * 64, a_row0 + args.a_up_offset);

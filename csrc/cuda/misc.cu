@@ -7,6 +7,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -14,6 +15,8 @@ namespace mb {
 // (vocab-parallel embedding: the shards are then summed/gathered).
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int H, int64_t vocab_start, int64_t vocab_rows) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int64_t id = ids[t] - vocab_start;
   const bool in = id >= 0 && id < vocab_rows;
@@ -28,7 +31,7 @@ void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int6
   TORCH_CHECK(H % 8 == 0 && out.is_contiguous() && out.numel() == (int64_t)T * H);
   if (T == 0) return;
   c10::cuda::CUDAGuard guard(table.device());
-  embed_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_k(embed_kernel, T, 128, 0, at::cuda::getCurrentCUDAStream(), 
       ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, vocab_start, table.size(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -37,6 +40,8 @@ void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int6
 // gu [T, 2I] = [gate | up] -> out [T, I] = silu(gate) * up
 __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int I,
                               int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int64_t t = i / I, c = i % I;
@@ -52,7 +57,7 @@ void swiglu(const at::Tensor& gu, at::Tensor& out) {
   TORCH_CHECK(n * 2 == gu.numel());
   if (n == 0) return;
   c10::cuda::CUDAGuard guard(gu.device());
-  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_k(swiglu_kernel, (unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), I, n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -61,6 +66,8 @@ void swiglu(const at::Tensor& gu, at::Tensor& out) {
 // vocab-parallel caller can reduce (value, index) pairs across ranks.
 __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int V, int64_t* __restrict__ out_idx,
                               float* __restrict__ out_val, int64_t index_offset) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const __nv_bfloat16* row = logits + (size_t)r * V;
   float bv = -INFINITY;
@@ -116,7 +123,7 @@ void argmax(const at::Tensor& logits, at::Tensor& out_idx, const c10::optional<a
   if (R == 0) return;
   c10::cuda::CUDAGuard guard(logits.device());
   float* pv = (out_val && out_val->defined()) ? out_val->data_ptr<float>() : nullptr;
-  argmax_kernel<<<R, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_k(argmax_kernel, R, 1024, 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, out_idx.data_ptr<int64_t>(), pv, index_offset);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -125,6 +132,8 @@ void argmax(const at::Tensor& logits, at::Tensor& out_idx, const c10::optional<a
 // model's tokens, per row.  draft/target [R, L] int64 -> out [R] int32.
 __global__ void verify_tokens_kernel(const int64_t* __restrict__ draft, const int64_t* __restrict__ target, int L,
                                      int* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   int first_bad = L;
   for (int i = threadIdx.x; i < L; i += blockDim.x)
@@ -140,7 +149,7 @@ void verify_tokens(const at::Tensor& draft, const at::Tensor& target, at::Tensor
   const int R = (int)draft.size(0), L = (int)draft.size(1);
   if (R == 0) return;
   c10::cuda::CUDAGuard guard(draft.device());
-  verify_tokens_kernel<<<R, 32, 0, at::cuda::getCurrentCUDAStream()>>>(draft.data_ptr<int64_t>(),
+  launch_k(verify_tokens_kernel, R, 32, 0, at::cuda::getCurrentCUDAStream(), draft.data_ptr<int64_t>(),
                                                                         target.data_ptr<int64_t>(), L,
                                                                         out.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

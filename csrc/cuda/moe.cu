@@ -15,6 +15,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -22,6 +23,8 @@ namespace mb {
 template <int EPL>  // experts per lane
 __global__ void moe_topk_kernel(const __nv_bfloat16* __restrict__ logits, int T, int E, int K, bool renorm,
                                 int* __restrict__ ids, float* __restrict__ wts, int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -74,6 +77,8 @@ __global__ void moe_topk_kernel(const __nv_bfloat16* __restrict__ logits, int T,
 // Single CTA: offs[0]=0, offs[e+1]=offs[e]+counts[e]; resets cursors.
 __global__ void moe_scan_kernel(const int* __restrict__ counts, int E, int* __restrict__ offs,
                                 int* __restrict__ cursor) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int s[1024];
   const int i = threadIdx.x;
   s[i] = i < E ? counts[i] : 0;
@@ -95,6 +100,8 @@ __global__ void moe_scan_kernel(const int* __restrict__ counts, int E, int* __re
 __global__ void moe_permute_kernel(const __nv_bfloat16* __restrict__ x, int T, int K, int H,
                                    const int* __restrict__ ids, const int* __restrict__ offs,
                                    int* __restrict__ cursor, int* __restrict__ pos, __nv_bfloat16* __restrict__ xs) {
+  pdl_wait();
+  pdl_trigger();
   const int pair = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (pair >= T * K) return;
@@ -115,6 +122,8 @@ __global__ void moe_permute_kernel(const __nv_bfloat16* __restrict__ x, int T, i
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos,
                                    const float* __restrict__ wts, int K, int H,
                                    const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8];
@@ -157,7 +166,7 @@ void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids
     auto pl = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
     const int epl = (E + 31) / 32;
 #define MB_TOPK(N) \
-  moe_topk_kernel<N><<<grid, block, 0, st>>>(pl, T, E, (int)K, renorm, ids.data_ptr<int>(), wts.data_ptr<float>(), \
+  launch_k(moe_topk_kernel<N>, grid, block, 0, st, pl, T, E, (int)K, renorm, ids.data_ptr<int>(), wts.data_ptr<float>(), \
                                              counts.data_ptr<int>())
     if (epl <= 1) MB_TOPK(1);
     else if (epl <= 2) MB_TOPK(2);
@@ -168,7 +177,7 @@ void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids
 #undef MB_TOPK
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
-  moe_scan_kernel<<<1, 1024, 0, st>>>(counts.data_ptr<int>(), E, offs.data_ptr<int>(), cursor.data_ptr<int>());
+  launch_k(moe_scan_kernel, 1, 1024, 0, st, counts.data_ptr<int>(), E, offs.data_ptr<int>(), cursor.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -181,7 +190,7 @@ void moe_permute(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& o
   c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int wpb = 8;
-  moe_permute_kernel<<<(T * K + wpb - 1) / wpb, wpb * 32, 0, st>>>(
+  launch_k(moe_permute_kernel, (T * K + wpb - 1) / wpb, wpb * 32, 0, st, 
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), T, K, H, ids.data_ptr<int>(), offs.data_ptr<int>(),
       cursor.data_ptr<int>(), pos.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -199,7 +208,7 @@ void moe_combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w
                                ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr())
                                : nullptr;
   const int threads = std::min(256, std::max(32, H / 8));
-  moe_combine_kernel<<<T, threads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()),
+  launch_k(moe_combine_kernel, T, threads, 0, st, reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()),
                                             pos.data_ptr<int>(), wts.data_ptr<float>(), K, H, r,
                                             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -8,6 +8,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -16,6 +17,8 @@ template <int H, bool ADD>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows,
                                float eps) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kChunks = H / 256;
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -63,6 +66,8 @@ template <bool ADD>
 __global__ void rmsnorm_generic_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                        const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H,
                                        float eps) {
+  pdl_wait();
+  pdl_trigger();
   const size_t row = blockIdx.x;
   __shared__ float red[32];
   float ss = 0.f;
@@ -117,15 +122,15 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, con
   dim3 grid((rows + wpb - 1) / wpb), block(32 * wpb);
 #define MB_RMS(HH)                                                                       \
   case HH:                                                                               \
-    if (add) rmsnorm_kernel<HH, true><<<grid, block, 0, st>>>(px, r, pw, po, rows, eps); \
-    else rmsnorm_kernel<HH, false><<<grid, block, 0, st>>>(px, r, pw, po, rows, eps);    \
+    if (add) launch_k(rmsnorm_kernel<HH, true>, grid, block, 0, st, px, r, pw, po, rows, eps); \
+    else launch_k(rmsnorm_kernel<HH, false>, grid, block, 0, st, px, r, pw, po, rows, eps);    \
     break;
   switch (H) {
     MB_RMS(256) MB_RMS(512) MB_RMS(768) MB_RMS(1024) MB_RMS(1536) MB_RMS(2048) MB_RMS(3072) MB_RMS(4096)
    
     default:
-      if (add) rmsnorm_generic_kernel<true><<<rows, 256, 0, st>>>(px, r, pw, po, H, eps);
-      else rmsnorm_generic_kernel<false><<<rows, 256, 0, st>>>(px, r, pw, po, H, eps);
+      if (add) launch_k(rmsnorm_generic_kernel<true>, rows, 256, 0, st, px, r, pw, po, H, eps);
+      else launch_k(rmsnorm_generic_kernel<false>, rows, 256, 0, st, px, r, pw, po, H, eps);
   }
 #undef MB_RMS
   C10_CUDA_KERNEL_LAUNCH_CHECK();

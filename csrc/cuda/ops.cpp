@@ -4,7 +4,7 @@
 
 namespace mb {
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,
-            const c10::optional<at::Tensor>& workspace, int64_t splits);
+            const c10::optional<at::Tensor>& workspace, int64_t splits, int64_t orient);
 void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y, int64_t groups,
                     bool swiglu, int64_t max_rows_per_group);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
@@ -16,6 +16,10 @@ void rope_qknorm(const at::Tensor& qkv, const c10::optional<at::Tensor>& q_w, co
 void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                  const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                  const c10::optional<at::Tensor>& workspace, double scale);
+void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                    const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
+                    const c10::optional<at::Tensor>& workspace, double scale);
+bool attn_decode_tc_supported(int64_t D, int64_t G);
 void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids, at::Tensor& wts,
                at::Tensor& counts, at::Tensor& offs, at::Tensor& cursor);
 void moe_permute(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& offs, at::Tensor& cursor,
@@ -36,6 +40,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &mb::rmsnorm);
   m.def("rope_qknorm", &mb::rope_qknorm);
   m.def("attn_decode", &mb::attn_decode);
+  m.def("attn_decode_tc", &mb::attn_decode_tc);
+  m.def("attn_decode_tc_supported", &mb::attn_decode_tc_supported);
   m.def("moe_route", &mb::moe_route);
   m.def("moe_permute", &mb::moe_permute);
   m.def("moe_combine", &mb::moe_combine);

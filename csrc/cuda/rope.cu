@@ -17,6 +17,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -27,6 +28,8 @@ __global__ void rope_qknorm_kernel(const __nv_bfloat16* __restrict__ qkv, const 
                                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                                    __nv_bfloat16* __restrict__ v_cache, int Hq, int Hkv, int rot_dim, int block_size,
                                    float eps, int q_stride) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int E = D / 32;  // elements per lane
   __shared__ float buf[8][D];
   const int t = blockIdx.x;
@@ -114,7 +117,7 @@ void rope_qknorm(const at::Tensor& qkv, const c10::optional<at::Tensor>& q_w, co
   const int* ps = (slots && slots->defined()) ? slots->data_ptr<int>() : nullptr;
   const int bs = (int)k_cache.size(2);
 #define MB_ROPE(DD)                                                                                            \
-  rope_qknorm_kernel<DD><<<T, 256, 0, st>>>(                                                                   \
+  launch_k(rope_qknorm_kernel<DD>, T, 256, 0, st,                                                                    \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), bf(q_w), bf(k_w), positions.data_ptr<int>(),     \
       inv_freq.data_ptr<float>(), ps, reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),                      \
       reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), \

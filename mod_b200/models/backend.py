@@ -81,6 +81,11 @@ class NativeBackend:
         self.N = N
         self._one_group = {}
 
+    def _sms(self, device) -> int:
+        if not hasattr(self, "_nsm"):
+            self._nsm = torch.cuda.get_device_properties(device).multi_processor_count
+        return self._nsm
+
     def _offs1(self, T, device):
         # built by a kernel (no host copy), so it is legal inside graph capture
         return torch.arange(2, dtype=torch.int32, device=device) * T
@@ -116,9 +121,18 @@ class NativeBackend:
 
     def attn_decode(self, q, k_cache, v_cache, block_tables, ctx_lens, splits=1):
         B, Hq, D = q.shape
+        tc = self.N.attn_decode_tc_supported(D, Hq // k_cache.shape[1])
+        if tc:
+            # persistent tcgen05 kernel (2 CTAs per SM): split sequences into
+            # chunks only when (sequence, KV head) items cannot fill the GPU
+            items = B * k_cache.shape[1]
+            want = -(-2 * self._sms(q.device) // max(1, items))
+            splits = max(1, min(want, -(-block_tables.shape[1] // 8)))
         ws = None
         if splits > 1:
             ws = torch.empty(B * Hq * splits * (D + 1), dtype=torch.float32, device=q.device)
+        if tc:
+            return self.N.attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws)
         return self.N.attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws)
 
     def attn_prefill(self, q, k, v):

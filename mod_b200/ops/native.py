@@ -20,13 +20,14 @@ def _C():
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
            residual: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
-           splits: int = 0) -> torch.Tensor:
-    """``out = x @ w.T (+ residual)``; tcgen05 GEMM.  ``splits=0`` picks split-K automatically."""
+           splits: int = 0, orient: int = -1) -> torch.Tensor:
+    """``out = x @ w.T (+ residual)``; tcgen05 GEMM.  ``splits=0`` picks split-K automatically;
+    ``orient`` forces the tile orientation (0: activations on the 128-row MMA side, 1: weights)."""
     x2 = x.reshape(-1, x.shape[-1])
     if out is None:
         out = torch.empty(x2.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
     _C().linear(x2, w, out.view(x2.shape[0], w.shape[0]),
-                None if residual is None else residual.reshape(x2.shape[0], w.shape[0]), workspace, splits)
+                None if residual is None else residual.reshape(x2.shape[0], w.shape[0]), workspace, splits, orient)
     return out
 
 
@@ -61,6 +62,21 @@ def attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits: i
         scale = 1.0 / math.sqrt(q.shape[-1])
     _C().attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, splits, workspace, scale)
     return out
+
+
+def attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits: int = 1, workspace=None,
+                   scale: Optional[float] = None):
+    """tcgen05 flash-decode (head_dim 128, group <= 16); same contract as attn_decode."""
+    if out is None:
+        out = torch.empty_like(q)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    _C().attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out, splits, workspace, scale)
+    return out
+
+
+def attn_decode_tc_supported(D: int, G: int) -> bool:
+    return bool(_C().attn_decode_tc_supported(D, G))
 
 
 def moe_route(logits, top_k, renorm, ids, wts, counts, offs, cursor):

@@ -1,0 +1,366 @@
+// Expert-parallel MoE dispatch / combine fused with the all-to-all over
+// NVLink peer memory (P2P loads and stores issued from inside the kernels; no
+// NCCL on this path).
+//
+// Every rank owns one "exchange" buffer, mapped into every other rank with
+// CUDA IPC, laid out as
+//   recv_x [N*C, H] bf16  rows sent to this rank (source r uses rows r*C ..)
+//   comb   [N*C, H] bf16  expert outputs returned to this rank (owner o uses rows o*C ..)
+//   meta   [N*C]    int32 local expert id of each received row
+//   cnt    [N]      int32 rows received from each source
+//   flag_d [N]      u32   dispatch epoch written by each source
+//   flag_c [N]      u32   combine epoch written by each owner
+// C = capacity per (source, owner) = max tokens per call x top-k, so a call can
+// never overflow.  One MoE call:
+//   ep_dispatch      (source) each (token, k) pair claims a slot in its owner's
+//                    receive region and stores the hidden row there; the last
+//                    CTA publishes counts and releases flag_d at the owner.
+//   ep_recv          (owner)  bounded wait for every source's flag, histogram
+//                    of local experts, expert-ordered position of each row.
+//   ep_permute       (owner)  copy received rows into expert order.
+//   grouped GEMMs    (owner)  gate/up + SwiGLU, down (gemm.cu).
+//   ep_combine_send  (owner)  store each result row into its source's comb
+//                    region; the last CTA releases flag_c at every source.
+//   ep_combine_reduce(source) bounded wait for every owner's flag, then
+//                    out[t] = residual[t] + sum_k w[t,k] * comb[map[t,k]] in a
+//                    fixed k order; the last CTA advances the epoch.
+// Flags carry a monotonically increasing epoch kept in device memory, so the
+// sequence is replayable inside a CUDA graph without host work.  Buffer reuse
+// across consecutive calls is safe: a source only dispatches call i+1 after
+// its combine of call i has seen every owner's flag, and an owner only sends
+// combine results after receiving every source's dispatch.
+//
+// The reference has no distributed code; its MoE loops over experts on one
+// device with a host sync per top-k slot (pio/models/qwen3_coder_30b/model.py:308-353).
+#include <cstring>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "status.h"
+
+namespace mb {
+
+struct EpLayout {
+  int64_t recv_x, comb, meta, cnt, flag_d, flag_c, total;
+};
+
+static EpLayout ep_layout(int64_t N, int64_t C, int64_t H) {
+  auto al = [](int64_t x) { return (x + 255) / 256 * 256; };
+  EpLayout L;
+  L.recv_x = 0;
+  L.comb = al(L.recv_x + N * C * H * 2);
+  L.meta = al(L.comb + N * C * H * 2);
+  L.cnt = al(L.meta + N * C * 4);
+  L.flag_d = al(L.cnt + N * 4);
+  L.flag_c = al(L.flag_d + N * 4);
+  L.total = al(L.flag_c + N * 4);
+  return L;
+}
+
+int64_t ep_buffer_bytes(int64_t N, int64_t C, int64_t H) { return ep_layout(N, C, H).total; }
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded spin until *p >= want (wrap-safe compare).  Returns false on timeout.
+__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t want, int* status, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if ((int32_t)(ld_acquire_sys(p) - want) >= 0) return true;
+    if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_status(status, code);
+      return false;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T* at_off(uint64_t base, int64_t off) {
+  return reinterpret_cast<T*>(base + off);
+}
+
+struct EpArgs {
+  const uint64_t* peers;  // [N] base address of every rank's exchange buffer (own rank included)
+  int rank, N, C, H, El;
+  EpLayout L;
+  uint32_t* epoch;        // [1] local
+  int* send_cnt;          // [N] local, zero between calls
+  int* done;              // [4] local CTA-completion counters, zero between calls
+  int* status;
+};
+
+// ---------------------------------------------------------------- dispatch
+__global__ void ep_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ ids,
+                                   int TK, int K, int* __restrict__ map) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const int warps = blockDim.x / 32, warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  for (int pair = blockIdx.x * warps + warp; pair < TK; pair += gridDim.x * warps) {
+    const int e = ids[pair];
+    const int dst = e / a.El;
+    int slot = 0;
+    if (lane == 0) {
+      slot = atomicAdd(&a.send_cnt[dst], 1);
+      map[pair] = dst * a.C + slot;
+      at_off<int>(a.peers[dst], a.L.meta)[a.rank * a.C + slot] = e % a.El;
+    }
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(pair / K) * a.H);
+    uint4* dstp = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[dst], a.L.recv_x) +
+                                           ((size_t)a.rank * a.C + slot) * a.H);
+    for (int i = lane; i < a.H / 8; i += 32) dstp[i] = src[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(&a.done[0], 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  for (int dst = threadIdx.x; dst < a.N; dst += blockDim.x) {
+    at_off<int>(a.peers[dst], a.L.cnt)[a.rank] = atomicAdd(&a.send_cnt[dst], 0);
+  }
+  __threadfence_system();
+  __syncthreads();
+  for (int dst = threadIdx.x; dst < a.N; dst += blockDim.x) {
+    st_release_sys(at_off<uint32_t>(a.peers[dst], a.L.flag_d) + a.rank, epoch);
+    a.send_cnt[dst] = 0;
+  }
+  if (threadIdx.x == 0) a.done[0] = 0;
+}
+
+// ---------------------------------------------------------------- receive
+// One CTA of 1024 threads: waits for all sources, orders rows by local expert.
+__global__ void ep_recv_kernel(EpArgs a, int* __restrict__ row_pos, int* __restrict__ offs, int* __restrict__ abort) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const uint64_t self = a.peers[a.rank];
+  __shared__ int hist[1024];
+  __shared__ int cursor[1024];
+  __shared__ int cnts[64];
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  for (int e = threadIdx.x; e < a.El; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  for (int src = threadIdx.x; src < a.N; src += blockDim.x) {
+    if (!wait_flag(at_off<uint32_t>(self, a.L.flag_d) + src, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
+    cnts[src] = ld_acquire_sys(reinterpret_cast<const uint32_t*>(at_off<int>(self, a.L.cnt) + src));
+  }
+  __syncthreads();
+  __threadfence();  // order this thread's reads after the flag acquires above
+  if (!ok_all) {
+    if (threadIdx.x == 0) *abort = 1;
+  }
+  const int* meta = at_off<int>(self, a.L.meta);
+  const int rows = a.N * a.C;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    const int src = i / a.C, slot = i % a.C;
+    if (ok_all && slot < cnts[src]) atomicAdd(&hist[__ldcg(meta + i)], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // El <= 1024: serial scan is a few hundred cycles
+    int acc = 0;
+    for (int e = 0; e < a.El; ++e) {
+      offs[e] = acc;
+      cursor[e] = acc;
+      acc += hist[e];
+    }
+    offs[a.El] = acc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    const int src = i / a.C, slot = i % a.C;
+    row_pos[i] = (ok_all && slot < cnts[src]) ? atomicAdd(&cursor[__ldcg(meta + i)], 1) : -1;
+  }
+}
+
+// warp per received row: recv_x[i] -> xs[row_pos[i]]
+__global__ void ep_permute_kernel(EpArgs a, const int* __restrict__ row_pos, __nv_bfloat16* __restrict__ xs) {
+  pdl_wait();
+  pdl_trigger();
+  const int warps = blockDim.x / 32, lane = threadIdx.x & 31;
+  const uint64_t self = a.peers[a.rank];
+  const __nv_bfloat16* rx = at_off<__nv_bfloat16>(self, a.L.recv_x);
+  for (int i = blockIdx.x * warps + threadIdx.x / 32; i < a.N * a.C; i += gridDim.x * warps) {
+    const int p = row_pos[i];
+    if (p < 0) continue;
+    const uint4* s = reinterpret_cast<const uint4*>(rx + (size_t)i * a.H);
+    uint4* d = reinterpret_cast<uint4*>(xs + (size_t)p * a.H);
+    for (int j = lane; j < a.H / 8; j += 32) d[j] = __ldcg(s + j);
+  }
+}
+
+// ---------------------------------------------------------------- combine
+__global__ void ep_combine_send_kernel(EpArgs a, const int* __restrict__ row_pos, const __nv_bfloat16* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const int warps = blockDim.x / 32, lane = threadIdx.x & 31;
+  for (int i = blockIdx.x * warps + threadIdx.x / 32; i < a.N * a.C; i += gridDim.x * warps) {
+    const int p = row_pos[i];
+    if (p < 0) continue;
+    const int src = i / a.C, slot = i % a.C;
+    const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)p * a.H);
+    uint4* d = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[src], a.L.comb) +
+                                        ((size_t)a.rank * a.C + slot) * a.H);
+    for (int j = lane; j < a.H / 8; j += 32) d[j] = s[j];
+  }
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(&a.done[1], 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  for (int src = threadIdx.x; src < a.N; src += blockDim.x)
+    st_release_sys(at_off<uint32_t>(a.peers[src], a.L.flag_c) + a.rank, epoch);
+  if (threadIdx.x == 0) a.done[1] = 0;
+}
+
+// CTA per token: wait for every owner, weighted sum in k order, + residual.
+__global__ void ep_combine_reduce_kernel(EpArgs a, const int* __restrict__ map, const float* __restrict__ wts, int T,
+                                         int K, const __nv_bfloat16* __restrict__ residual,
+                                         __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const uint64_t self = a.peers[a.rank];
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  for (int o = threadIdx.x; o < a.N; o += blockDim.x)
+    if (!wait_flag(at_off<uint32_t>(self, a.L.flag_c) + o, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
+  __syncthreads();
+  __threadfence();
+  const __nv_bfloat16* comb = at_off<__nv_bfloat16>(self, a.L.comb);
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    for (int c = threadIdx.x * 8; c < a.H; c += blockDim.x * 8) {
+      float acc[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = residual ? __bfloat162float(residual[(size_t)t * a.H + c + q]) : 0.f;
+      if (ok_all) {
+        for (int k = 0; k < K; ++k) {
+          const int m = map[t * K + k];
+          const float w = wts[t * K + k];
+          uint4 raw = __ldcg(reinterpret_cast<const uint4*>(comb + (size_t)m * a.H + c));
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += w * __bfloat162float(h[q]);
+        }
+      }
+      __align__(16) __nv_bfloat16 o8[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o8[q] = __float2bfloat16(acc[q]);
+      *reinterpret_cast<uint4*>(out + (size_t)t * a.H + c) = *reinterpret_cast<uint4*>(o8);
+    }
+  }
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(&a.done[2], 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    *a.epoch = epoch;  // every kernel of this call has read the old value
+    a.done[2] = 0;
+  }
+}
+
+// ---------------------------------------------------------------- host
+static EpArgs make_args(const at::Tensor& peers, int64_t rank, int64_t N, int64_t C, int64_t H, int64_t El,
+                        at::Tensor& state) {
+  TORCH_CHECK(peers.scalar_type() == at::kLong && peers.numel() == N && peers.is_cuda());
+  TORCH_CHECK(state.scalar_type() == at::kInt && state.numel() >= 8 + N && state.is_cuda());
+  TORCH_CHECK(H % 8 == 0 && N <= 64 && El <= 1024);
+  EpArgs a;
+  a.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.rank = (int)rank;
+  a.N = (int)N;
+  a.C = (int)C;
+  a.H = (int)H;
+  a.El = (int)El;
+  a.L = ep_layout(N, C, H);
+  int* s = state.data_ptr<int>();
+  a.epoch = reinterpret_cast<uint32_t*>(s);  // state[0]
+  a.done = s + 4;                             // state[4..7]
+  a.send_cnt = s + 8;                         // state[8..8+N)
+  a.status = status_ptr(peers.device().index());
+  return a;
+}
+
+// Runs the dispatch half: ids [T, K] int32 (global expert ids) -> rows in the
+// owners' exchange buffers; on return (stream order) this rank's xs holds its
+// received rows in local-expert order with offs [El+1].
+void ep_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                 const at::Tensor& x, const at::Tensor& ids, at::Tensor& map, at::Tensor& row_pos, at::Tensor& offs,
+                 at::Tensor& xs, at::Tensor& abort) {
+  const int64_t N = peers.numel(), T = x.size(0), H = x.size(1), K = ids.size(1);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && ids.scalar_type() == at::kInt);
+  TORCH_CHECK(T * K <= C, "ep_dispatch: T*K (", T * K, ") exceeds capacity ", C);
+  TORCH_CHECK(row_pos.numel() >= N * C && offs.numel() >= El + 1 && xs.size(0) >= N * C && map.numel() >= T * K);
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int TK = (int)(T * K);
+  const int grid = std::max(1, std::min(148, (TK + 7) / 8));
+  launch_k(ep_dispatch_kernel, grid, 256, 0, st, a, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+           ids.data_ptr<int>(), TK, (int)K, map.data_ptr<int>());
+  launch_k(ep_recv_kernel, 1, 1024, 0, st, a, row_pos.data_ptr<int>(), offs.data_ptr<int>(), abort.data_ptr<int>());
+  const int rows = (int)(N * C);
+  launch_k(ep_permute_kernel, std::max(1, std::min(296, (rows + 7) / 8)), 256, 0, st, a,
+           (const int*)row_pos.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Combine half: y [N*C, H] expert outputs in xs order -> out [T, H].
+void ep_combine(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                const at::Tensor& row_pos, const at::Tensor& y, const at::Tensor& map, const at::Tensor& wts,
+                const c10::optional<at::Tensor>& residual, at::Tensor& out) {
+  const int64_t N = peers.numel(), T = out.size(0), H = out.size(1), K = wts.size(1);
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && out.is_contiguous());
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(y.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int rows = (int)(N * C);
+  launch_k(ep_combine_send_kernel, std::max(1, std::min(296, (rows + 7) / 8)), 256, 0, st, a,
+           (const int*)row_pos.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()));
+  const __nv_bfloat16* r =
+      (residual && residual->defined()) ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  launch_k(ep_combine_reduce_kernel, (int)std::max<int64_t>(1, T), 256, 0, st, a, (const int*)map.data_ptr<int>(),
+           (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ---------------------------------------------------------------- IPC buffers
+// Exchange buffers are plain cudaMalloc allocations shared with CUDA IPC
+// handles (no multicast objects).
+std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes) {
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&p, bytes));
+  C10_CUDA_CHECK(cudaMemset(p, 0, bytes));
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  return {reinterpret_cast<int64_t>(p), std::string(reinterpret_cast<const char*>(&h), sizeof(h))};
+}
+
+int64_t ipc_open(const std::string& handle) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) { C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+void ipc_free(int64_t ptr) { C10_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr))); }
+
+}  // namespace mb

@@ -26,6 +26,17 @@ void moe_permute(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& o
                  at::Tensor& pos, at::Tensor& xs);
 void moe_combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& wts,
                  const c10::optional<at::Tensor>& residual, at::Tensor& out);
+int64_t ep_buffer_bytes(int64_t N, int64_t C, int64_t H);
+void ep_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                 const at::Tensor& x, const at::Tensor& ids, at::Tensor& map, at::Tensor& row_pos, at::Tensor& offs,
+                 at::Tensor& xs, at::Tensor& abort);
+void ep_combine(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                const at::Tensor& row_pos, const at::Tensor& y, const at::Tensor& map, const at::Tensor& wts,
+                const c10::optional<at::Tensor>& residual, at::Tensor& out);
+std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
+int64_t ipc_open(const std::string& handle);
+void ipc_close(int64_t ptr);
+void ipc_free(int64_t ptr);
 void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
 void swiglu(const at::Tensor& gu, at::Tensor& out);
 void argmax(const at::Tensor& logits, at::Tensor& out_idx, const c10::optional<at::Tensor>& out_val,
@@ -45,6 +56,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &mb::moe_route);
   m.def("moe_permute", &mb::moe_permute);
   m.def("moe_combine", &mb::moe_combine);
+  m.def("ep_buffer_bytes", &mb::ep_buffer_bytes);
+  m.def("ep_dispatch", &mb::ep_dispatch);
+  m.def("ep_combine", &mb::ep_combine);
+  m.def("ipc_alloc", [](int64_t b) {
+    auto r = mb::ipc_alloc(b);
+    return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));
+  });
+  m.def("ipc_open", [](pybind11::bytes h) { return mb::ipc_open(std::string(h)); });
+  m.def("ipc_close", &mb::ipc_close);
+  m.def("ipc_free", &mb::ipc_free);
   m.def("embed", &mb::embed);
   m.def("swiglu", &mb::swiglu);
   m.def("argmax", &mb::argmax);

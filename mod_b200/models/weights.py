@@ -127,14 +127,23 @@ class _Init:
     def zeros(self, *shape) -> torch.Tensor:
         return torch.zeros(*shape, device=self.device, dtype=self.dtype)
 
+    def expert_normal(self, out: torch.Tensor, seed: int, layer: int, expert: int, which: int) -> None:
+        """Fills ``out`` from a generator keyed by (seed, layer, expert, which), so an
+        expert's weights do not depend on how experts are sharded across ranks."""
+        self.egen = getattr(self, "egen", None) or torch.Generator(device=self.gen.device)
+        self.egen.manual_seed(((seed * 1_000_003 + layer) * 4099 + expert) * 3 + which + 17)
+        out.normal_(0.0, self.std, generator=self.egen)
+
 
 def random_weights(cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
                    expert_range: Optional[tuple] = None) -> ModelWeights:
     """N(0, 0.02) weights of the given architecture.
 
     ``expert_range=(lo, hi)`` materialises only experts [lo, hi) (expert
-    parallelism); the generator still advances as if all experts existed per
-    layer only when ``expert_range`` is None, so EP shards are seeded per rank.
+    parallelism).  Expert weights come from per-(layer, expert) generators and
+    everything else from one sequential generator, so every rank of an
+    expert-parallel group holds the same dense weights and the union of the
+    shards equals the unsharded model.
     """
     cfg.validate()
     ini = _Init(device, dtype, seed)
@@ -166,8 +175,12 @@ def random_weights(cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: i
             E, I = cfg.num_experts, cfg.moe_intermediate_size
             lo, hi = expert_range if expert_range else (0, E)
             n = hi - lo
-            moe = MoEWeights(router=ini.normal(E, H), w13=ini.normal(n * 2 * I, H), w2=ini.normal(n * H, I),
-                             e_lo=lo, e_hi=hi)
+            w13 = torch.empty(n * 2 * I, H, device=device, dtype=dtype)
+            w2 = torch.empty(n * H, I, device=device, dtype=dtype)
+            for j, e in enumerate(range(lo, hi)):
+                ini.expert_normal(w13[j * 2 * I:(j + 1) * 2 * I], seed, i, e, 0)
+                ini.expert_normal(w2[j * H:(j + 1) * H], seed, i, e, 1)
+            moe = MoEWeights(router=ini.normal(E, H), w13=w13, w2=w2, e_lo=lo, e_hi=hi)
             if cfg.shared_expert_intermediate_size:
                 S = cfg.shared_expert_intermediate_size
                 moe.shared = MLPWeights(gate_up=ini.normal(2 * S, H), down=ini.normal(H, S))

@@ -7,6 +7,7 @@ from mod_b200.engine import SamplingParams
 from mod_b200.engine.llm_engine import LLMEngine
 from mod_b200.models import oracle
 from mod_b200.models.weights import random_weights
+from tests.test_engine_cpu import decisive
 
 pytestmark = pytest.mark.gpu
 
@@ -18,7 +19,7 @@ def _cos(a, b):
 @pytest.mark.parametrize("name", ["tiny-dense", "tiny-moe", "tiny-glm", "tiny-next"])
 def test_native_prefill_and_decode_logits_match_oracle(cuda, name):
     cfg = get_preset(name)
-    w = random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0)
+    w = decisive(random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0))
     eng = LLMEngine(cfg, weights=w, backend="native", device=cuda, max_batch=4, max_model_len=128)
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (33, 17, 50)]
@@ -41,7 +42,7 @@ def test_native_prefill_and_decode_logits_match_oracle(cuda, name):
 @pytest.mark.parametrize("name", ["tiny-dense", "tiny-moe"])
 def test_native_graph_decode_matches_eager(cuda, name):
     cfg = get_preset(name)
-    w = random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0)
+    w = decisive(random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0))
     g = torch.Generator().manual_seed(7)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (12, 30, 7)]
     outs = []

@@ -1,0 +1,55 @@
+"""Expert-parallel MoE: baseline on gloo CPU ranks, fused path on GPUs."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _spawn_cpu(rank, world, port):
+    sys.path.insert(0, HERE)
+    import _ep_worker
+
+    _ep_worker.run(rank, world, "nccl", port, "cpu")
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_baseline_gloo_matches_unsharded(world):
+    mp.spawn(_spawn_cpu, args=(world, _port()), nprocs=world, join=True)
+
+
+@pytest.mark.gpu
+def test_fused_ep_single_gpu_self_exchange(cuda):
+    sys.path.insert(0, HERE)
+    import _ep_worker
+    import torch.distributed as dist
+
+    _ep_worker.run(0, 1, "fused", _port(), "cuda")
+    assert not dist.is_initialized()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("impl", ["fused", "nccl"])
+def test_ep_multi_gpu(cuda, impl):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    n = 2 if n < 4 else 4
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_ep_worker.py"), impl]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -13,7 +13,10 @@ Per run:
   4. ``e2e``: K decode steps through the public API ``LLMEngine.step()``: each
      step copies its inputs host->device from pinned memory, runs, and reads
      the sampled tokens back device->host.
-N > 1 runs one process per GPU (torchrun); each rank serves 128/N sequences.
+N > 1 runs one process per GPU (torchrun) with expert parallelism: each rank
+serves 128/N sequences with a replicated attention stack (DP attention) and
+holds E/N experts; MoE layers exchange tokens with the fused NVLink
+dispatch/combine kernels (native) or NCCL all-to-all (baseline).
 Decode reads ~61 GB of weights per step on one GPU, far above the 126 MB L2,
 so no L2 flush is needed between steps.
 """
@@ -155,12 +158,12 @@ def main():
     assert per_rank * world == args.batch, "global batch must divide by the GPU count"
     K, W = args.steps, args.warmup
     backend = "native" if args.impl == "native" else "torch"
-    max_len = args.prompt_len + W + 2 * K + 16
+    max_len = args.prompt_len + W + 3 * K + 16
     eng = LLMEngine(cfg, backend=backend, device=dev, max_batch=per_rank, max_model_len=max_len,
                     max_prefill_tokens=16384, seed=0, use_graphs=True)
     g = torch.Generator().manual_seed(1000 + rank)
     prompts = [torch.randint(0, cfg.vocab_size, (args.prompt_len,), generator=g).tolist() for _ in range(per_rank)]
-    params = SamplingParams(max_new_tokens=W + 2 * K + 8, ignore_eos=True)
+    params = SamplingParams(max_new_tokens=W + 3 * K + 8, ignore_eos=True)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
@@ -175,6 +178,12 @@ def main():
         eng.step()
     runner = eng.runner
     B = max(runner.graphs) if runner.graphs else None
+    if B is None:  # eager path (baseline): a timed step is one engine step
+        def one_step():
+            eng.step()
+    else:
+        def one_step():
+            runner.graphs[B].replay()
 
     def maxr(x):
         if world == 1:
@@ -191,7 +200,7 @@ def main():
         torch.cuda.synchronize()
         st.record()
         for _ in range(K):
-            runner.graphs[B].replay()
+            one_step()
         en.record()
         torch.cuda.synchronize()
         if world > 1:
@@ -210,7 +219,7 @@ def main():
     if world > 1:
         dist.barrier()
     e2e_ms = maxr((time.perf_counter() - t1) * 1000) / K
-    ours, total = count_launches(lambda: runner.graphs[B].replay())
+    ours, total = count_launches(one_step)
     from mod_b200.ops import check_status
 
     if backend == "native":
@@ -223,8 +232,10 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random token ids, random-init N(0,0.02) weights, seed 0)",
             "impl": args.impl,
             "config": {"model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt_len,
-                       "parallelism": f"dp{world}" if world > 1 else "single", "layers": cfg.num_hidden_layers,
-                       "decode_batch_per_gpu": per_rank, "timed": "CUDA-graph replays of one decode step at fixed context",
+                       "parallelism": f"ep{world}+dp_attn{world}" if world > 1 else "single",
+                       "layers": cfg.num_hidden_layers, "decode_batch_per_gpu": per_rank,
+                       "timed": ("CUDA-graph replays of one decode step at fixed context" if B is not None
+                                 else "engine decode steps (eager)"),
                        "l2": "no flush: a step reads ~61 GB of weights (> 126 MB L2)"},
             "e2e": {"value": round(args.batch / (e2e_ms / 1000.0), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},

@@ -35,13 +35,36 @@ class LLMEngine:
     def __init__(self, cfg: ModelConfig, weights: Optional[ModelWeights] = None, backend: str = "native",
                  device: Union[str, torch.device] = "cuda", max_batch: int = 128, max_model_len: int = 4096,
                  num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
-                 max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None):
+                 max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
+                 expert_parallel: Optional[bool] = None):
+        """``expert_parallel`` (default: on when a process group of >1 ranks
+        exists and the model is MoE): every rank serves its own requests with a
+        replicated attention stack and holds E/world experts; MoE layers
+        exchange tokens with the fused NVLink dispatch/combine (native backend)
+        or NCCL all-to-all (torch backend)."""
+        import torch.distributed as dist
+
         self.cfg = cfg
         self.device = torch.device(device)
+        world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        rank = dist.get_rank() if world > 1 else 0
+        if expert_parallel is None:
+            expert_parallel = world > 1 and cfg.is_moe
+        self.expert_parallel = expert_parallel
+        self.backend = make_backend(backend)
+        moe_impl = None
+        if expert_parallel:
+            El = cfg.num_experts // world
+            if weights is None and model is None:
+                weights = random_weights(cfg, device=self.device, seed=seed, expert_range=(rank * El, (rank + 1) * El))
+            from ..parallel.ep import FusedEPMoE, NcclEPMoE
+
+            moe_impl = (FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
+                                   prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
+                        if backend == "native" else NcclEPMoE(cfg, self.backend))
         if weights is None and model is None:
             weights = random_weights(cfg, device=self.device, seed=seed)
-        self.backend = make_backend(backend)
-        self.model = model if model is not None else DecoderLM(cfg, weights, self.backend)
+        self.model = model if model is not None else DecoderLM(cfg, weights, self.backend, moe_impl=moe_impl)
         bs = 16
         if num_blocks is None:
             num_blocks = self._auto_blocks(kv_mem_fraction, max_batch, max_model_len, kv_heads)
@@ -51,7 +74,7 @@ class LLMEngine:
         self.blocks = BlockManager(num_blocks, bs, max_seqs=max_batch)
         self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens)
         self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
-                                  use_graphs=use_graphs, device=self.device)
+                                  use_graphs=use_graphs and backend == "native", device=self.device)
         self.seqs: Dict[int, Sequence] = {}
         self.last_step: Dict[str, float] = {}
 

@@ -67,10 +67,30 @@ class ExchangeBuffer:
             self.ptr = 0
 
 
-class FusedEPMoE:
-    """Callable ``(x [T, H], moe_weights) -> [T, H]`` for one EP rank."""
+class _EpContext:
+    """Exchange buffer + device state for one capacity (max tokens per call)."""
 
-    def __init__(self, cfg, backend, max_tokens: int, group=None):
+    def __init__(self, C, world, rank, El, K, H, max_tokens, group):
+        self.max_tokens = max_tokens
+        self.cap = max_tokens * K
+        self.buf = ExchangeBuffer(C.ep_buffer_bytes(world, self.cap, H), group)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.state = torch.zeros(8 + world, dtype=torch.int32, device=dev)
+        rows = world * self.cap
+        self.row_pos = torch.empty(rows, dtype=torch.int32, device=dev)
+        self.offs = torch.zeros(El + 1, dtype=torch.int32, device=dev)
+        self.xs = torch.empty(rows, H, dtype=torch.bfloat16, device=dev)
+        self.abort = torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+class FusedEPMoE:
+    """Callable ``(x [T, H], moe_weights) -> [T, H]`` for one EP rank.
+
+    Two exchange contexts: a small one sized for a decode step (the one used
+    inside CUDA graphs) and a large one for prefill, which is processed in
+    chunks; all ranks run the same number of rounds."""
+
+    def __init__(self, cfg, backend, max_tokens: int, group=None, prefill_tokens: int = 1024):
         from ..ops import load_extension, native
 
         self.C = load_extension()
@@ -83,21 +103,12 @@ class FusedEPMoE:
         assert E % self.world == 0, "experts must divide evenly across ranks"
         self.El = E // self.world
         self.K = K
-        self.max_tokens = max_tokens
-        self.cap = max_tokens * K                    # rows per (source, owner)
-        H = cfg.hidden_size
-        self.H = H
-        nbytes = self.C.ep_buffer_bytes(self.world, self.cap, H)
-        self.buf = ExchangeBuffer(nbytes, group)
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.state = torch.zeros(8 + self.world, dtype=torch.int32, device=dev)
-        rows = self.world * self.cap
-        self.row_pos = torch.empty(rows, dtype=torch.int32, device=dev)
-        self.offs = torch.zeros(self.El + 1, dtype=torch.int32, device=dev)
-        self.xs = torch.empty(rows, H, dtype=torch.bfloat16, device=dev)
-        self.abort = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.H = cfg.hidden_size
+        self.small = _EpContext(self.C, self.world, self.rank, self.El, K, self.H, max_tokens, group)
+        self.large = (_EpContext(self.C, self.world, self.rank, self.El, K, self.H, prefill_tokens, group)
+                      if prefill_tokens > max_tokens else self.small)
 
-    def _chunk(self, x, mo):
+    def _chunk(self, ctx, x, mo):
         cfg, N = self.cfg, self.N
         T = x.shape[0]
         dev = x.device
@@ -110,32 +121,34 @@ class FusedEPMoE:
         cursor = torch.empty(E, dtype=torch.int32, device=dev)
         N.moe_route(logits, self.K, cfg.norm_topk_prob, ids, wts, counts, offs_g, cursor)
         emap = torch.empty(T * self.K, dtype=torch.int32, device=dev)
-        self.C.ep_dispatch(self.buf.peers, self.state, self.rank, self.cap, self.El, x, ids, emap, self.row_pos,
-                           self.offs, self.xs, self.abort)
-        rows = self.xs.shape[0]
+        self.C.ep_dispatch(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, x, ids, emap, ctx.row_pos,
+                           ctx.offs, ctx.xs, ctx.abort)
+        rows = ctx.xs.shape[0]
         exp_rows = max(1, (self.world * T * self.K) // max(1, self.El * self.world))
-        h = N.grouped_linear(self.xs, mo.w13, self.offs, self.El, True, min(rows, 4 * exp_rows))
-        y = N.grouped_linear(h, mo.w2, self.offs, self.El, False, min(rows, 4 * exp_rows))
+        h = N.grouped_linear(ctx.xs, mo.w13, ctx.offs, self.El, True, min(rows, 4 * exp_rows))
+        y = N.grouped_linear(h, mo.w2, ctx.offs, self.El, False, min(rows, 4 * exp_rows))
         out = torch.empty_like(x)
-        self.C.ep_combine(self.buf.peers, self.state, self.rank, self.cap, self.El, self.row_pos, y, emap, wts,
-                          None, out)
+        self.C.ep_combine(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, ctx.row_pos, y, emap, wts, None,
+                          out)
         return out
 
     def __call__(self, x: torch.Tensor, mo) -> torch.Tensor:
         T = x.shape[0]
-        # every rank must run the same number of rounds: agree on the chunk count
-        n = max(1, -(-T // self.max_tokens))
-        capturing = torch.cuda.is_current_stream_capturing()
-        if self.world > 1 and not capturing:
-            t = torch.tensor([n], dtype=torch.int64, device=x.device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
-            n = int(t.item())
-        elif capturing:
-            assert T <= self.max_tokens, "captured EP step exceeds the exchange capacity"
+        if torch.cuda.is_current_stream_capturing():
+            assert T <= self.small.max_tokens, "captured EP step exceeds the decode exchange capacity"
+            ctx, n = self.small, 1
+        else:
+            tmax = T
+            if self.world > 1:  # all ranks must pick the same context and round count
+                t = torch.tensor([T], dtype=torch.int64, device=x.device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+                tmax = int(t.item())
+            ctx = self.small if tmax <= self.small.max_tokens else self.large
+            n = max(1, -(-tmax // ctx.max_tokens))
         outs = []
         for c in range(n):
-            xc = x[c * self.max_tokens:(c + 1) * self.max_tokens]
-            outs.append(self._chunk(xc.contiguous(), mo))
+            xc = x[c * ctx.max_tokens:(c + 1) * ctx.max_tokens]
+            outs.append(self._chunk(ctx, xc.contiguous(), mo))
         out = torch.cat(outs, 0) if len(outs) > 1 else outs[0]
         if mo.shared is not None:
             sh = self.be.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down).float()

@@ -205,7 +205,7 @@ static at::ScalarType to_torch(const std::string& d) {
   throw std::runtime_error("safetensors: unsupported dtype " + d);
 }
 
-static std::string from_torch(at::ScalarType t) {
+[[maybe_unused]] static std::string from_torch(at::ScalarType t) {
   switch (t) {
     case at::kDouble: return "F64";
     case at::kFloat: return "F32";
@@ -296,7 +296,9 @@ at::Tensor SafeTensorsFile::get_slice(const std::string& name, int64_t dim, int6
   TORCH_CHECK(dim >= 0 && dim < t.dim(), "get_slice: bad dim");
   TORCH_CHECK(rank >= 0 && rank < world, "get_slice: bad rank");
   const int64_t n = t.size(dim);
-  TORCH_CHECK(n % world == 0, "get_slice: dim ", dim, " of ", name, " (", n, ") not divisible by ", world);
+  if (n % world != 0)
+    throw std::invalid_argument("get_slice: dim " + std::to_string(dim) + " of " + name + " (" + std::to_string(n) +
+                                ") is not divisible by " + std::to_string(world));
   const int64_t part = n / world;
   at::Tensor s = t.narrow(dim, rank * part, part);
   return dim == 0 ? s : s.contiguous();
@@ -319,56 +321,6 @@ std::map<std::string, TensorInfo> read_header(const std::string& path) {
   return out;
 }
 
-static std::string esc(const std::string& s) {
-  std::string o;
-  for (char c : s) {
-    if (c == '"' || c == '\\') { o += '\\'; o += c; }
-    else if (c == '\n') o += "\\n";
-    else o += c;
-  }
-  return o;
-}
-
-void save_file(const std::string& path, const std::map<std::string, at::Tensor>& tensors,
-               const std::map<std::string, std::string>& metadata) {
-  std::ostringstream h;
-  h << "{";
-  bool first = true;
-  if (!metadata.empty()) {
-    h << "\"__metadata__\":{";
-    bool f2 = true;
-    for (auto& m : metadata) {
-      h << (f2 ? "" : ",") << "\"" << esc(m.first) << "\":\"" << esc(m.second) << "\"";
-      f2 = false;
-    }
-    h << "}";
-    first = false;
-  }
-  int64_t off = 0;
-  std::vector<at::Tensor> cpu;
-  for (auto& kv : tensors) {
-    at::Tensor t = kv.second.detach().to(at::kCPU).contiguous();
-    const int64_t nb = t.numel() * t.element_size();
-    h << (first ? "" : ",") << "\"" << esc(kv.first) << "\":{\"dtype\":\"" << from_torch(t.scalar_type())
-      << "\",\"shape\":[";
-    for (int64_t i = 0; i < t.dim(); ++i) h << (i ? "," : "") << t.size(i);
-    h << "],\"data_offsets\":[" << off << "," << off + nb << "]}";
-    off += nb;
-    first = false;
-    cpu.push_back(t);
-  }
-  h << "}";
-  std::string hdr = h.str();
-  while ((8 + hdr.size()) % 8) hdr += ' ';  // keep tensor data 8-byte aligned
-  std::ofstream f(path, std::ios::binary);
-  if (!f) throw std::runtime_error("safetensors: cannot write " + path);
-  uint64_t n = hdr.size();
-  f.write(reinterpret_cast<const char*>(&n), 8);
-  f.write(hdr.data(), hdr.size());
-  for (auto& t : cpu) f.write(reinterpret_cast<const char*>(t.data_ptr()), t.numel() * t.element_size());
-  if (!f) throw std::runtime_error("safetensors: write failed for " + path);
-}
-
 void bind(pybind11::module& m) {
   namespace py = pybind11;
   py::class_<SafeTensorsFile>(m, "SafeTensorsFile")
@@ -380,8 +332,6 @@ void bind(pybind11::module& m) {
       .def("shape", [](const SafeTensorsFile& f, const std::string& n) { return f.info(n).shape; })
       .def("dtype", [](const SafeTensorsFile& f, const std::string& n) { return f.info(n).dtype; })
       .def_property_readonly("path", &SafeTensorsFile::path);
-  m.def("save_file", &save_file, py::arg("path"), py::arg("tensors"),
-        py::arg("metadata") = std::map<std::string, std::string>{});
   m.def("read_header", [](const std::string& p) {
     py::dict d;
     for (auto& kv : read_header(p)) {

@@ -5,7 +5,7 @@
 // [begin, end]} (offsets relative to the end of the header), plus an optional
 // "__metadata__" object of string pairs; then the raw tensor bytes.
 //
-// The reader mmaps the file and returns zero-copy torch views that keep the
+// Writing is done in Python (mod_b200/io/safetensors.py).  The reader mmaps the file and returns zero-copy torch views that keep the
 // mapping alive; shard slicing (dim, rank, world) returns a view for dim 0 and
 // a contiguous copy otherwise, so a tensor-/expert-parallel rank touches only
 // its slice.  The reference's loader (pio/plugins/cpu/c_src/safetensors_loader.c)
@@ -45,8 +45,6 @@ class SafeTensorsFile {
   size_t data_start_ = 0;
 };
 
-void save_file(const std::string& path, const std::map<std::string, at::Tensor>& tensors,
-               const std::map<std::string, std::string>& metadata);
 std::map<std::string, TensorInfo> read_header(const std::string& path);
 
 void bind(pybind11::module& m);

@@ -1,0 +1,146 @@
+"""Request managers kept for API parity with the reference.
+
+* :class:`BatchManager` - ``add_request`` / ``step`` / ``get_status`` as in
+  ``pio/common/managers/batch_manager.py:9-84``, but each ``step`` advances the
+  continuous batcher by one engine step instead of running one request to
+  completion; a failed request is marked FAILED while the others continue.
+* :class:`StreamingEngine` - asynchronous front-end: requests go to a
+  priority queue; a worker thread drives the engine; ``generate_stream``
+  yields tokens as they are produced
+  (``pio/common/processing/streaming_computation.py:43-197``).
+* :class:`AdaptiveAdmission` - admission control from free KV blocks and the
+  measured step time (the role of ``AdaptiveBatchManager``,
+  ``pio/common/processing/adaptive_batch_manager.py:42-251``).
+"""
+from __future__ import annotations
+
+import heapq
+import itertools
+import queue
+import threading
+import time
+from typing import Any, Dict, Iterator, List, Optional
+
+from ..engine.sequence import SamplingParams, SeqStatus
+
+
+class BatchManager:
+    def __init__(self, plugin_or_engine):
+        self.plugin = plugin_or_engine if hasattr(plugin_or_engine, "engine") else None
+        self._engine = None if self.plugin else plugin_or_engine
+        self.requests: Dict[Any, int] = {}
+
+    @property
+    def engine(self):
+        return self.plugin.engine if self.plugin else self._engine
+
+    def add_request(self, request_id, token_ids: List[int], params: Optional[SamplingParams] = None) -> None:
+        self.requests[request_id] = self.engine.add_request([int(t) for t in token_ids], params)
+
+    def step(self) -> List[Any]:
+        """One engine step; returns the ids of requests that completed in it."""
+        done = self.engine.step()
+        inv = {v: k for k, v in self.requests.items()}
+        return [inv[s.req_id] for s in done if s.req_id in inv]
+
+    def get_status(self, request_id) -> str:
+        seq = self.engine.seqs.get(self.requests.get(request_id))
+        return "unknown" if seq is None else seq.status.value
+
+    def get_output(self, request_id) -> List[int]:
+        return list(self.engine.seqs[self.requests[request_id]].output)
+
+    def run_all(self) -> Dict[Any, List[int]]:
+        while self.engine.has_unfinished():
+            self.step()
+        return {rid: self.get_output(rid) for rid in self.requests}
+
+
+class StreamingEngine:
+    """Thread-safe streaming front-end over one engine."""
+
+    def __init__(self, engine, max_queue: int = 1024):
+        self.engine = engine
+        self.max_queue = max_queue
+        self._pq: List = []
+        self._count = itertools.count()
+        self._lock = threading.Lock()
+        self._cv = threading.Condition(self._lock)
+        self._streams: Dict[int, "queue.Queue"] = {}
+        self._stop = False
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
+        self.stats = {"submitted": 0, "completed": 0, "rejected": 0}
+
+    def submit_request(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0) -> int:
+        with self._lock:
+            if len(self._pq) >= self.max_queue:
+                self.stats["rejected"] += 1
+                raise RuntimeError("queue full")
+            rid = next(self._count)
+            q: "queue.Queue" = queue.Queue()
+            self._streams[rid] = q
+            heapq.heappush(self._pq, (priority, rid, list(token_ids), params))
+            self.stats["submitted"] += 1
+            self._cv.notify()
+        return rid
+
+    def generate_stream(self, rid: int, timeout: float = 300.0) -> Iterator[int]:
+        q = self._streams[rid]
+        while True:
+            item = q.get(timeout=timeout)
+            if item is None:
+                return
+            if isinstance(item, Exception):
+                raise item
+            yield item
+
+    def _loop(self):
+        while True:
+            with self._lock:
+                while not self._stop and not self._pq and not self.engine.has_unfinished():
+                    self._cv.wait(timeout=0.1)
+                if self._stop:
+                    return
+                while self._pq:
+                    _, rid, ids, params = heapq.heappop(self._pq)
+                    q = self._streams[rid]
+
+                    def cb(seq, tok, q=q):
+                        q.put(tok)
+
+                    eng_id = self.engine.add_request(ids, params, callback=cb)
+                    self.engine.seqs[eng_id].stream_id = rid
+            done = self.engine.step()
+            for s in done:
+                q = self._streams.get(getattr(s, "stream_id", -1))
+                if q is not None:
+                    q.put(RuntimeError(s.error) if s.status == SeqStatus.FAILED else None)
+                    self.stats["completed"] += 1
+
+    def shutdown(self):
+        with self._lock:
+            self._stop = True
+            self._cv.notify()
+        self._thread.join(timeout=10)
+
+
+class AdaptiveAdmission:
+    """Chooses how many new requests to admit per step: stays within free KV
+    blocks (with headroom for decode growth) and backs off when the measured
+    step time exceeds a latency target."""
+
+    def __init__(self, target_step_s: float = 0.05, headroom_blocks: int = 64):
+        self.target = target_step_s
+        self.headroom = headroom_blocks
+        self.ewma = None
+
+    def observe(self, step_seconds: float) -> None:
+        self.ewma = step_seconds if self.ewma is None else 0.8 * self.ewma + 0.2 * step_seconds
+
+    def max_admit(self, free_blocks: int, blocks_per_request: int, running: int, max_batch: int) -> int:
+        room = max(0, free_blocks - self.headroom) // max(1, blocks_per_request)
+        n = min(room, max_batch - running)
+        if self.ewma is not None and self.ewma > self.target:
+            n = min(n, max(1, n // 2))
+        return max(0, n)

@@ -1,0 +1,15 @@
+"""Qwen3-0.6B plugin (counterpart of ``pio/models/qwen3_0_6b/plugin.py:20-178``)."""
+from ....api.engine_plugin import EnginePlugin
+
+
+class Qwen3_0_6B_Plugin(EnginePlugin):
+    preset = "qwen3-0.6b"
+    display_name = "Qwen3-0.6B"
+    family = "Qwen"
+    architecture = "Qwen3 Transformer"
+    size = "0.6B"
+    modalities = ('text',)
+
+
+def create_qwen3_0_6b_plugin():
+    return Qwen3_0_6B_Plugin()

@@ -1,0 +1,15 @@
+"""Qwen3-Coder-Next plugin (counterpart of ``pio/models/qwen3_coder_next/plugin.py``)."""
+from ....api.engine_plugin import EnginePlugin
+
+
+class Qwen3_Coder_Next_Plugin(EnginePlugin):
+    preset = "qwen3-next"
+    display_name = "Qwen3-Coder-Next"
+    family = "Qwen"
+    architecture = "Qwen3-Next hybrid gated DeltaNet + gated attention MoE"
+    size = "80B-A3B"
+    modalities = ('text',)
+
+
+def create_qwen3_coder_next_plugin():
+    return Qwen3_Coder_Next_Plugin()

@@ -320,6 +320,17 @@ void ep_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Receive step alone (fault tests: a wait for flags no peer writes must time
+// out, record kErrPeerTimeout and return, leaving the context usable).
+void ep_recv_only(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El, int64_t H,
+                  at::Tensor& row_pos, at::Tensor& offs, at::Tensor& abort) {
+  EpArgs a = make_args(peers, rank, peers.numel(), C, H, El, state);
+  c10::cuda::CUDAGuard guard(peers.device());
+  launch_k(ep_recv_kernel, 1, 1024, 0, at::cuda::getCurrentCUDAStream(), a, row_pos.data_ptr<int>(),
+           offs.data_ptr<int>(), abort.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Combine half: y [N*C, H] expert outputs in xs order -> out [T, H].
 void ep_combine(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                 const at::Tensor& row_pos, const at::Tensor& y, const at::Tensor& map, const at::Tensor& wts,

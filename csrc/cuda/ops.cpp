@@ -33,6 +33,8 @@ void ep_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64
 void ep_combine(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                 const at::Tensor& row_pos, const at::Tensor& y, const at::Tensor& map, const at::Tensor& wts,
                 const c10::optional<at::Tensor>& residual, at::Tensor& out);
+void ep_recv_only(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El, int64_t H,
+                  at::Tensor& row_pos, at::Tensor& offs, at::Tensor& abort);
 std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
 int64_t ipc_open(const std::string& handle);
 void ipc_close(int64_t ptr);
@@ -59,6 +61,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_buffer_bytes", &mb::ep_buffer_bytes);
   m.def("ep_dispatch", &mb::ep_dispatch);
   m.def("ep_combine", &mb::ep_combine);
+  m.def("ep_recv_only", &mb::ep_recv_only);
   m.def("ipc_alloc", [](int64_t b) {
     auto r = mb::ipc_alloc(b);
     return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));

@@ -75,6 +75,9 @@ class LLMEngine:
         self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens)
         self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
                                   use_graphs=use_graphs and backend == "native", device=self.device)
+        from .sampler import Sampler
+
+        self.runner.sampler = Sampler()
         self.seqs: Dict[int, Sequence] = {}
         self.last_step: Dict[str, float] = {}
 

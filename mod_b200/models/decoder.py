@@ -41,6 +41,7 @@ class DecoderLM:
         self.inv_freq = R.inv_freq(cfg.rotary_dim, cfg.rope_theta, device=dev)
         self.delta = {i: DeltaNetLayer(cfg, L.delta) for i, L in enumerate(weights.layers) if L.delta is not None}
         self.device = dev
+        self.layer_source = None  # optional i -> LayerWeights (weight streaming)
 
     # ------------------------------------------------------------------ blocks
     def _attention(self, i, L, x, fb: ForwardBatch, kv: KVCache):
@@ -113,6 +114,8 @@ class DecoderLM:
         hidden = fb.inputs_embeds if fb.inputs_embeds is not None else be.embed(fb.input_ids, w.embed)
         residual = None
         for i, L in enumerate(w.layers):
+            if self.layer_source is not None:
+                L = self.layer_source(i)
             if residual is None:
                 residual = hidden.clone()
                 x = be.rmsnorm(hidden, L.in_norm, eps)

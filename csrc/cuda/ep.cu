@@ -105,7 +105,11 @@ __global__ void ep_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x
   const uint32_t epoch = *a.epoch + 1;
   const int warps = blockDim.x / 32, warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   for (int pair = blockIdx.x * warps + warp; pair < TK; pair += gridDim.x * warps) {
-    const int e = ids[pair];
+    int e = ids[pair];
+    if (e < 0 || e >= a.El * a.N) {  // defensive: an invalid id must never become an address
+      set_status(a.status, kErrBounds);
+      e = 0;
+    }
     const int dst = e / a.El;
     int slot = 0;
     if (lane == 0) {

@@ -15,6 +15,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "common.cuh"
+#include "status.h"
 #include "launch.cuh"
 
 namespace mb {
@@ -22,7 +23,8 @@ namespace mb {
 // One warp per token.  E <= 1024, K <= 16.
 template <int EPL>  // experts per lane
 __global__ void moe_topk_kernel(const __nv_bfloat16* __restrict__ logits, int T, int E, int K, bool renorm,
-                                int* __restrict__ ids, float* __restrict__ wts, int* __restrict__ counts) {
+                                int* __restrict__ ids, float* __restrict__ wts, int* __restrict__ counts,
+                                int* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -68,6 +70,12 @@ __global__ void moe_topk_kernel(const __nv_bfloat16* __restrict__ logits, int T,
       if (i * 32 + lane == bi) v[i] = -2.f;
   }
   if (lane < K) {
+    // non-finite logits select nothing: never index with an invalid id
+    if (my_id < 0 || my_id >= E) {
+      set_status(status, kErrBounds);
+      my_id = 0;
+      my_w = 0.f;
+    }
     ids[(size_t)t * K + lane] = my_id;
     wts[(size_t)t * K + lane] = renorm ? my_w / picked_sum : my_w;
     atomicAdd(&counts[my_id], 1);
@@ -107,7 +115,7 @@ __global__ void moe_permute_kernel(const __nv_bfloat16* __restrict__ x, int T, i
   if (pair >= T * K) return;
   int p = 0;
   if (lane == 0) {
-    const int e = ids[pair];
+    const int e = ids[pair];  // always in [0, E): moe_topk clamps invalid selections
     p = offs[e] + atomicAdd(&cursor[e], 1);
     pos[pair] = p;
   }
@@ -167,7 +175,7 @@ void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids
     const int epl = (E + 31) / 32;
 #define MB_TOPK(N) \
   launch_k(moe_topk_kernel<N>, grid, block, 0, st, pl, T, E, (int)K, renorm, ids.data_ptr<int>(), wts.data_ptr<float>(), \
-                                             counts.data_ptr<int>())
+                                             counts.data_ptr<int>(), status_ptr(logits.device().index()))
     if (epl <= 1) MB_TOPK(1);
     else if (epl <= 2) MB_TOPK(2);
     else if (epl <= 4) MB_TOPK(4);

@@ -20,6 +20,9 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                     const c10::optional<at::Tensor>& workspace, double scale);
 bool attn_decode_tc_supported(int64_t D, int64_t G);
+void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                     const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,
+                     at::Tensor& out, int64_t max_q_len, double scale);
 void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids, at::Tensor& wts,
                at::Tensor& counts, at::Tensor& offs, at::Tensor& cursor);
 void moe_permute(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& offs, at::Tensor& cursor,
@@ -55,6 +58,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode", &mb::attn_decode);
   m.def("attn_decode_tc", &mb::attn_decode_tc);
   m.def("attn_decode_tc_supported", &mb::attn_decode_tc_supported);
+  m.def("attn_prefill_tc", &mb::attn_prefill_tc);
   m.def("moe_route", &mb::moe_route);
   m.def("moe_permute", &mb::moe_permute);
   m.def("moe_combine", &mb::moe_combine);

@@ -136,8 +136,19 @@ class NativeBackend:
         return self.N.attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws)
 
     def attn_prefill(self, q, k, v):
-        # causal prefill attention; replaced by the tcgen05 flash kernel when built
         return R.attn_prefill(q, k, v)
+
+    def attn_prefill_paged(self, q, k_cache, v_cache, fb):
+        """All sequences of a prefill step in one tcgen05 flash-attention launch
+        (head_dim 128); None when the shape is not covered."""
+        if q.shape[-1] != 128:
+            return None
+        ql = fb.query_lens
+        cu = [0]
+        for n in ql:
+            cu.append(cu[-1] + n)
+        cu_q = torch.tensor(cu, dtype=torch.int32).to(q.device, non_blocking=True)
+        return self.N.attn_prefill_tc(q, k_cache, v_cache, fb.block_tables, cu_q, fb.ctx_lens, max(ql))
 
     def moe(self, x, mo, top_k, renorm, inter, residual=None):
         N = self.N

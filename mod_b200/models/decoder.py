@@ -57,6 +57,8 @@ class DecoderLM:
             o = be.attn_paged(q, kc, vc, fb)
         elif fb.is_decode:
             o = be.attn_decode(q, kc, vc, fb.block_tables, fb.ctx_lens, fb.attn_splits)
+        elif hasattr(be, "attn_prefill_paged") and (o := be.attn_prefill_paged(q, kc, vc, fb)) is not None:
+            pass
         else:
             o = torch.empty_like(q)
             start = 0

@@ -75,6 +75,19 @@ def attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits
     return out
 
 
+def attn_prefill_tc(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, max_q_len: int, out=None,
+                    scale: Optional[float] = None):
+    """Causal tcgen05 flash prefill over the paged cache.  q [T, Hq, D] (D = 128)."""
+    T, Hq, D = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    _C().attn_prefill_tc(q.view(T, Hq * D), k_cache, v_cache, block_tables, cu_q, ctx_lens, out.view(T, Hq * D),
+                         max_q_len, scale)
+    return out
+
+
 def attn_decode_tc_supported(D: int, G: int) -> bool:
     return bool(_C().attn_decode_tc_supported(D, G))
 

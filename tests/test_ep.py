@@ -53,3 +53,31 @@ def test_ep_multi_gpu(cuda, impl):
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_ep_worker.py"), impl]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def _pipe_worker(rank, world, port):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from mod_b200.parallel.pipeline import PipelineExecutor, PipelineStage, split_layers
+
+    torch.manual_seed(0)
+    ws = [torch.randn(16, 16) * 0.3 for _ in range(6)]
+    layers = [(lambda x, w=w: torch.tanh(x @ w)) for w in ws]
+    stages = [PipelineStage(s, r) for r, s in enumerate(split_layers(layers, world))]
+    x = torch.randn(8, 16)
+    out = PipelineExecutor(stages, micro_batches=4).forward(x if rank == 0 else None, shape=(8, 16))
+    if rank == world - 1:
+        ref = x
+        for f in layers:
+            ref = f(ref)
+        assert torch.allclose(out, ref, atol=1e-6)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_pipeline_gloo_three_stages():
+    mp.spawn(_pipe_worker, args=(3, _port()), nprocs=3, join=True)

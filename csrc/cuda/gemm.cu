@@ -257,3 +257,74 @@ void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& 
 }
 
 }  // namespace mb
+
+namespace mb {
+
+// Tensor-parallel GEMM.  gather: activations are the concatenation of every
+// rank's shard (read in place from the peers with TMA); scatter: the output
+// partial rows go to their owning ranks' reduce-scatter slots.
+//   x     : local activations [T, K] (scatter) - unused when gather
+//   w     : weight shard [N_out(*2 for swiglu), K]
+//   out   : local output [T, N_out] (not scatter)
+void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool gather, bool scatter, bool swiglu,
+             int64_t T, const at::Tensor& maps, int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks,
+             int64_t peer_rows, int64_t sub, const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off) {
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous());
+  const int64_t K = w.size(1);
+  const int64_t n_out = swiglu ? w.size(0) / 2 : w.size(0);
+  TORCH_CHECK(T == peer_rows * nranks, "tp_gemm: T must equal peer_rows * ranks");
+  c10::cuda::CUDAGuard guard(w.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  GemmArgs a{};
+  a.K = (int)K;
+  a.groups = 1;
+  a.splits = 1;
+  a.ldc = (int)n_out;
+  a.out_rows = (int)T;
+  a.status = status_ptr(w.device().index());
+  a.tp.peer_maps = gather ? reinterpret_cast<const CUtensorMap*>(maps.data_ptr()) : nullptr;
+  a.tp.ag_flags = reinterpret_cast<const uint32_t*>(ag_flags);
+  int* s = state.data_ptr<int>();
+  a.tp.epoch = reinterpret_cast<uint32_t*>(s);
+  a.tp.done = s + 4;
+  a.tp.peer_rows = (int)peer_rows;
+  a.tp.sub = (int)sub;
+  a.tp.nranks = (int)nranks;
+  a.tp.rank = (int)rank;
+  a.tp.rs_peers = rs_peers.defined() && rs_peers.numel() ? reinterpret_cast<const uint64_t*>(rs_peers.data_ptr<int64_t>()) : nullptr;
+  a.tp.rs_off = rs_off;
+  a.tp.rs_flag_off = rs_flag_off;
+  a.mode = scatter ? kEpiScatterRS : (swiglu ? kEpiSwiGLU : kEpiStore);
+  a.out = scatter ? nullptr : out.data_ptr();
+  TORCH_CHECK(!(scatter && swiglu), "tp_gemm: scatter with swiglu is not supported");
+  TORCH_CHECK(!gather || !scatter, "tp_gemm: a boundary either gathers its input or scatters its output");
+  const bool swap = T <= 256 && n_out % 128 == 0;
+  if (swap) {
+    const int bn = pick_bn(T, swiglu);
+    TORCH_CHECK(!gather || (bn % sub == 0 && peer_rows % sub == 0), "tp_gemm: sub-load rows must tile BN");
+    auto ta = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, 128);
+    auto tb = gather ? ta : make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
+    a.a_rows = (int)w.size(0);
+    a.a_up_offset = swiglu ? (int)n_out : 0;
+    a.b_rows = (int)T;
+    a.swap = 1;
+    dispatch(bn, swiglu, ta, tb, a, dim3((unsigned)(n_out / 128), 1, 1), st);
+  } else {
+    TORCH_CHECK(!swiglu || true, "");
+    const int bn = n_out >= 256 ? 256 : pick_bn(n_out, false);
+    TORCH_CHECK(!gather || (128 % sub == 0 && peer_rows % sub == 0), "tp_gemm: sub-load rows must tile 128");
+    auto tb = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, swiglu ? 128 : bn);
+    auto ta = gather ? tb : make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), 128);
+    a.a_rows = (int)((T + 127) / 128 * 128);
+    a.b_rows = (int)n_out;
+    a.swap = 0;
+    TORCH_CHECK(!swiglu, "tp_gemm: SwiGLU needs the swap orientation (T <= 256); use gather + separate swiglu");
+    const int m_tiles = (int)((T + 127) / 128);
+    const int n_tiles = (int)((n_out + bn - 1) / bn);
+    int ny = n_tiles;
+    while ((int64_t)m_tiles * ny > num_sms() * 2 && ny > 1) ny = (ny + 1) / 2;
+    dispatch(bn, false, ta, tb, a, dim3(m_tiles, ny, 1), st);
+  }
+}
+
+}  // namespace mb

@@ -27,6 +27,24 @@ enum EpiMode : int {
   kEpiStore = 0,      // bf16 store of D (optionally + bf16 residual)
   kEpiSwiGLU = 1,     // dual accumulator: silu(D_gate) * D_up
   kEpiPartialF32 = 2, // fp32 split-K partial to a workspace
+  kEpiScatterRS = 3,  // tensor parallel: bf16 partial rows stored into the owning rank's slot (P2P)
+};
+
+// Tensor-parallel operands of a GEMM: activations gathered from the peers'
+// shard buffers (all-gather fused into the operand loads) and/or a
+// reduce-scatter epilogue.  Peer memory is only ever read by plain
+// (non-multicast) TMA loads and written by ordinary stores.
+struct TpArgs {
+  const CUtensorMap* peer_maps;   // [N] maps over each rank's activation shard, box = 64 x sub rows
+  const uint32_t* ag_flags;       // [N] local: ag_flags[p] >= *epoch once rank p's shard is ready
+  uint32_t* epoch;                // local boundary counter
+  int peer_rows;                  // rows per shard (tokens per rank)
+  int sub;                        // rows per TMA sub-load
+  int nranks, rank;
+  const uint64_t* rs_peers;       // [N] base of every rank's exchange buffer
+  int64_t rs_off;                 // byte offset of the partial slots [N][peer_rows][ldc]
+  int64_t rs_flag_off;            // byte offset of the RS flags [N]
+  int* done;                      // local CTA-completion counter
 };
 
 struct GemmArgs {
@@ -44,7 +62,27 @@ struct GemmArgs {
   int ldc;
   int out_rows;          // tokens (rows of out) for the split-K workspace stride
   int* status;
+  TpArgs tp;             // tp.peer_maps == nullptr: not tensor parallel
 };
+
+// Loads `rows` activation rows starting at gathered row `row0`, k-block kx,
+// either from the local map or from the peers' shard buffers.
+__device__ __forceinline__ void load_act(const GemmArgs& a, const CUtensorMap* local, void* dst, uint64_t* bar, int kx,
+                                         int row0, int rows) {
+  if (!a.tp.peer_maps) {
+    tma_load_2d(dst, local, bar, kx, row0);
+    return;
+  }
+  for (int r = 0; r < rows; r += a.tp.sub) {
+    int p = (row0 + r) / a.tp.peer_rows;
+    int lr = (row0 + r) - p * a.tp.peer_rows;
+    if (p >= a.tp.nranks) {   // past the gathered rows: out-of-range coordinate -> TMA zero fill
+      p = a.tp.nranks - 1;
+      lr = a.tp.peer_rows;
+    }
+    tma_load_2d(reinterpret_cast<uint8_t*>(dst) + r * 128, &a.tp.peer_maps[p], bar, kx, lr);
+  }
+}
 
 template <int BN, int STAGES, bool DUAL>
 struct GemmSmem {
@@ -134,7 +172,7 @@ __global__ void __launch_bounds__(192, 1)
       // ------------------------------------------------ TMA producer
       const bool leader = elect_one_sync();
       // weight tiles of the first stages, issued before the dependency wait
-      const int pre = dense ? min(STAGES, kbs) : 0;
+      const int pre = (dense && args.swap) ? min(STAGES, kbs) : 0;
       if (leader) {
         for (int s = 0; s < pre; ++s) {
           uint8_t* st = smem + s * L::kStageBytes;
@@ -147,6 +185,21 @@ __global__ void __launch_bounds__(192, 1)
         pdl_wait();
         pdl_trigger();
       }
+      if (args.tp.peer_maps && leader) {  // every peer's shard must be published for this boundary
+        const uint32_t want = *args.tp.epoch;
+        for (int p = 0; p < args.tp.nranks; ++p) {
+          const uint64_t t0 = globaltimer_ns();
+          while (true) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(args.tp.ag_flags + p) : "memory");
+            if ((int32_t)(v - want) >= 0) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              set_status(args.status, kErrPeerTimeout);
+              break;
+            }
+          }
+        }
+      }
       if (leader) {
         int it = 0;
         bool ok = true;
@@ -156,15 +209,20 @@ __global__ void __launch_bounds__(192, 1)
             const int s = it % STAGES;
             uint8_t* st = smem + s * L::kStageBytes;
             if (it < pre) {  // weights already in flight: add the activation tile
-              tma_load_2d(st + L::kABytes * (DUAL ? 2 : 1), &tmB, &full[s], kb * 64, b0 + nt * BN);
+              load_act(args, &tmB, st + L::kABytes * (DUAL ? 2 : 1), &full[s], kb * 64, b0 + nt * BN, BN);
               continue;
             }
             const uint32_t ph = (it / STAGES) & 1;
             if (!mbar_wait(&empty[s], ph ^ 1, args.status)) { ok = false; break; }
             mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-            tma_load_2d(st, &tmA, &full[s], kb * 64, a_row0);
-            if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], kb * 64, a_row0 + args.a_up_offset);
-            tma_load_2d(st + L::kABytes * (DUAL ? 2 : 1), &tmB, &full[s], kb * 64, b0 + nt * BN);
+            if (args.swap) {
+              tma_load_2d(st, &tmA, &full[s], kb * 64, a_row0);
+              if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], kb * 64, a_row0 + args.a_up_offset);
+              load_act(args, &tmB, st + L::kABytes * (DUAL ? 2 : 1), &full[s], kb * 64, b0 + nt * BN, BN);
+            } else {  // normal orientation: activations are the 128-row A operand
+              load_act(args, &tmA, st, &full[s], kb * 64, a_row0, 128);
+              tma_load_2d(st + L::kABytes, &tmB, &full[s], kb * 64, b0 + nt * BN);
+            }
           }
         }
       }
@@ -229,6 +287,10 @@ __global__ void __launch_bounds__(192, 1)
                 const size_t o = (size_t)(b0 + j) * args.ldc + arow;
                 if (args.mode == kEpiPartialF32) {
                   reinterpret_cast<float*>(args.out)[(size_t)split * args.out_rows * args.ldc + o] = v[q];
+                } else if (args.mode == kEpiScatterRS) {
+                  const int tok = b0 + j, d = tok / args.tp.peer_rows, jl = tok - d * args.tp.peer_rows;
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.tp.rs_peers[d] + args.tp.rs_off);
+                  dst[((size_t)args.tp.rank * args.tp.peer_rows + jl) * args.ldc + arow] = __float2bfloat16(v[q]);
                 } else {
                   float r = args.residual ? __bfloat162float(args.residual[o]) : 0.f;
                   reinterpret_cast<__nv_bfloat16*>(args.out)[o] = __float2bfloat16(v[q] + r);
@@ -238,7 +300,20 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             // out[arow, j]: 16 consecutive columns per thread.
             const int grow = g * args.a_rows + arow;
-            if (grow < args.out_rows) {
+            if (grow < args.out_rows && args.mode == kEpiScatterRS) {
+              const int d = grow / args.tp.peer_rows, jl = grow - d * args.tp.peer_rows;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.tp.rs_peers[d] + args.tp.rs_off) +
+                                   ((size_t)args.tp.rank * args.tp.peer_rows + jl) * args.ldc + jbase;
+              __align__(16) __nv_bfloat16 h[16];
+#pragma unroll
+              for (int q = 0; q < 16; ++q) h[q] = __float2bfloat16(v[q]);
+              if (jbase + 16 <= cnt) {
+                reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<uint4*>(h)[0];
+                reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<uint4*>(h)[1];
+              } else {
+                for (int q = 0; q < 16 && jbase + q < cnt; ++q) dst[q] = h[q];
+              }
+            } else if (grow < args.out_rows) {
               const size_t o = (size_t)grow * args.ldc + jbase;
               if (args.mode == kEpiPartialF32) {
                 float* dst = reinterpret_cast<float*>(args.out) + (size_t)split * args.out_rows * args.ldc + o;
@@ -276,6 +351,24 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (args.mode == kEpiScatterRS) {
+    // last CTA: every partial of this rank is stored -> release the owners' flags
+    __shared__ int last;
+    __threadfence_system();
+    __syncthreads();
+    const int nct = gridDim.x * gridDim.y * gridDim.z;
+    if (threadIdx.x == 0) last = atomicAdd(args.tp.done, 1) == nct - 1;
+    __syncthreads();
+    if (last) {
+      __threadfence_system();
+      const uint32_t e = *args.tp.epoch;
+      for (int d = threadIdx.x; d < args.tp.nranks; d += blockDim.x) {
+        uint32_t* f = reinterpret_cast<uint32_t*>(args.tp.rs_peers[d] + args.tp.rs_flag_off) + args.tp.rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+      }
+      if (threadIdx.x == 0) *args.tp.done = 0;
+    }
   }
 }
 

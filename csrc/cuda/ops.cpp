@@ -38,6 +38,16 @@ void ep_combine(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_
                 const c10::optional<at::Tensor>& residual, at::Tensor& out);
 void ep_recv_only(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El, int64_t H,
                   at::Tensor& row_pos, at::Tensor& offs, at::Tensor& abort);
+void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool gather, bool scatter, bool swiglu,
+             int64_t T, const at::Tensor& maps, int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks,
+             int64_t peer_rows, int64_t sub, const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off);
+at::Tensor tp_make_peer_maps(const std::vector<int64_t>& ag_addrs, int64_t rows, int64_t H, int64_t sub);
+void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_t rows, int64_t H, int64_t ag_off,
+               int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off, at::Tensor& state,
+               const c10::optional<at::Tensor>& x_add, at::Tensor& residual, const at::Tensor& w, double eps,
+               const c10::optional<at::Tensor>& local_out);
+void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, int64_t ag_off, int64_t ag_flag_off,
+                    at::Tensor& state, const at::Tensor& idx, at::Tensor& out);
 std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
 int64_t ipc_open(const std::string& handle);
 void ipc_close(int64_t ptr);
@@ -66,6 +76,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &mb::ep_dispatch);
   m.def("ep_combine", &mb::ep_combine);
   m.def("ep_recv_only", &mb::ep_recv_only);
+  m.def("tp_gemm", &mb::tp_gemm);
+  m.def("tp_make_peer_maps", &mb::tp_make_peer_maps);
+  m.def("tp_reduce", &mb::tp_reduce);
+  m.def("tp_gather_rows", &mb::tp_gather_rows);
   m.def("ipc_alloc", [](int64_t b) {
     auto r = mb::ipc_alloc(b);
     return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));

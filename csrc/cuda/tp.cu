@@ -1,0 +1,217 @@
+// Tensor-parallel plumbing over NVLink peer memory (no NCCL on these paths).
+//
+// Every rank owns an exchange buffer (CUDA IPC, mapped into every peer):
+//   ag    [peer_rows, H] bf16   this rank's normed activation shard (read by peers' GEMMs)
+//   rs    [N, peer_rows, H]     reduce-scatter slots: partial rows from each source rank
+//   ag_flags [N] u32            ag_flags[p] = boundary epoch once rank p's shard is published
+//   rs_flags [N] u32            rs_flags[p] = epoch once rank p's partials for this rank are stored
+// Sequence parallelism: the residual stream is split by tokens, rank r owns
+// rows [r*peer_rows, (r+1)*peer_rows).  A layer boundary is
+//   gather-GEMM (gemm.cu, activations loaded from the peers' ag buffers)
+//   -> local attention / MLP math
+//   -> scatter-GEMM (partials P2P-stored into the owners' rs slots)
+//   -> tp_reduce (owner: wait flags, sum partials in rank order + residual,
+//      RMSNorm, write its ag shard, advance the epoch, release ag flags).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "status.h"
+
+namespace mb {
+
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows, int64_t cols, int64_t ld_bytes,
+                         int box_cols, int box_rows, CUtensorMapSwizzle sw);
+
+// One 2-D map per rank over its ag shard, box 64 x sub rows, as a device byte tensor.
+at::Tensor tp_make_peer_maps(const std::vector<int64_t>& ag_addrs, int64_t rows, int64_t H, int64_t sub) {
+  std::vector<CUtensorMap> maps;
+  for (auto a : ag_addrs)
+    maps.push_back(make_tmap_2d(reinterpret_cast<void*>(a), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rows, H, H * 2, 64,
+                                (int)sub, CU_TENSOR_MAP_SWIZZLE_128B));
+  auto host = at::empty({(int64_t)(maps.size() * sizeof(CUtensorMap))}, at::kByte);
+  std::memcpy(host.data_ptr(), maps.data(), maps.size() * sizeof(CUtensorMap));
+  return host.to(at::Device(at::kCUDA, c10::cuda::current_device()));
+}
+
+__device__ __forceinline__ uint32_t ld_acq(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// CTA per local row.  nsrc == 0: publish only (no partials to wait for).
+template <int CH>  // one warp per row: H / 256 chunks of 8 columns per lane
+__global__ void tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int nsrc, int rows,
+                                 int64_t ag_off, int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off,
+                                 uint32_t* epoch, int* done, const __nv_bfloat16* __restrict__ x_add,
+                                 __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
+                                 __nv_bfloat16* __restrict__ local_out, int* status) {
+  constexpr int H = CH * 256;
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t e = *epoch;
+  const int t = blockIdx.x;
+  const uint64_t self = peers[rank];
+  __shared__ float red[8];
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  if (nsrc > 0) {
+    const uint32_t* rf = reinterpret_cast<const uint32_t*>(self + rs_flag_off);
+    for (int s = threadIdx.x; s < nranks; s += blockDim.x) {
+      const uint64_t t0 = globaltimer_ns();
+      while ((int32_t)(ld_acq(rf + s) - e) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_status(status, kErrPeerTimeout);
+          ok_all = 0;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    __threadfence();
+  }
+  // each thread: CH chunks of 8 columns (blockDim = 32)
+  float v[CH][8];
+  float ss = 0.f;
+  const __nv_bfloat16* slots = reinterpret_cast<const __nv_bfloat16*>(self + rs_off);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = c * 256 + threadIdx.x * 8;
+    float acc[8];
+    uint4 rr = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rr)[q]);
+    if (x_add) {
+      uint4 xa = *reinterpret_cast<const uint4*>(x_add + (size_t)t * H + col);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&xa)[q]);
+    }
+    if (ok_all) {
+      for (int s = 0; s < nsrc; ++s) {  // fixed rank order: deterministic
+        uint4 pr = __ldcg(reinterpret_cast<const uint4*>(slots + ((size_t)s * rows + t) * H + col));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&pr)[q]);
+      }
+    }
+    __align__(16) __nv_bfloat16 hb[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      hb[q] = __float2bfloat16(acc[q]);
+      v[c][q] = __bfloat162float(hb[q]);
+      ss += v[c][q] * v[c][q];
+    }
+    *reinterpret_cast<uint4*>(residual + (size_t)t * H + col) = *reinterpret_cast<uint4*>(hb);
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / H + eps);
+  __nv_bfloat16* ag = reinterpret_cast<__nv_bfloat16*>(self + ag_off);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = c * 256 + threadIdx.x * 8;
+    uint4 wr = *reinterpret_cast<const uint4*>(w + col);
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16(v[c][q] * inv * __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&wr)[q]));
+    *reinterpret_cast<uint4*>(ag + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
+    if (local_out) *reinterpret_cast<uint4*>(local_out + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
+  }
+  // last CTA: advance the epoch and publish this rank's shard to every peer
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  const uint32_t ne = e + 1;
+  for (int p = threadIdx.x; p < nranks; p += blockDim.x) {
+    uint32_t* f = reinterpret_cast<uint32_t*>(peers[p] + ag_flag_off) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ne) : "memory");
+  }
+  if (threadIdx.x == 0) {
+    *epoch = ne;
+    *done = 0;
+  }
+}
+
+void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_t rows, int64_t H, int64_t ag_off,
+               int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off, at::Tensor& state,
+               const c10::optional<at::Tensor>& x_add, at::Tensor& residual, const at::Tensor& w, double eps,
+               const c10::optional<at::Tensor>& local_out) {
+  TORCH_CHECK(H % 256 == 0 && H / 256 <= 32, "tp_reduce: hidden size must be a multiple of 256 (<= 8192)");
+  TORCH_CHECK(residual.is_contiguous() && residual.size(0) == rows && residual.size(1) == H);
+  const int N = (int)peers.numel();
+  c10::cuda::CUDAGuard guard(residual.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  int* s = state.data_ptr<int>();
+  auto bf = [](const c10::optional<at::Tensor>& t) -> __nv_bfloat16* {
+    return (t && t->defined()) ? reinterpret_cast<__nv_bfloat16*>(t->data_ptr()) : nullptr;
+  };
+  const uint64_t* pp = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  auto* res = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  auto* ww = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  const int grid = (int)std::max<int64_t>(1, rows);
+#define MB_TPR(C) \
+  case C: launch_k(tp_reduce_kernel<C>, grid, 32, 0, st, pp, (int)rank, N, with_partials ? N : 0, (int)rows, ag_off, rs_off, \
+                   ag_flag_off, rs_flag_off, reinterpret_cast<uint32_t*>(s), s + 5, (const __nv_bfloat16*)bf(x_add), res, ww, \
+                   (float)eps, bf(local_out), status_ptr(residual.device().index())); break;
+  switch (H / 256) {
+    MB_TPR(4) MB_TPR(8) MB_TPR(16) MB_TPR(1) MB_TPR(2) MB_TPR(32)
+    default: TORCH_CHECK(false, "tp_reduce: unsupported hidden size");
+  }
+#undef MB_TPR
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Bounded wait, one warp: every rank's shard of the current epoch is published
+// (flags live in this rank's own buffer, written by the peers).
+__global__ void tp_wait_flags_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int64_t ag_flag_off,
+                                     const uint32_t* epoch, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t e = *epoch;
+  const uint32_t* f = reinterpret_cast<const uint32_t*>(peers[rank] + ag_flag_off);
+  for (int p = threadIdx.x; p < nranks; p += blockDim.x) {
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acq(f + p) - e) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_status(status, kErrPeerTimeout);
+        break;
+      }
+    }
+  }
+}
+
+// out[i] = row idx[i] of the gathered (published) shards, read over NVLink.
+__global__ void tp_gather_rows_kernel(const uint64_t* __restrict__ peers, int peer_rows, int64_t ag_off,
+                                      const int64_t* __restrict__ idx, int H, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t g = idx[blockIdx.x];
+  const int p = (int)(g / peer_rows), r = (int)(g % peer_rows);
+  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(peers[p] + ag_off) + (size_t)r * H;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+    *reinterpret_cast<uint4*>(out + (size_t)blockIdx.x * H + c) = __ldcg(reinterpret_cast<const uint4*>(src + c));
+}
+
+void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, int64_t ag_off, int64_t ag_flag_off,
+                    at::Tensor& state, const at::Tensor& idx, at::Tensor& out) {
+  const int B = (int)idx.numel(), H = (int)out.size(1);
+  if (B == 0) return;
+  c10::cuda::CUDAGuard guard(out.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const uint64_t* pp = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  launch_k(tp_wait_flags_kernel, 1, 32, 0, st, pp, (int)rank, (int)peers.numel(), ag_flag_off,
+           reinterpret_cast<const uint32_t*>(state.data_ptr<int>()), status_ptr(out.device().index()));
+  launch_k(tp_gather_rows_kernel, B, 128, 0, st, pp, (int)peer_rows, ag_off, (const int64_t*)idx.data_ptr<int64_t>(), H,
+           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mb

@@ -36,7 +36,7 @@ class LLMEngine:
                  device: Union[str, torch.device] = "cuda", max_batch: int = 128, max_model_len: int = 4096,
                  num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
                  max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
-                 expert_parallel: Optional[bool] = None):
+                 expert_parallel: Optional[bool] = None, tensor_parallel: bool = False):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
@@ -52,6 +52,20 @@ class LLMEngine:
             expert_parallel = world > 1 and cfg.is_moe
         self.expert_parallel = expert_parallel
         self.backend = make_backend(backend)
+        self.tensor_parallel = tensor_parallel and world > 1
+        if self.tensor_parallel and model is None:
+            from ..models.tp_decoder import TPDecoderLM, shard_weights
+            from ..parallel.tp import FusedTP, NcclTP
+
+            if weights is None:
+                weights = random_weights(cfg, device=self.device, seed=seed)
+            shard = shard_weights(cfg, weights, rank, world)
+            weights = None
+            mt = max(max_batch, max_prefill_tokens)
+            comm = FusedTP(cfg.hidden_size, mt) if backend == "native" else NcclTP(cfg.hidden_size, mt)
+            model = TPDecoderLM(cfg, shard, self.backend, comm, world)
+            kv_heads = model.Hkv
+            expert_parallel = False
         moe_impl = None
         if expert_parallel:
             El = cfg.num_experts // world

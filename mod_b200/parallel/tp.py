@@ -1,0 +1,161 @@
+"""Tensor parallelism with sequence-parallel residual stream.
+
+Rank r owns token rows [r*pr, (r+1)*pr) of the residual stream (pr = padded
+tokens / ranks).  Each layer boundary is
+
+    all-gather(normed shard) -> column-parallel GEMM      (QKV, gate/up)
+    row-parallel GEMM -> reduce-scatter (+ residual, + next RMSNorm)   (o_proj, down)
+
+:class:`FusedTP` does both boundaries with the kernels in ``csrc/cuda/gemm.cu``
+and ``csrc/cuda/tp.cu``: the GEMM reads the other ranks' shards in place over
+NVLink (TMA loads from IPC-mapped buffers, no multicast) and scatters its
+partial rows into the owners' slots with peer stores; a fused reduce kernel
+sums them in rank order, adds the residual, applies the RMSNorm and publishes
+the next shard.  :class:`NcclTP` is the baseline: NCCL all-gather /
+reduce-scatter around cuBLAS GEMMs.
+
+The reference has tensor-parallel settings only as configuration strings
+(``pio/models/glm_4_7_flash/config.py:108-111``).
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops import reference as R
+
+
+def padded_tokens(T: int, world: int) -> int:
+    """Token count padded so every rank gets an equal, tileable shard."""
+    if T <= 256:
+        t = 8 * world
+        while t < T:
+            t *= 2
+        if t <= 256:
+            return t
+    step = 128 * world
+    return -(-T // step) * step
+
+
+class FusedTP:
+    def __init__(self, hidden: int, max_tokens: int, group=None):
+        from ..ops import load_extension
+        from .ep import ExchangeBuffer
+
+        self.C = load_extension()
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.H = hidden
+        self.cap = padded_tokens(max_tokens, self.world) // self.world  # rows per rank
+        al = lambda x: (x + 255) // 256 * 256  # noqa: E731
+        N, cap, H = self.world, self.cap, hidden
+        self.ag_off = 0
+        self.rs_off = al(cap * H * 2)
+        self.ag_flag_off = al(self.rs_off + N * cap * H * 2)
+        self.rs_flag_off = al(self.ag_flag_off + N * 4)
+        total = al(self.rs_flag_off + N * 4)
+        self.buf = ExchangeBuffer(total, group)
+        self.peers = self.buf.peers
+        addrs = self.peers.tolist()
+        self.ag_addrs = [a + self.ag_off for a in addrs]
+        self.ag_flags_addr = addrs[self.rank] + self.ag_flag_off
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.state = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.maps: Dict[int, torch.Tensor] = {}
+        self.empty = torch.empty(0, dtype=torch.int64, device=dev)
+
+    def _maps(self, sub: int) -> torch.Tensor:
+        if sub not in self.maps:
+            self.maps[sub] = self.C.tp_make_peer_maps(self.ag_addrs, self.cap, self.H, sub)
+        return self.maps[sub]
+
+    @staticmethod
+    def _sub(T: int, pr: int, n_out: int) -> int:
+        if T <= 256 and n_out % 128 == 0:
+            bn = 16
+            while bn < T:
+                bn *= 2
+            return min(pr, bn)
+        return min(pr, 128)
+
+    # -------------------------------------------------------------- boundaries
+    def publish(self, residual: torch.Tensor, norm_w: torch.Tensor, eps: float, partials: bool,
+                x_add: Optional[torch.Tensor] = None, local_out: Optional[torch.Tensor] = None) -> None:
+        """residual [pr, H] += x_add (+ sum of partials); shard = rmsnorm(residual) -> published."""
+        self.C.tp_reduce(self.peers, self.rank, partials, residual.shape[0], self.H, self.ag_off, self.rs_off,
+                         self.ag_flag_off, self.rs_flag_off, self.state, x_add, residual, norm_w, eps, local_out)
+
+    def ag_gemm(self, w: torch.Tensor, T: int, swiglu: bool = False) -> torch.Tensor:
+        """[T, N_out] = gather(published shards) @ w^T (w: [N_out, H] or [2*N_out, H] for SwiGLU)."""
+        pr = T // self.world
+        n_out = w.shape[0] // 2 if swiglu else w.shape[0]
+        fused_swiglu = swiglu and T <= 256 and n_out % 128 == 0
+        cols = n_out if fused_swiglu else w.shape[0]
+        out = torch.empty(T, cols, dtype=torch.bfloat16, device=w.device)
+        sub = self._sub(T, pr, cols)
+        self.C.tp_gemm(self.empty, w, out, True, False, fused_swiglu, T, self._maps(sub), self.ag_flags_addr,
+                       self.state, self.rank, self.world, pr, sub, self.peers, self.rs_off, self.rs_flag_off)
+        if swiglu and not fused_swiglu:
+            from ..ops import native
+
+            out = native.swiglu(out)
+        return out
+
+    def gemm_rs(self, x: torch.Tensor, w: torch.Tensor) -> None:
+        """Partial [T, H] = x @ w^T, rows scattered to their owners' reduce slots."""
+        T = x.shape[0]
+        pr = T // self.world
+        self.C.tp_gemm(x, w, self.empty, False, True, False, T, self.empty, 0, self.state, self.rank, self.world, pr,
+                       min(pr, 128), self.peers, self.rs_off, self.rs_flag_off)
+
+    def gather_rows(self, idx: torch.Tensor, T: int) -> torch.Tensor:
+        out = torch.empty(idx.numel(), self.H, dtype=torch.bfloat16, device=idx.device)
+        self.C.tp_gather_rows(self.peers, self.rank, T // self.world, self.ag_off, self.ag_flag_off, self.state,
+                              idx, out)
+        return out
+
+
+class NcclTP:
+    """Baseline: NCCL all-gather / reduce-scatter + cuBLAS, same interface."""
+
+    def __init__(self, hidden: int, max_tokens: int, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.H = hidden
+        self.shard: Optional[torch.Tensor] = None
+        self.partial: Optional[torch.Tensor] = None
+
+    def publish(self, residual, norm_w, eps, partials, x_add=None, local_out=None):
+        if partials:
+            if dist.get_backend(self.group) == "nccl":
+                red = torch.empty_like(residual)
+                dist.reduce_scatter_tensor(red, self.partial.contiguous(), group=self.group)
+            else:  # gloo has no reduce-scatter: all-reduce and keep this rank's rows
+                full = self.partial.clone()
+                dist.all_reduce(full, group=self.group)
+                pr = residual.shape[0]
+                red = full[self.rank * pr:(self.rank + 1) * pr]
+            residual.add_(red.to(residual.dtype))
+        if x_add is not None:
+            residual.add_(x_add)
+        self.shard = R.rmsnorm(residual, norm_w, eps)
+        if local_out is not None:
+            local_out.copy_(self.shard)
+
+    def _gather(self, T):
+        parts = [torch.empty_like(self.shard) for _ in range(self.world)]
+        dist.all_gather(parts, self.shard.contiguous(), group=self.group)
+        return torch.cat(parts, 0)
+
+    def ag_gemm(self, w, T, swiglu=False):
+        y = torch.matmul(self._gather(T), w.t())
+        return R.swiglu(y) if swiglu else y
+
+    def gemm_rs(self, x, w):
+        self.partial = torch.matmul(x, w.t())
+
+    def gather_rows(self, idx, T):
+        return self._gather(T).index_select(0, idx)

@@ -81,3 +81,29 @@ def _pipe_worker(rank, world, port):
 
 def test_pipeline_gloo_three_stages():
     mp.spawn(_pipe_worker, args=(3, _port()), nprocs=3, join=True)
+
+
+def _spawn_tp_cpu(rank, world, port):
+    sys.path.insert(0, HERE)
+    import _tp_worker
+
+    _tp_worker.run(rank, world, "torch", port, "cpu")
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_baseline_gloo_matches_single(world):
+    mp.spawn(_spawn_tp_cpu, args=(world, _port()), nprocs=world, join=True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("backend", ["native", "torch"])
+def test_tp_multi_gpu(cuda, backend):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    n = 2 if n < 4 else 4
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), backend]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

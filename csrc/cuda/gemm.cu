@@ -260,71 +260,102 @@ void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& 
 
 namespace mb {
 
-// Tensor-parallel GEMM.  gather: activations are the concatenation of every
-// rank's shard (read in place from the peers with TMA); scatter: the output
-// partial rows go to their owning ranks' reduce-scatter slots.
-//   x     : local activations [T, K] (scatter) - unused when gather
-//   w     : weight shard [N_out(*2 for swiglu), K]
-//   out   : local output [T, N_out] (not scatter)
-void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool gather, bool scatter, bool swiglu,
-             int64_t T, const at::Tensor& maps, int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks,
-             int64_t peer_rows, int64_t sub, const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off) {
-  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous());
-  const int64_t K = w.size(1);
+// Tensor-parallel GEMM.
+//   wait    : the activations x are this rank's gathered buffer, filled by the
+//             peers' P2P pushes; the TMA producer waits (bounded) until every
+//             rank's shard of the current epoch has arrived.
+//   scatter : partial output rows go to their owners' reduce-scatter slots
+//             (directly from the epilogue, or after a split-K reduction).
+void tp_splitk_scatter(const at::Tensor& ws, int64_t splits, int64_t T, int64_t H, int64_t peer_rows,
+                       const at::Tensor& peers, int64_t rank, int64_t rs_off, int64_t rs_flag_off, at::Tensor& state);
+
+void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool wait, bool scatter, bool swiglu,
+             int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks, int64_t peer_rows,
+             const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off, const c10::optional<at::Tensor>& workspace) {
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && x.scalar_type() == at::kBFloat16);
+  const int64_t T = x.size(0), K = w.size(1);
+  TORCH_CHECK(x.size(1) == K && x.stride(1) == 1);
   const int64_t n_out = swiglu ? w.size(0) / 2 : w.size(0);
-  TORCH_CHECK(T == peer_rows * nranks, "tp_gemm: T must equal peer_rows * ranks");
+  TORCH_CHECK(!(scatter && swiglu), "tp_gemm: scatter with swiglu is not supported");
+  TORCH_CHECK(!scatter || T == peer_rows * nranks, "tp_gemm: scatter needs T == peer_rows * ranks");
   c10::cuda::CUDAGuard guard(w.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   GemmArgs a{};
   a.K = (int)K;
   a.groups = 1;
-  a.splits = 1;
   a.ldc = (int)n_out;
   a.out_rows = (int)T;
   a.status = status_ptr(w.device().index());
-  a.tp.peer_maps = gather ? reinterpret_cast<const CUtensorMap*>(maps.data_ptr()) : nullptr;
-  a.tp.ag_flags = reinterpret_cast<const uint32_t*>(ag_flags);
   int* s = state.data_ptr<int>();
+  a.tp.ag_flags = wait ? reinterpret_cast<const uint32_t*>(ag_flags) : nullptr;
   a.tp.epoch = reinterpret_cast<uint32_t*>(s);
   a.tp.done = s + 4;
   a.tp.peer_rows = (int)peer_rows;
-  a.tp.sub = (int)sub;
   a.tp.nranks = (int)nranks;
   a.tp.rank = (int)rank;
-  a.tp.rs_peers = rs_peers.defined() && rs_peers.numel() ? reinterpret_cast<const uint64_t*>(rs_peers.data_ptr<int64_t>()) : nullptr;
+  a.tp.rs_peers = rs_peers.numel() ? reinterpret_cast<const uint64_t*>(rs_peers.data_ptr<int64_t>()) : nullptr;
   a.tp.rs_off = rs_off;
   a.tp.rs_flag_off = rs_flag_off;
-  a.mode = scatter ? kEpiScatterRS : (swiglu ? kEpiSwiGLU : kEpiStore);
-  a.out = scatter ? nullptr : out.data_ptr();
-  TORCH_CHECK(!(scatter && swiglu), "tp_gemm: scatter with swiglu is not supported");
-  TORCH_CHECK(!gather || !scatter, "tp_gemm: a boundary either gathers its input or scatters its output");
   const bool swap = T <= 256 && n_out % 128 == 0;
   if (swap) {
     const int bn = pick_bn(T, swiglu);
-    TORCH_CHECK(!gather || (bn % sub == 0 && peer_rows % sub == 0), "tp_gemm: sub-load rows must tile BN");
     auto ta = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, 128);
-    auto tb = gather ? ta : make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
+    auto tb = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
     a.a_rows = (int)w.size(0);
     a.a_up_offset = swiglu ? (int)n_out : 0;
     a.b_rows = (int)T;
     a.swap = 1;
-    dispatch(bn, swiglu, ta, tb, a, dim3((unsigned)(n_out / 128), 1, 1), st);
+    const int m_tiles = (int)(n_out / 128);
+    const int kb = (int)((K + 63) / 64);
+    int splits = 1;
+    if (!swiglu) {
+      while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4) splits *= 2;
+      if (!(workspace && workspace->defined() && workspace->numel() >= (int64_t)splits * T * n_out)) splits = 1;
+    }
+    a.splits = splits;
+    if (splits > 1) {
+      a.mode = kEpiPartialF32;
+      a.out = workspace->data_ptr();
+    } else if (scatter) {
+      a.mode = kEpiScatterRS;
+    } else {
+      a.mode = swiglu ? kEpiSwiGLU : kEpiStore;
+      a.out = out.data_ptr();
+    }
+    dispatch(bn, swiglu, ta, tb, a, dim3(m_tiles, 1, splits), st);
+    if (splits > 1) {
+      if (scatter) {
+        tp_splitk_scatter(*workspace, splits, T, n_out, peer_rows, rs_peers, rank, rs_off, rs_flag_off, state);
+      } else {
+        const int64_t n = T * n_out;
+        launch_k(splitk_reduce_kernel, (unsigned)((n / 4 + 255) / 256), 256, 0, st, (const float*)workspace->data_ptr<float>(),
+                 splits, n, (const __nv_bfloat16*)nullptr, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+      }
+    }
   } else {
-    TORCH_CHECK(!swiglu || true, "");
+    TORCH_CHECK(!swiglu, "tp_gemm: fused SwiGLU needs T <= 256");
     const int bn = n_out >= 256 ? 256 : pick_bn(n_out, false);
-    TORCH_CHECK(!gather || (128 % sub == 0 && peer_rows % sub == 0), "tp_gemm: sub-load rows must tile 128");
-    auto tb = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, swiglu ? 128 : bn);
-    auto ta = gather ? tb : make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), 128);
+    auto ta = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), 128);
+    auto tb = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, bn);
     a.a_rows = (int)((T + 127) / 128 * 128);
     a.b_rows = (int)n_out;
     a.swap = 0;
-    TORCH_CHECK(!swiglu, "tp_gemm: SwiGLU needs the swap orientation (T <= 256); use gather + separate swiglu");
+    a.splits = 1;
+    a.mode = scatter ? kEpiScatterRS : kEpiStore;
+    a.out = scatter ? nullptr : out.data_ptr();
     const int m_tiles = (int)((T + 127) / 128);
     const int n_tiles = (int)((n_out + bn - 1) / bn);
     int ny = n_tiles;
     while ((int64_t)m_tiles * ny > num_sms() * 2 && ny > 1) ny = (ny + 1) / 2;
     dispatch(bn, false, ta, tb, a, dim3(m_tiles, ny, 1), st);
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Non-owning bf16 [rows, cols] view of device memory (exchange buffers).
+at::Tensor wrap_bf16(int64_t addr, int64_t rows, int64_t cols) {
+  return at::from_blob(reinterpret_cast<void*>(addr), {rows, cols},
+                       at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, c10::cuda::current_device()));
 }
 
 }  // namespace mb

@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(192, 1)
         pdl_wait();
         pdl_trigger();
       }
-      if (args.tp.peer_maps && leader) {  // every peer's shard must be published for this boundary
+      if (args.tp.ag_flags && leader) {  // every peer's shard must be published for this boundary
         const uint32_t want = *args.tp.epoch;
         for (int p = 0; p < args.tp.nranks; ++p) {
           const uint64_t t0 = globaltimer_ns();

@@ -38,9 +38,10 @@ void ep_combine(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_
                 const c10::optional<at::Tensor>& residual, at::Tensor& out);
 void ep_recv_only(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El, int64_t H,
                   at::Tensor& row_pos, at::Tensor& offs, at::Tensor& abort);
-void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool gather, bool scatter, bool swiglu,
-             int64_t T, const at::Tensor& maps, int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks,
-             int64_t peer_rows, int64_t sub, const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off);
+void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool wait, bool scatter, bool swiglu,
+             int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks, int64_t peer_rows,
+             const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off, const c10::optional<at::Tensor>& workspace);
+at::Tensor wrap_bf16(int64_t addr, int64_t rows, int64_t cols);
 at::Tensor tp_make_peer_maps(const std::vector<int64_t>& ag_addrs, int64_t rows, int64_t H, int64_t sub);
 void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_t rows, int64_t H, int64_t ag_off,
                int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off, at::Tensor& state,
@@ -78,6 +79,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_recv_only", &mb::ep_recv_only);
   m.def("tp_gemm", &mb::tp_gemm);
   m.def("tp_make_peer_maps", &mb::tp_make_peer_maps);
+  m.def("wrap_bf16", &mb::wrap_bf16);
   m.def("tp_reduce", &mb::tp_reduce);
   m.def("tp_gather_rows", &mb::tp_gather_rows);
   m.def("ipc_alloc", [](int64_t b) {

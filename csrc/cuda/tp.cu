@@ -110,7 +110,6 @@ __global__ void tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, i
   }
   ss = warp_sum(ss);
   const float inv = rsqrtf(ss / H + eps);
-  __nv_bfloat16* ag = reinterpret_cast<__nv_bfloat16*>(self + ag_off);
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int col = c * 256 + threadIdx.x * 8;
@@ -118,7 +117,11 @@ __global__ void tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, i
     __align__(16) __nv_bfloat16 o[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16(v[c][q] * inv * __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&wr)[q]));
-    *reinterpret_cast<uint4*>(ag + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
+    // all-gather by push: this row lands at gathered row rank*rows + t in every rank's buffer
+    const size_t grow = (size_t)rank * rows + t;
+    for (int p = 0; p < nranks; ++p)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers[p] + ag_off) + grow * H + col) =
+          *reinterpret_cast<uint4*>(o);
     if (local_out) *reinterpret_cast<uint4*>(local_out + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
   }
   // last CTA: advance the epoch and publish this rank's shard to every peer
@@ -169,6 +172,52 @@ void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Split-K reduce-scatter: sums the fp32 partials of the row-parallel GEMM,
+// rounds to bf16 and stores each row once, into its owner's slot for this
+// rank; the last CTA releases the owners' flags.  CTA per token row.
+__global__ void tp_splitk_scatter_kernel(const float* __restrict__ ws, int splits, int T, int H, int peer_rows,
+                                         const uint64_t* __restrict__ peers, int rank, int nranks, int64_t rs_off,
+                                         int64_t rs_flag_off, const uint32_t* epoch, int* done) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int d = t / peer_rows, jl = t - d * peer_rows;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers[d] + rs_off) + ((size_t)rank * peer_rows + jl) * H;
+  for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
+    float4 acc = *reinterpret_cast<const float4*>(ws + (size_t)t * H + c);
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(ws + ((size_t)s * T + t) * H + c);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+    reinterpret_cast<__nv_bfloat162*>(dst + c)[0] = lo;
+    reinterpret_cast<__nv_bfloat162*>(dst + c)[1] = hi;
+  }
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  const uint32_t e = *epoch;
+  for (int p = threadIdx.x; p < nranks; p += blockDim.x) {
+    uint32_t* f = reinterpret_cast<uint32_t*>(peers[p] + rs_flag_off) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+  }
+  if (threadIdx.x == 0) *done = 0;
+}
+
+void tp_splitk_scatter(const at::Tensor& ws, int64_t splits, int64_t T, int64_t H, int64_t peer_rows,
+                       const at::Tensor& peers, int64_t rank, int64_t rs_off, int64_t rs_flag_off, at::Tensor& state) {
+  c10::cuda::CUDAGuard guard(ws.device());
+  int* s = state.data_ptr<int>();
+  launch_k(tp_splitk_scatter_kernel, (int)T, 256, 0, at::cuda::getCurrentCUDAStream(), (const float*)ws.data_ptr<float>(),
+           (int)splits, (int)T, (int)H, (int)peer_rows, reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+           (int)rank, (int)peers.numel(), rs_off, rs_flag_off, reinterpret_cast<const uint32_t*>(s), s + 6);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Bounded wait, one warp: every rank's shard of the current epoch is published
 // (flags live in this rank's own buffer, written by the peers).
 __global__ void tp_wait_flags_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int64_t ag_flag_off,
@@ -194,8 +243,8 @@ __global__ void tp_gather_rows_kernel(const uint64_t* __restrict__ peers, int pe
   pdl_wait();
   pdl_trigger();
   const int64_t g = idx[blockIdx.x];
-  const int p = (int)(g / peer_rows), r = (int)(g % peer_rows);
-  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(peers[p] + ag_off) + (size_t)r * H;
+  (void)peer_rows;
+  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(peers[0] + ag_off) + (size_t)g * H;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
     *reinterpret_cast<uint4*>(out + (size_t)blockIdx.x * H + c) = __ldcg(reinterpret_cast<const uint4*>(src + c));
 }
@@ -209,7 +258,7 @@ void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, in
   const uint64_t* pp = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
   launch_k(tp_wait_flags_kernel, 1, 32, 0, st, pp, (int)rank, (int)peers.numel(), ag_flag_off,
            reinterpret_cast<const uint32_t*>(state.data_ptr<int>()), status_ptr(out.device().index()));
-  launch_k(tp_gather_rows_kernel, B, 128, 0, st, pp, (int)peer_rows, ag_off, (const int64_t*)idx.data_ptr<int64_t>(), H,
+  launch_k(tp_gather_rows_kernel, B, 128, 0, st, pp + rank, (int)peer_rows, ag_off, (const int64_t*)idx.data_ptr<int64_t>(), H,
            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

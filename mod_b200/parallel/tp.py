@@ -7,11 +7,13 @@ tokens / ranks).  Each layer boundary is
     row-parallel GEMM -> reduce-scatter (+ residual, + next RMSNorm)   (o_proj, down)
 
 :class:`FusedTP` does both boundaries with the kernels in ``csrc/cuda/gemm.cu``
-and ``csrc/cuda/tp.cu``: the GEMM reads the other ranks' shards in place over
-NVLink (TMA loads from IPC-mapped buffers, no multicast) and scatters its
-partial rows into the owners' slots with peer stores; a fused reduce kernel
-sums them in rank order, adds the residual, applies the RMSNorm and publishes
-the next shard.  :class:`NcclTP` is the baseline: NCCL all-gather /
+and ``csrc/cuda/tp.cu``: the fused reduce kernel that produces a rank's
+normed shard stores it straight into every rank's gathered buffer over NVLink
+(each byte crosses once) and releases a flag; the next GEMM waits on those
+flags inside its TMA producer and reads locally.  The row-parallel GEMM stores
+each partial row once into its owner's slot (from the epilogue, or after a
+split-K reduction); the owner's reduce kernel sums the slots in rank order,
+adds the residual, applies the next RMSNorm and pushes the new shard.  :class:`NcclTP` is the baseline: NCCL all-gather /
 reduce-scatter around cuBLAS GEMMs.
 
 The reference has tensor-parallel settings only as configuration strings
@@ -40,6 +42,11 @@ def padded_tokens(T: int, world: int) -> int:
 
 
 class FusedTP:
+    """Fused boundaries.  Each rank's exchange buffer holds
+    ``gathered [N*cap, H]`` (every rank's normed shard, pushed there by the
+    owners' reduce kernels), ``slots [N, cap, H]`` (reduce-scatter partials from
+    each source) and the two flag arrays."""
+
     def __init__(self, hidden: int, max_tokens: int, group=None):
         from ..ops import load_extension
         from .ep import ExchangeBuffer
@@ -52,51 +59,35 @@ class FusedTP:
         al = lambda x: (x + 255) // 256 * 256  # noqa: E731
         N, cap, H = self.world, self.cap, hidden
         self.ag_off = 0
-        self.rs_off = al(cap * H * 2)
+        self.rs_off = al(N * cap * H * 2)
         self.ag_flag_off = al(self.rs_off + N * cap * H * 2)
         self.rs_flag_off = al(self.ag_flag_off + N * 4)
         total = al(self.rs_flag_off + N * 4)
         self.buf = ExchangeBuffer(total, group)
         self.peers = self.buf.peers
-        addrs = self.peers.tolist()
-        self.ag_addrs = [a + self.ag_off for a in addrs]
-        self.ag_flags_addr = addrs[self.rank] + self.ag_flag_off
+        self.own = self.peers.tolist()[self.rank]
+        self.ag_flags_addr = self.own + self.ag_flag_off
         dev = torch.device("cuda", torch.cuda.current_device())
         self.state = torch.zeros(8, dtype=torch.int32, device=dev)
-        self.maps: Dict[int, torch.Tensor] = {}
-        self.empty = torch.empty(0, dtype=torch.int64, device=dev)
-
-    def _maps(self, sub: int) -> torch.Tensor:
-        if sub not in self.maps:
-            self.maps[sub] = self.C.tp_make_peer_maps(self.ag_addrs, self.cap, self.H, sub)
-        return self.maps[sub]
-
-    @staticmethod
-    def _sub(T: int, pr: int, n_out: int) -> int:
-        if T <= 256 and n_out % 128 == 0:
-            bn = 16
-            while bn < T:
-                bn *= 2
-            return min(pr, bn)
-        return min(pr, 128)
+        self.gathered = self.C.wrap_bf16(self.own + self.ag_off, N * cap, H)
 
     # -------------------------------------------------------------- boundaries
     def publish(self, residual: torch.Tensor, norm_w: torch.Tensor, eps: float, partials: bool,
                 x_add: Optional[torch.Tensor] = None, local_out: Optional[torch.Tensor] = None) -> None:
-        """residual [pr, H] += x_add (+ sum of partials); shard = rmsnorm(residual) -> published."""
+        """residual [pr, H] += x_add (+ sum of partials); rmsnorm(residual) is pushed to every rank."""
         self.C.tp_reduce(self.peers, self.rank, partials, residual.shape[0], self.H, self.ag_off, self.rs_off,
                          self.ag_flag_off, self.rs_flag_off, self.state, x_add, residual, norm_w, eps, local_out)
 
     def ag_gemm(self, w: torch.Tensor, T: int, swiglu: bool = False) -> torch.Tensor:
-        """[T, N_out] = gather(published shards) @ w^T (w: [N_out, H] or [2*N_out, H] for SwiGLU)."""
-        pr = T // self.world
+        """[T, N_out] = gathered activations @ w^T (w: [N_out, H] or [2*N_out, H] for SwiGLU)."""
         n_out = w.shape[0] // 2 if swiglu else w.shape[0]
         fused_swiglu = swiglu and T <= 256 and n_out % 128 == 0
         cols = n_out if fused_swiglu else w.shape[0]
         out = torch.empty(T, cols, dtype=torch.bfloat16, device=w.device)
-        sub = self._sub(T, pr, cols)
-        self.C.tp_gemm(self.empty, w, out, True, False, fused_swiglu, T, self._maps(sub), self.ag_flags_addr,
-                       self.state, self.rank, self.world, pr, sub, self.peers, self.rs_off, self.rs_flag_off)
+        ws = torch.empty(8 * T * cols, dtype=torch.float32, device=w.device) if T <= 256 else None
+        x = self.gathered[:T]
+        self.C.tp_gemm(x, w, out, True, False, fused_swiglu, self.ag_flags_addr, self.state, self.rank, self.world,
+                       T // self.world, self.peers, self.rs_off, self.rs_flag_off, ws)
         if swiglu and not fused_swiglu:
             from ..ops import native
 
@@ -104,11 +95,11 @@ class FusedTP:
         return out
 
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor) -> None:
-        """Partial [T, H] = x @ w^T, rows scattered to their owners' reduce slots."""
+        """Partial [T, H] = x @ w^T, each row stored once into its owner's slot."""
         T = x.shape[0]
-        pr = T // self.world
-        self.C.tp_gemm(x, w, self.empty, False, True, False, T, self.empty, 0, self.state, self.rank, self.world, pr,
-                       min(pr, 128), self.peers, self.rs_off, self.rs_flag_off)
+        ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
+        self.C.tp_gemm(x, w, x, False, True, False, 0, self.state, self.rank, self.world, T // self.world,
+                       self.peers, self.rs_off, self.rs_flag_off, ws)
 
     def gather_rows(self, idx: torch.Tensor, T: int) -> torch.Tensor:
         out = torch.empty(idx.numel(), self.H, dtype=torch.bfloat16, device=idx.device)

@@ -28,6 +28,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--prefill-tokens", type=int, default=16384)
     ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--profile", action="store_true", help="print a per-kernel table of 3 decode steps (rank 0)")
     a = ap.parse_args(argv)
     from ..config import get_preset
     from ..engine import SamplingParams
@@ -68,6 +69,12 @@ def main(argv=None):
     e.record()
     torch.cuda.synchronize()
     ms = mdist.max_over_ranks(s.elapsed_time(e) / a.steps, dev)
+    if a.profile:
+        from .profile import kernel_table
+
+        table = kernel_table(step, 3)
+        if rank == 0:
+            print(table)
     if backend == "native":
         from ..ops import check_status
 

@@ -132,6 +132,69 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   reinterpret_cast<__nv_bfloat162*>(out + i)[1] = hi;
 }
 
+// SwiGLU split-K reduction: ws [splits][T][2*I] (gate | up) -> out [T, I]
+__global__ void splitk_swiglu_kernel(const float* __restrict__ ws, int splits, int T, int I,
+                                     __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)T * I) return;
+  const int64_t t = i / I, c = i % I;
+  float g = 0.f, u = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float* p = ws + ((int64_t)s * T + t) * 2 * I;
+    g += p[c];
+    u += p[I + c];
+  }
+  out[i] = __float2bfloat16(silu(g) * u);
+}
+
+// y[T, I] = silu(x @ gate^T) * (x @ up^T) with w = [gate; up] ([2I, K]), dual-accumulator
+// tcgen05 GEMM; decode shapes (T <= 256) use split-K with the SwiGLU applied after the reduction.
+void swiglu_linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& workspace,
+                   int64_t wait_flags, const c10::optional<at::Tensor>& state) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && w.is_contiguous());
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.is_contiguous());
+  const int64_t T = x.size(0), K = x.size(1), I = w.size(0) / 2;
+  TORCH_CHECK(w.size(1) == K && y.size(0) == T && y.size(1) == I && I % 128 == 0 && T <= 256,
+              "swiglu_linear: needs T <= 256 and I % 128 == 0");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  GemmArgs a{};
+  a.K = (int)K;
+  a.groups = 1;
+  a.ldc = (int)I;
+  a.out_rows = (int)T;
+  a.status = status_ptr(x.device().index());
+  if (wait_flags && state && state->defined()) {
+    a.tp.ag_flags = reinterpret_cast<const uint32_t*>(wait_flags);
+    a.tp.epoch = reinterpret_cast<uint32_t*>(state->data_ptr<int>());
+  }
+  const int bn = pick_bn(T, true);
+  auto ta = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, 128);
+  auto tb = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
+  a.a_rows = (int)w.size(0);
+  a.a_up_offset = (int)I;
+  a.b_rows = (int)T;
+  a.swap = 1;
+  const int m_tiles = (int)(I / 128);
+  const int kb = (int)((K + 63) / 64);
+  int splits = 1;
+  while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4) splits *= 2;
+  if (!(workspace && workspace->defined() && workspace->numel() >= (int64_t)splits * T * 2 * I)) splits = 1;
+  a.splits = splits;
+  a.mode = splits > 1 ? kEpiPartialF32 : kEpiSwiGLU;
+  a.out = splits > 1 ? workspace->data_ptr() : y.data_ptr();
+  dispatch(bn, true, ta, tb, a, dim3(m_tiles, 1, splits), st);
+  if (splits > 1) {
+    const int64_t n = T * I;
+    launch_k(splitk_swiglu_kernel, (unsigned)((n + 255) / 256), 256, 0, st, (const float*)workspace->data_ptr<float>(),
+             splits, (int)T, (int)I, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // y[T, N] = x[T, K] @ w[N, K]^T (+ residual).  `workspace` (fp32, may be
 // empty) enables split-K for decode shapes that would otherwise leave SMs idle.
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,

@@ -271,11 +271,13 @@ __global__ void __launch_bounds__(192, 1)
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           tmem_ld16(taddr + c0, v);
+          float u[16];
           if (DUAL) {
-            float u[16];
             tmem_ld16(taddr + BN + c0, u);
+            if (args.mode != kEpiPartialF32) {
 #pragma unroll
-            for (int q = 0; q < 16; ++q) v[q] = silu(v[q]) * u[q];
+              for (int q = 0; q < 16; ++q) v[q] = silu(v[q]) * u[q];
+            }
           }
           const int jbase = nt * BN + c0;         // B row inside the group
           if (args.swap) {
@@ -286,7 +288,14 @@ __global__ void __launch_bounds__(192, 1)
               if (j < cnt) {
                 const size_t o = (size_t)(b0 + j) * args.ldc + arow;
                 if (args.mode == kEpiPartialF32) {
-                  reinterpret_cast<float*>(args.out)[(size_t)split * args.out_rows * args.ldc + o] = v[q];
+                  if (DUAL) {  // raw gate / up partials side by side: [tok][2*ldc]; SwiGLU after the reduction
+                    float* w2 = reinterpret_cast<float*>(args.out) + (size_t)split * args.out_rows * 2 * args.ldc +
+                                (size_t)(b0 + j) * 2 * args.ldc + arow;
+                    w2[0] = v[q];
+                    w2[args.ldc] = u[q];
+                  } else {
+                    reinterpret_cast<float*>(args.out)[(size_t)split * args.out_rows * args.ldc + o] = v[q];
+                  }
                 } else if (args.mode == kEpiScatterRS) {
                   const int tok = b0 + j, d = tok / args.tp.peer_rows, jl = tok - d * args.tp.peer_rows;
                   __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.tp.rs_peers[d] + args.tp.rs_off);

@@ -5,6 +5,8 @@
 namespace mb {
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,
             const c10::optional<at::Tensor>& workspace, int64_t splits, int64_t orient);
+void swiglu_linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& workspace,
+                   int64_t wait_flags, const c10::optional<at::Tensor>& state);
 void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y, int64_t groups,
                     bool swiglu, int64_t max_rows_per_group);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
@@ -64,6 +66,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mod_b200 sm_100a kernels";
   m.def("linear", &mb::linear);
   m.def("grouped_linear", &mb::grouped_linear);
+  m.def("swiglu_linear", &mb::swiglu_linear);
   m.def("rmsnorm", &mb::rmsnorm);
   m.def("rope_qknorm", &mb::rope_qknorm);
   m.def("attn_decode", &mb::attn_decode);

@@ -108,7 +108,9 @@ class NativeBackend:
         x2 = x.reshape(-1, x.shape[-1])
         T = x2.shape[0]
         I = gate_up.shape[0] // 2
-        if I % 128 == 0:
+        if I % 128 == 0 and T <= 256:
+            h = self.N.swiglu_linear(x2, gate_up)
+        elif I % 128 == 0:
             offs = self._offs1(T, x.device)
             h = self.N.grouped_linear(x2, gate_up, offs, 1, True, T)
         else:

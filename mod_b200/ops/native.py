@@ -31,6 +31,18 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     return out
 
 
+def swiglu_linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                  workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(x @ gate^T) * (x @ up^T), w = [gate; up]; decode shapes (T <= 256) with split-K."""
+    T, I = x.shape[0], w.shape[0] // 2
+    if out is None:
+        out = torch.empty(T, I, dtype=x.dtype, device=x.device)
+    if workspace is None:
+        workspace = torch.empty(8 * T * 2 * I, dtype=torch.float32, device=x.device)
+    _C().swiglu_linear(x, w, out, workspace, 0, None)
+    return out
+
+
 def grouped_linear(xs: torch.Tensor, w: torch.Tensor, offs: torch.Tensor, groups: int, swiglu: bool,
                    max_rows_per_group: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     rows_pg = w.shape[0] // groups

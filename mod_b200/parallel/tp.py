@@ -84,9 +84,12 @@ class FusedTP:
         fused_swiglu = swiglu and T <= 256 and n_out % 128 == 0
         cols = n_out if fused_swiglu else w.shape[0]
         out = torch.empty(T, cols, dtype=torch.bfloat16, device=w.device)
-        ws = torch.empty(8 * T * cols, dtype=torch.float32, device=w.device) if T <= 256 else None
+        ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
         x = self.gathered[:T]
-        self.C.tp_gemm(x, w, out, True, False, fused_swiglu, self.ag_flags_addr, self.state, self.rank, self.world,
+        if fused_swiglu:  # split-K dual GEMM, SwiGLU after the reduction; waits on the shards' flags
+            self.C.swiglu_linear(x, w, out, ws, self.ag_flags_addr, self.state)
+            return out
+        self.C.tp_gemm(x, w, out, True, False, False, self.ag_flags_addr, self.state, self.rank, self.world,
                        T // self.world, self.peers, self.rs_off, self.rs_flag_off, ws)
         if swiglu and not fused_swiglu:
             from ..ops import native

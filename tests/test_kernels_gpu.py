@@ -62,6 +62,17 @@ def test_linear_residual(cuda):
     _close(y, x.float() @ w.float().t() + r.float())
 
 
+@pytest.mark.parametrize("T,K,I", [(1, 256, 128), (64, 4096, 6144), (128, 2048, 768), (200, 1024, 512)])
+def test_swiglu_linear_splitk(cuda, T, K, I):
+    native, check = _N()
+    torch.manual_seed(9)
+    x, w = _rand(T, K), _rand(2 * I, K, scale=0.05)
+    y = native.swiglu_linear(x, w)
+    check()
+    gu = x.float() @ w.float().t()
+    _close(y, torch.nn.functional.silu(gu[:, :I]) * gu[:, I:])
+
+
 @pytest.mark.parametrize("E,I,H,T,k", [(8, 128, 256, 16, 2), (16, 768, 2048, 128, 8), (128, 768, 2048, 128, 8),
                                        (4, 256, 512, 700, 2)])
 def test_grouped_swiglu_and_down(cuda, E, I, H, T, k):

@@ -60,16 +60,16 @@ CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows,
   return m;
 }
 
-template <int BN, int STAGES, bool DUAL>
+template <int BN, int STAGES, bool DUAL, bool W8 = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, cudaStream_t st) {
-  using L = GemmSmem<BN, STAGES, DUAL>;
-  auto k = gemm_tc_kernel<BN, STAGES, DUAL>;
+  using L = GemmSmem<BN, STAGES, DUAL, W8>;
+  auto k = gemm_tc_kernel<BN, STAGES, DUAL, W8>;
   static bool attr = false;  // per instantiation
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     attr = true;
   }
-  launch_k(k, grid, 192, L::kBytes, st, ta, tb, a);
+  launch_k(k, grid, L::kThreads, L::kBytes, st, ta, tb, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -93,6 +93,27 @@ static void dispatch(int bn, bool dual, const CUtensorMap& ta, const CUtensorMap
     case 64: return launch<64, 4, false>(ta, tb, a, grid, st);
     case 128: return launch<128, 3, false>(ta, tb, a, grid, st);
     default: return launch<256, 4, false>(ta, tb, a, grid, st);
+  }
+}
+
+// int8-weight variant: each stage also holds the raw int8 A tile(s) (8 KB each).
+// Stage counts keep two CTAs per SM up to BN = 64 (single-accumulator) / 64 (dual).
+static void dispatch_w8(int bn, bool dual, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                        dim3 grid, cudaStream_t st) {
+  if (dual) {
+    switch (bn) {
+      case 16: return launch<16, 2, true, true>(ta, tb, a, grid, st);
+      case 32: return launch<32, 2, true, true>(ta, tb, a, grid, st);
+      case 64: return launch<64, 2, true, true>(ta, tb, a, grid, st);
+      default: return launch<128, 3, true, true>(ta, tb, a, grid, st);
+    }
+  }
+  switch (bn) {
+    case 16: return launch<16, 4, false, true>(ta, tb, a, grid, st);
+    case 32: return launch<32, 3, false, true>(ta, tb, a, grid, st);
+    case 64: return launch<64, 3, false, true>(ta, tb, a, grid, st);
+    case 128: return launch<128, 4, false, true>(ta, tb, a, grid, st);
+    default: return launch<256, 3, false, true>(ta, tb, a, grid, st);
   }
 }
 
@@ -416,6 +437,95 @@ void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool wai
 }
 
 // Non-owning bf16 [rows, cols] view of device memory (exchange buffers).
+// int8 weight-only GEMM with per-row (output channel) scales:
+//   y[t, n] = scale[n] * sum_k x[t, k] * wq[n, k]  (+ residual)
+// Weights are the 128-row A operand (swap orientation) at every T; converter
+// warps expand each int8 tile to bf16 in shared memory, so weight traffic is
+// half of the bf16 GEMM's.  offs (int32 [groups+1]) selects grouped (MoE)
+// mode; swiglu takes [2I, K] gate|up weights per group and writes silu(g)*u.
+void linear_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
+               const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& workspace,
+               const c10::optional<at::Tensor>& offs, int64_t groups, bool swiglu, int64_t max_rows_per_group) {
+  TORCH_CHECK(x.is_cuda() && wq.is_cuda() && scale.is_cuda() && y.is_cuda());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && wq.scalar_type() == at::kChar && scale.scalar_type() == at::kFloat &&
+              y.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && wq.is_contiguous() && scale.is_contiguous() && y.is_contiguous());
+  const bool grouped = offs && offs->defined();
+  const int64_t T = x.size(0), K = x.size(1);
+  TORCH_CHECK(wq.size(1) == K && K % 64 == 0, "linear_w8: K must be a multiple of 64");
+  TORCH_CHECK(scale.numel() == wq.size(0), "linear_w8: one scale per weight row");
+  if (!grouped) groups = 1;
+  const int64_t rows_pg = wq.size(0) / groups;
+  TORCH_CHECK(rows_pg * groups == wq.size(0));
+  const int64_t n_out = swiglu ? rows_pg / 2 : rows_pg;
+  TORCH_CHECK(n_out % 128 == 0, "linear_w8: output features must be a multiple of 128");
+  TORCH_CHECK(y.size(0) == T && y.size(1) == n_out);
+  if (T == 0) return;
+  const __nv_bfloat16* res = nullptr;
+  if (residual && residual->defined()) {
+    TORCH_CHECK(!swiglu && residual->is_contiguous() && residual->sizes() == y.sizes());
+    res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int64_t rows_hint = grouped ? std::max<int64_t>(1, max_rows_per_group) : T;
+  const int bn = pick_bn(std::min<int64_t>(rows_hint, 256), swiglu);
+  auto ta = make_tmap_2d(wq.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, wq.size(0), K, K, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+  auto tb = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
+  GemmArgs a{};
+  a.K = (int)K;
+  a.a_rows = (int)rows_pg;
+  a.a_up_offset = swiglu ? (int)n_out : 0;
+  a.b_rows = (int)T;
+  a.b_offs = grouped ? offs->data_ptr<int>() : nullptr;
+  a.groups = (int)groups;
+  a.swap = 1;
+  a.ldc = (int)n_out;
+  a.out_rows = (int)T;
+  a.status = status_ptr(x.device().index());
+  a.w_scale = scale.data_ptr<float>();
+  a.residual = res;
+  const int m_tiles = (int)(n_out / 128);
+  const int n_tiles = (int)((rows_hint + bn - 1) / bn);
+  int splits = 1;
+  if (!grouped && T <= 256) {
+    const int kb = (int)(K / 64);
+    while (m_tiles * splits * 2 <= num_sms() && splits * 2 <= kb / 4) splits *= 2;
+    const int64_t need = (int64_t)splits * T * n_out * (swiglu ? 2 : 1);
+    if (!(workspace && workspace->defined() && workspace->numel() >= need && (T * n_out) % 4 == 0)) splits = 1;
+  }
+  a.splits = splits;
+  if (splits > 1) {
+    a.mode = kEpiPartialF32;
+    a.out = workspace->data_ptr();
+    a.residual = nullptr;
+  } else {
+    a.mode = swiglu ? kEpiSwiGLU : kEpiStore;
+    a.out = y.data_ptr();
+  }
+  int ny;
+  if (grouped) {
+    ny = std::max(1, std::min(n_tiles, 8));
+  } else {  // token tiles spread over CTAs, a couple of waves at most
+    ny = n_tiles;
+    while ((int64_t)m_tiles * ny > 2 * num_sms() && ny > 1) ny = (ny + 1) / 2;
+  }
+  dispatch_w8(bn, swiglu, ta, tb, a, dim3(m_tiles, ny, grouped ? groups : splits), st);
+  if (splits > 1) {
+    const int64_t n = T * n_out;
+    if (swiglu) {
+      launch_k(splitk_swiglu_kernel, (unsigned)((n + 255) / 256), 256, 0, st,
+               (const float*)workspace->data_ptr<float>(), splits, (int)T, (int)n_out,
+               reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+    } else {
+      launch_k(splitk_reduce_kernel, (unsigned)((n / 4 + 255) / 256), 256, 0, st, workspace->data_ptr<float>(), splits,
+               n, res, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
 at::Tensor wrap_bf16(int64_t addr, int64_t rows, int64_t cols) {
   return at::from_blob(reinterpret_cast<void*>(addr), {rows, cols},
                        at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, c10::cuda::current_device()));

@@ -63,7 +63,23 @@ struct GemmArgs {
   int out_rows;          // tokens (rows of out) for the split-K workspace stride
   int* status;
   TpArgs tp;             // tp.peer_maps == nullptr: not tensor parallel
+  const float* w_scale;  // int8-weight variant: per-row scale of A (row g*a_rows + r), applied in the epilogue
 };
+
+// Exact int8 -> bf16 for 4 packed values (byte i = element i).  Float
+// magic-number method: placing the biased byte u = b + 128 in the low mantissa
+// bits of 2^23 gives the float 2^23 + u; subtracting 2^23 + 128 leaves b
+// exactly, and any integer in [-128, 127] is exact in bf16, so truncating to
+// the upper half is exact too.  Full-rate PRMT/FADD only (no I2F).
+__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  const float f0 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7650)) - 8388736.f;
+  const float f1 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7651)) - 8388736.f;
+  const float f2 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7652)) - 8388736.f;
+  const float f3 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7653)) - 8388736.f;
+  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+}
 
 // Loads `rows` activation rows starting at gathered row `row0`, k-block kx,
 // either from the local map or from the peers' shard buffers.
@@ -84,19 +100,29 @@ __device__ __forceinline__ void load_act(const GemmArgs& a, const CUtensorMap* l
   }
 }
 
-template <int BN, int STAGES, bool DUAL>
+// Stage layout: A tile(s) [128 x 64] bf16 SW128 | B tile [BN x 64] bf16 SW128 |
+// (W8) raw int8 A tile(s) [128 x 64], unswizzled, that the converter warps expand
+// into the A slots.
+template <int BN, int STAGES, bool DUAL, bool W8 = false>
 struct GemmSmem {
+  static constexpr int kNA = DUAL ? 2 : 1;
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = BN * 64 * 2;
-  static constexpr int kStageBytes = kABytes * (DUAL ? 2 : 1) + kBBytes;
+  static constexpr int kRawBytes = W8 ? 128 * 64 : 0;
+  static constexpr int kRawOff = kABytes * kNA + kBBytes;
+  static constexpr int kStageBytes = kRawOff + kRawBytes * kNA;
+  static constexpr int kTxBytes = kStageBytes - (W8 ? kABytes * kNA : 0);  // bytes TMA delivers per stage
   static constexpr int kBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kThreads = W8 ? 320 : 192;
 };
 
-template <int BN, int STAGES, bool DUAL>
-__global__ void __launch_bounds__(192, 1)
+// Warp roles: 0 TMA producer, 1 MMA issuer, 2-5 epilogue (TMEM lane quadrant
+// warp % 4), 6-9 int8 -> bf16 converters (W8 only).
+template <int BN, int STAGES, bool DUAL, bool W8 = false>
+__global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    GemmArgs args) {
-  using L = GemmSmem<BN, STAGES, DUAL>;
+  using L = GemmSmem<BN, STAGES, DUAL, W8>;
   constexpr int kAcc = DUAL ? 2 * BN : BN;          // TMEM columns per buffer
   constexpr int kTmemCols = (2 * kAcc <= 32) ? 32 : (2 * kAcc <= 64) ? 64 : (2 * kAcc <= 128) ? 128
                             : (2 * kAcc <= 256) ? 256 : 512;
@@ -107,7 +133,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;   // [2]
   uint64_t* tempty = tfull + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* cfull = tempty + 2;      // [STAGES] (W8) A tiles converted
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cfull + STAGES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -147,6 +174,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      if (W8) mbar_init(&cfull[s], 128);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -176,9 +204,12 @@ __global__ void __launch_bounds__(192, 1)
       if (leader) {
         for (int s = 0; s < pre; ++s) {
           uint8_t* st = smem + s * L::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          tma_load_2d(st, &tmA, &full[s], (kb_lo + s) * 64, a_row0);
-          if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], (kb_lo + s) * 64, a_row0 + args.a_up_offset);
+          uint8_t* wa = W8 ? st + L::kRawOff : st;
+          mbar_arrive_expect_tx(&full[s], L::kTxBytes);
+          tma_load_2d(wa, &tmA, &full[s], (kb_lo + s) * 64, a_row0);
+          if (DUAL)
+            tma_load_2d(wa + (W8 ? L::kRawBytes : L::kABytes), &tmA, &full[s], (kb_lo + s) * 64,
+                        a_row0 + args.a_up_offset);
         }
       }
       if (dense) {
@@ -214,10 +245,13 @@ __global__ void __launch_bounds__(192, 1)
             }
             const uint32_t ph = (it / STAGES) & 1;
             if (!mbar_wait(&empty[s], ph ^ 1, args.status)) { ok = false; break; }
-            mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+            mbar_arrive_expect_tx(&full[s], L::kTxBytes);
             if (args.swap) {
-              tma_load_2d(st, &tmA, &full[s], kb * 64, a_row0);
-              if (DUAL) tma_load_2d(st + L::kABytes, &tmA, &full[s], kb * 64, a_row0 + args.a_up_offset);
+              uint8_t* wa = W8 ? st + L::kRawOff : st;
+              tma_load_2d(wa, &tmA, &full[s], kb * 64, a_row0);
+              if (DUAL)
+                tma_load_2d(wa + (W8 ? L::kRawBytes : L::kABytes), &tmA, &full[s], kb * 64,
+                            a_row0 + args.a_up_offset);
               load_act(args, &tmB, st + L::kABytes * (DUAL ? 2 : 1), &full[s], kb * 64, b0 + nt * BN, BN);
             } else {  // normal orientation: activations are the 128-row A operand
               load_act(args, &tmA, st, &full[s], kb * 64, a_row0, 128);
@@ -241,6 +275,7 @@ __global__ void __launch_bounds__(192, 1)
             const int s = it % STAGES;
             const uint32_t ph = (it / STAGES) & 1;
             if (!mbar_wait(&full[s], ph, args.status)) { ok = false; break; }
+            if (W8 && !mbar_wait(&cfull[s], ph, args.status)) { ok = false; break; }
             tc_fence_after();
             uint8_t* st = smem + s * L::kStageBytes;
             const uint32_t a_addr = smem_u32(st);
@@ -254,6 +289,36 @@ __global__ void __launch_bounds__(192, 1)
             tc_commit(&empty[s]);
           }
           tc_commit(&tfull[buf]);
+        }
+      }
+    } else if (W8 && warp >= 6) {
+      // ------------------------------------------------ int8 -> bf16 converters (warps 6-9)
+      // Thread c expands 16-byte chunks idx = c + 128 m of the [128 x 64] tile:
+      // row r = idx / 8, chunk k = idx % 8 -> SW128 position r*128 + (k ^ (r % 8))*16.
+      const int c = threadIdx.x - 192;
+      int it = 0;
+      bool ok = true;
+      for (int t = 0; t < my_tiles && ok; ++t) {
+        for (int kb = 0; kb < kbs; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1, args.status)) { ok = false; break; }
+          uint8_t* st = smem + s * L::kStageBytes;
+#pragma unroll
+          for (int a = 0; a < L::kNA; ++a) {
+            const uint8_t* raw = st + L::kRawOff + a * L::kRawBytes;
+            uint8_t* dst = st + a * L::kABytes;
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+              const int idx = c + 128 * m, r = idx >> 3, k = idx & 7;
+              const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 64 + k * 8);
+              uint4 o;
+              i8x4_to_bf16x4(w.x, o.x, o.y);
+              i8x4_to_bf16x4(w.y, o.z, o.w);
+              *reinterpret_cast<uint4*>(dst + r * 128 + ((k ^ (r & 7)) << 4)) = o;
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+          mbar_arrive(&cfull[s]);
         }
       }
     } else {
@@ -271,9 +336,19 @@ __global__ void __launch_bounds__(192, 1)
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           tmem_ld16(taddr + c0, v);
+          if (W8) {
+            const float sc = args.w_scale[g * args.a_rows + arow];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] *= sc;
+          }
           float u[16];
           if (DUAL) {
             tmem_ld16(taddr + BN + c0, u);
+            if (W8) {
+              const float sc = args.w_scale[g * args.a_rows + arow + args.a_up_offset];
+#pragma unroll
+              for (int q = 0; q < 16; ++q) u[q] *= sc;
+            }
             if (args.mode != kEpiPartialF32) {
 #pragma unroll
               for (int q = 0; q < 16; ++q) v[q] = silu(v[q]) * u[q];

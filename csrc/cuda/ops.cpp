@@ -18,6 +18,18 @@ void rope_qknorm(const at::Tensor& qkv, const c10::optional<at::Tensor>& q_w, co
 void attn_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                  const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                  const c10::optional<at::Tensor>& workspace, double scale);
+void deltanet_decode(const at::Tensor& mixed, const at::Tensor& z, const at::Tensor& ba, const at::Tensor& conv_w,
+                     at::Tensor& conv_state, at::Tensor& ssm, const at::Tensor& slots, const at::Tensor& A_log,
+                     const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor& out, int64_t Hk, int64_t Hv,
+                     int64_t dk, int64_t dv, double eps);
+void deltanet_prefill(const at::Tensor& mixed, const at::Tensor& z, const at::Tensor& ba, const at::Tensor& conv_w,
+                      at::Tensor& conv_state, at::Tensor& ssm, const at::Tensor& slots, const at::Tensor& cu,
+                      const at::Tensor& seq_of, const at::Tensor& A_log, const at::Tensor& dt_bias,
+                      const at::Tensor& norm_w, at::Tensor& out, at::Tensor& xc, int64_t Hk, int64_t Hv, int64_t dk,
+                      int64_t dv, double eps);
+void linear_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
+               const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& workspace,
+               const c10::optional<at::Tensor>& offs, int64_t groups, bool swiglu, int64_t max_rows_per_group);
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                     const c10::optional<at::Tensor>& workspace, double scale);
@@ -71,6 +83,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_qknorm", &mb::rope_qknorm);
   m.def("attn_decode", &mb::attn_decode);
   m.def("attn_decode_tc", &mb::attn_decode_tc);
+  m.def("deltanet_decode", &mb::deltanet_decode);
+  m.def("linear_w8", &mb::linear_w8);
+  m.def("deltanet_prefill", &mb::deltanet_prefill);
   m.def("attn_decode_tc_supported", &mb::attn_decode_tc_supported);
   m.def("attn_prefill_tc", &mb::attn_prefill_tc);
   m.def("moe_route", &mb::moe_route);

@@ -86,6 +86,71 @@ def case(name: str):
         cu = torch.arange(B + 1, device=dev, dtype=torch.int32) * ctx
         flops = 4 * B * Hq * D * ctx * (ctx + 1) // 2
         return (lambda: N.attn_prefill_tc(q, kc, vc, bt, cu, cl, ctx)), kv_bytes + 2 * q.numel() * 2, flops
+    if name in ("w8_qkv", "w8_prefill"):
+        from ..ops.quant import quantize_int8
+
+        T_, K, Nn = (128, 2048, 5120) if name == "w8_qkv" else (4096, 2048, 2048)
+        ws = _rot(lambda: quantize_int8(torch.randn(Nn, K, device=dev) * 0.02), K * Nn)
+        x = torch.randn(T_, K, device=dev).to(bf)
+        y = torch.empty(T_, Nn, device=dev, dtype=bf)
+        wsp = torch.empty(8 * T_ * Nn, device=dev) if T_ <= 256 else None
+        i = [0]
+
+        def run():
+            w = ws[i[0] % len(ws)]
+            N.linear_w8(x, w.q, w.scale, out=y, workspace=wsp)
+            i[0] += 1
+        return run, K * Nn + Nn * 4 + T_ * K * 2 + T_ * Nn * 2, 2 * T_ * K * Nn
+    if name == "w8_moe_gateup":
+        # Qwen3-Next experts: 512 experts, top-10, intermediate 512, hidden 2048; 128 tokens
+        from ..ops.quant import quantize_int8
+
+        E, I, H, k = 512, 512, 2048, 10
+        rows = T * k
+        counts = torch.full((E,), rows // E, dtype=torch.int32)
+        counts[: rows - int(counts.sum())] += 1
+        offs = torch.zeros(E + 1, dtype=torch.int32)
+        offs[1:] = counts.cumsum(0)
+        offs = offs.to(dev)
+        w = quantize_int8(torch.randn(E * 2 * I, H, device=dev) * 0.02)
+        xs = torch.randn(rows, H, device=dev).to(bf)
+        out = torch.empty(rows, I, device=dev, dtype=bf)
+        return ((lambda: N.linear_w8(xs, w.q, w.scale, out=out, offs=offs, groups=E, swiglu=True,
+                                     max_rows_per_group=4)), E * 2 * I * H + E * 2 * I * 4, 2 * rows * H * 2 * I)
+    if name in ("deltanet_decode", "deltanet_prefill"):
+        # Qwen3-Next linear attention: 16 key heads, 32 value heads, d = 128, conv 4
+        Hk, Hv, d = 16, 32, 128
+        C = 2 * Hk * d + Hv * d
+        S = 128
+        conv = torch.zeros(S, C, 3, device=dev)
+        ssm = torch.randn(S, Hv, d, d, device=dev) * 0.01
+        cw = (torch.randn(C, 4, device=dev) * 0.3).to(bf)
+        A = torch.zeros(Hv, device=dev)
+        dtb = torch.zeros(Hv, device=dev)
+        nw = torch.ones(d, device=dev, dtype=bf)
+        if name == "deltanet_decode":
+            B = 128
+            mix = torch.randn(B, C, device=dev).to(bf)
+            z = torch.randn(B, Hv * d, device=dev).to(bf)
+            ba = torch.randn(B, 2 * Hv, device=dev).to(bf)
+            slots = torch.arange(B, device=dev)
+            out = torch.empty(B, Hv * d, device=dev, dtype=bf)
+            nbytes = B * Hv * d * d * 4 * 2 + B * C * (2 + 4 * 2 + 3 * 8) + B * Hv * d * 4
+            return ((lambda: N.deltanet_decode(mix, z, ba, cw, conv, ssm, slots, A, dtb, nw, Hk, Hv, d, d, 1e-6,
+                                               out=out)), nbytes, B * Hv * d * d * 6)
+        nseq, L = 4, 2048
+        Tt = nseq * L
+        mix = torch.randn(Tt, C, device=dev).to(bf)
+        z = torch.randn(Tt, Hv * d, device=dev).to(bf)
+        ba = torch.randn(Tt, 2 * Hv, device=dev).to(bf)
+        slots = torch.arange(nseq, device=dev)
+        cu = torch.arange(nseq + 1, device=dev, dtype=torch.int32) * L
+        seq_of = torch.arange(Tt, device=dev, dtype=torch.int32) // L
+        out = torch.empty(Tt, Hv * d, device=dev, dtype=bf)
+        xc = torch.empty(Tt, C, device=dev)
+        return ((lambda: N.deltanet_prefill(mix, z, ba, cw, conv, ssm, slots, cu, seq_of, A, dtb, nw, Hk, Hv, d, d,
+                                            1e-6, out=out, xc=xc)), Tt * C * (2 + 4 + 4) + Tt * Hv * d * 4,
+                Tt * Hv * d * d * 6)
     if name == "rmsnorm":
         x = torch.randn(65536, 2048, device=dev).to(bf)
         w = torch.ones(2048, device=dev, dtype=bf)
@@ -94,7 +159,8 @@ def case(name: str):
     raise KeyError(name)
 
 
-CASES = ["qkv", "o", "router", "lm_head", "moe_gateup", "moe_down", "attn_decode", "attn_prefill", "rmsnorm"]
+CASES = ["qkv", "o", "router", "lm_head", "moe_gateup", "moe_down", "attn_decode", "attn_prefill", "rmsnorm",
+         "w8_qkv", "w8_prefill", "w8_moe_gateup", "deltanet_decode", "deltanet_prefill"]
 
 
 def main(argv=None):

@@ -36,12 +36,15 @@ class LLMEngine:
                  device: Union[str, torch.device] = "cuda", max_batch: int = 128, max_model_len: int = 4096,
                  num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
                  max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
-                 expert_parallel: Optional[bool] = None, tensor_parallel: bool = False):
+                 expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
+                 quantization: Optional[str] = None):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
         exchange tokens with the fused NVLink dispatch/combine (native backend)
-        or NCCL all-to-all (torch backend)."""
+        or NCCL all-to-all (torch backend).  ``quantization="int8"`` stores the
+        projection matrices as int8 with per-channel scales (int8 weight-only
+        GEMMs); expert weights stay bf16 under expert parallelism."""
         import torch.distributed as dist
 
         self.cfg = cfg
@@ -78,6 +81,13 @@ class LLMEngine:
                         if backend == "native" else NcclEPMoE(cfg, self.backend))
         if weights is None and model is None:
             weights = random_weights(cfg, device=self.device, seed=seed)
+        if quantization not in (None, "none", "int8"):
+            raise ValueError(f"unknown quantization {quantization!r} (supported: int8)")
+        if quantization == "int8" and weights is not None:
+            from ..ops.quant import quantize_model
+
+            quantize_model(weights, experts=not expert_parallel)
+        self.quantization = quantization
         self.model = model if model is not None else DecoderLM(cfg, weights, self.backend, moe_impl=moe_impl)
         bs = 16
         if num_blocks is None:

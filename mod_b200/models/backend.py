@@ -17,13 +17,14 @@ import torch
 import torch.nn.functional as F
 
 from ..ops import reference as R
+from ..ops.quant import Int8Weight, dense
 
 
 class TorchBackend:
     name = "torch"
 
     def linear(self, x, w, bias=None, residual=None, out=None):
-        y = R.linear(x, w, residual=residual)
+        y = R.linear(x, dense(w, x.dtype), residual=residual)
         if bias is not None:
             y = y + bias
         if out is not None:
@@ -35,8 +36,8 @@ class TorchBackend:
         return R.rmsnorm(x, w, eps, residual=residual)
 
     def swiglu_mlp(self, x, gate_up, down, residual=None):
-        h = R.swiglu(R.linear(x, gate_up))
-        return R.linear(h, down, residual=residual)
+        h = R.swiglu(R.linear(x, dense(gate_up, x.dtype)))
+        return R.linear(h, dense(down, x.dtype), residual=residual)
 
     def rope_qknorm(self, qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps):
         return R.rope_qknorm(qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps)
@@ -52,7 +53,7 @@ class TorchBackend:
         logits = R.linear(x, mo.router)
         ids, wts = R.moe_route(logits, top_k, renorm)
         E = mo.e_hi - mo.e_lo
-        out = R.moe_experts(x, ids - mo.e_lo, wts, mo.w13, mo.w2, E, inter)
+        out = R.moe_experts(x, ids - mo.e_lo, wts, dense(mo.w13, x.dtype), dense(mo.w2, x.dtype), E, inter)
         if mo.shared is not None:
             sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down).float()
             out = out + torch.sigmoid(R.linear(x, mo.shared_gate).float()) * sh
@@ -96,7 +97,13 @@ class NativeBackend:
         if T <= 256 and w.shape[0] % 128 == 0:
             # split-K workspace for skinny (decode) shapes
             ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=x.device)
-        y = self.N.linear(x, w, out=out, residual=residual, workspace=ws)
+        if isinstance(w, Int8Weight):
+            if w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0:
+                y = self.N.linear_w8(x, w.q, w.scale, out=out, residual=residual, workspace=ws)
+            else:  # shapes outside the kernel's tiling
+                y = self.N.linear(x, w.dequant(x.dtype), out=out, residual=residual)
+        else:
+            y = self.N.linear(x, w, out=out, residual=residual, workspace=ws)
         if bias is not None:
             y += bias
         return y
@@ -108,7 +115,13 @@ class NativeBackend:
         x2 = x.reshape(-1, x.shape[-1])
         T = x2.shape[0]
         I = gate_up.shape[0] // 2
-        if I % 128 == 0 and T <= 256:
+        if isinstance(gate_up, Int8Weight):
+            if I % 128 == 0 and gate_up.shape[1] % 64 == 0:
+                ws = torch.empty(8 * T * 2 * I, dtype=torch.float32, device=x.device) if T <= 256 else None
+                h = self.N.linear_w8(x2, gate_up.q, gate_up.scale, workspace=ws, swiglu=True)
+            else:
+                h = self.N.swiglu(self.linear(x2, gate_up))
+        elif I % 128 == 0 and T <= 256:
             h = self.N.swiglu_linear(x2, gate_up)
         elif I % 128 == 0:
             offs = self._offs1(T, x.device)
@@ -169,8 +182,14 @@ class NativeBackend:
         N.moe_permute(x, ids, offs, cursor, pos, xs)
         exp_rows = max(1, (T * top_k) // E)
         max_rows = min(T * top_k, 4 * exp_rows)
-        h = N.grouped_linear(xs, mo.w13, offs, E, True, max_rows)
-        y = N.grouped_linear(h, mo.w2, offs, E, False, max_rows)
+        if isinstance(mo.w13, Int8Weight):
+            h = N.linear_w8(xs, mo.w13.q, mo.w13.scale, offs=offs, groups=E, swiglu=True, max_rows_per_group=max_rows)
+        else:
+            h = N.grouped_linear(xs, mo.w13, offs, E, True, max_rows)
+        if isinstance(mo.w2, Int8Weight):
+            y = N.linear_w8(h, mo.w2.q, mo.w2.scale, offs=offs, groups=E, max_rows_per_group=max_rows)
+        else:
+            y = N.grouped_linear(h, mo.w2, offs, E, False, max_rows)
         out = torch.empty_like(x)
         if mo.shared is not None:
             sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down)
@@ -203,6 +222,7 @@ class CpuBackend(TorchBackend):
 
     def linear(self, x, w, bias=None, residual=None, out=None):
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        w = dense(w, torch.float32)
         y = torch.empty(x2.shape[0], w.shape[0], dtype=torch.float32)
         self.C.linear(x2, w, y)
         if bias is not None:

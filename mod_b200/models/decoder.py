@@ -85,6 +85,10 @@ class DecoderLM:
     def _deltanet(self, i, x, fb: ForwardBatch, states: StateCache):
         layer = self.delta[i]
         conv, ssm = states.layer(i)
+        if layer._native(self.be, x):
+            if fb.is_decode:
+                return layer.decode_native(self.be, x, conv, ssm, fb.state_slots)
+            return layer.prefill_native(self.be, x, conv, ssm, fb.state_slots, fb.query_lens)
         if fb.is_decode:
             return layer.decode(self.be, x, conv, ssm, fb.state_slots)
         outs = []

@@ -83,6 +83,59 @@ def recurrent_step(q, k, v, g, beta, state):
     return o, state
 
 
+def _gates(ba, A_log, dt_bias, Hv):
+    ba = ba.float()
+    beta = torch.sigmoid(ba[:, :Hv])
+    g = -torch.exp(A_log.float()) * F.softplus(ba[:, Hv:] + dt_bias.float())
+    return beta, g
+
+
+def _split_qkv(mixed, Hk, Hv, dk, dv):
+    kd = Hk * dk
+    T = mixed.shape[0]
+    q = mixed[:, :kd].reshape(T, Hk, dk)
+    k = mixed[:, kd:2 * kd].reshape(T, Hk, dk)
+    v = mixed[:, 2 * kd:].reshape(T, Hv, dv)
+    rep = Hv // Hk
+    q = _l2n(q).repeat_interleave(rep, dim=1) / math.sqrt(dk)
+    k = _l2n(k).repeat_interleave(rep, dim=1)
+    return q, k, v
+
+
+def _gated_norm(o, z, norm_w, eps, Hv, dv):
+    T = o.shape[0]
+    zf = z.float().reshape(T, Hv, dv)
+    o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float()
+    return (o * F.silu(zf)).reshape(T, Hv * dv)
+
+
+def ref_prefill(mix, z, ba, conv_w, A_log, dt_bias, norm_w, conv_state, ssm_state, slot: int, Hk, Hv, dk, dv, eps):
+    """fp32 oracle of one sequence's prefill after the projections (mix = raw q|k|v channels).
+    Updates ``conv_state[slot]`` / ``ssm_state[slot]``; returns the gated-normed output [L, Hv*dv] fp32."""
+    beta, g = _gates(ba, A_log, dt_bias, Hv)
+    Kc = conv_w.shape[1]
+    xin = torch.cat([conv_state[slot].t(), mix.float()], dim=0)        # [K-1+L, C]
+    conv_state[slot] = xin[-(Kc - 1):].t()
+    xc = F.conv1d(xin.t()[None], conv_w.float()[:, None, :], groups=xin.shape[1])[0].t()
+    q, k, v = _split_qkv(F.silu(xc), Hk, Hv, dk, dv)
+    o, S = chunk_gated_delta_rule(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1).float(),
+                                  g.t(), beta.t(), ssm_state[slot])
+    ssm_state[slot] = S
+    return _gated_norm(o.transpose(0, 1), z, norm_w, eps, Hv, dv)
+
+
+def ref_decode(mix, z, ba, conv_w, A_log, dt_bias, norm_w, conv_state, ssm_state, slots, Hk, Hv, dk, dv, eps):
+    """fp32 oracle of one decode step (one token per sequence in ``slots``)."""
+    beta, g = _gates(ba, A_log, dt_bias, Hv)
+    cs = conv_state[slots]                                           # [B, C, K-1]
+    xin = torch.cat([cs, mix.float()[:, :, None]], dim=2)            # [B, C, K]
+    conv_state[slots] = xin[:, :, 1:]
+    q, k, v = _split_qkv(F.silu((xin * conv_w.float()[None]).sum(-1)), Hk, Hv, dk, dv)
+    o, S = recurrent_step(q, k, v.float(), g, beta, ssm_state[slots])
+    ssm_state[slots] = S
+    return _gated_norm(o, z, norm_w, eps, Hv, dv)
+
+
 class DeltaNetLayer:
     """Engine-side gated DeltaNet block.  ``be`` supplies the GEMMs."""
 
@@ -91,57 +144,58 @@ class DeltaNetLayer:
         self.Hk = num_k_heads or cfg.linear_num_key_heads
         self.Hv = num_v_heads or cfg.linear_num_value_heads
         self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        self._f32 = None
 
-    def _project(self, be, x):
+    def _native(self, be, x) -> bool:
+        return (getattr(be, "name", "") == "native" and x.dtype == torch.bfloat16 and self.dk == self.dv
+                and self.dk in (64, 128) and self.w.conv.shape[1] == 4 and self.Hv % self.Hk == 0)
+
+    def _gates_f32(self):
+        if self._f32 is None:
+            self._f32 = (self.w.A_log.float().contiguous(), self.w.dt_bias.float().contiguous(),
+                         self.w.conv.to(torch.bfloat16).contiguous(), self.w.norm.to(torch.bfloat16).contiguous())
+        return self._f32
+
+    def _native_split(self, be, x):
         kd, vd = self.Hk * self.dk, self.Hv * self.dv
         p = be.linear(x, self.w.in_qkvz)
-        ba = be.linear(x, self.w.in_ba).float()
-        mix, z = p[:, : 2 * kd + vd], p[:, 2 * kd + vd:]
-        b, a = ba[:, : self.Hv], ba[:, self.Hv:]
-        beta = torch.sigmoid(b)
-        g = -torch.exp(self.w.A_log.float()) * F.softplus(a + self.w.dt_bias.float())
-        return mix, z, beta, g
+        ba = be.linear(x, self.w.in_ba)
+        return p[:, :2 * kd + vd].contiguous(), p[:, 2 * kd + vd:].contiguous(), ba.contiguous()
 
-    def _split(self, mixed):
-        kd = self.Hk * self.dk
-        T = mixed.shape[0]
-        q = mixed[:, :kd].reshape(T, self.Hk, self.dk)
-        k = mixed[:, kd:2 * kd].reshape(T, self.Hk, self.dk)
-        v = mixed[:, 2 * kd:].reshape(T, self.Hv, self.dv)
-        rep = self.Hv // self.Hk
-        q = _l2n(q).repeat_interleave(rep, dim=1) / math.sqrt(self.dk)
-        k = _l2n(k).repeat_interleave(rep, dim=1)
-        return q, k, v
-
-    def _finish(self, be, o, z, dtype):
-        T = o.shape[0]
-        zf = z.float().reshape(T, self.Hv, self.dv)
-        o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps) * self.w.norm.float()
-        o = (o * F.silu(zf)).reshape(T, self.Hv * self.dv).to(dtype)
+    def decode_native(self, be, x, conv_state, ssm_state, slots):
+        """Fused decode kernel (conv, norms, gates, delta rule, gated RMSNorm), then out projection."""
+        mixed, z, ba = self._native_split(be, x)
+        A, dtb, cw, nw = self._gates_f32()
+        o = be.N.deltanet_decode(mixed, z, ba, cw, conv_state, ssm_state, slots, A, dtb, nw, self.Hk, self.Hv,
+                                 self.dk, self.dv, self.cfg.rms_norm_eps)
         return be.linear(o, self.w.out)
+
+    def prefill_native(self, be, x, conv_state, ssm_state, slots, query_lens):
+        """All prefill sequences of a step in one conv kernel + one scan kernel."""
+        mixed, z, ba = self._native_split(be, x)
+        A, dtb, cw, nw = self._gates_f32()
+        ql = torch.tensor(query_lens, dtype=torch.int32)
+        cu = torch.zeros(len(query_lens) + 1, dtype=torch.int32)
+        cu[1:] = ql.cumsum(0)
+        seq_of = torch.repeat_interleave(torch.arange(len(query_lens), dtype=torch.int32), ql)
+        dev = x.device
+        o = be.N.deltanet_prefill(mixed, z, ba, cw, conv_state, ssm_state, slots, cu.to(dev), seq_of.to(dev), A,
+                                  dtb, nw, self.Hk, self.Hv, self.dk, self.dv, self.cfg.rms_norm_eps)
+        return be.linear(o, self.w.out)
+
+    def _dims(self):
+        return self.Hk, self.Hv, self.dk, self.dv, self.cfg.rms_norm_eps
 
     def prefill(self, be, x, conv_state, ssm_state, slot: int):
         """x: [L, H] tokens of one sequence; updates the slot's states in place."""
-        mix, z, beta, g = self._project(be, x)
-        Kc = self.w.conv.shape[1]
-        xin = torch.cat([conv_state[slot].t(), mix.float()], dim=0)        # [K-1+L, C]
-        conv_state[slot] = xin[-(Kc - 1):].t()
-        xc = F.conv1d(xin.t()[None], self.w.conv.float()[:, None, :], groups=xin.shape[1])[0].t()
-        mixed = F.silu(xc)
-        q, k, v = self._split(mixed)
-        o, S = chunk_gated_delta_rule(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1).float(),
-                                      g.t(), beta.t(), ssm_state[slot])
-        ssm_state[slot] = S
-        return self._finish(be, o.transpose(0, 1), z, x.dtype)
+        mix, z, ba = self._native_split(be, x)
+        w = self.w
+        o = ref_prefill(mix, z, ba, w.conv, w.A_log, w.dt_bias, w.norm, conv_state, ssm_state, slot, *self._dims())
+        return be.linear(o.to(x.dtype), w.out)
 
     def decode(self, be, x, conv_state, ssm_state, slots):
         """x: [B, H], one token per sequence in ``slots``."""
-        mix, z, beta, g = self._project(be, x)
-        cs = conv_state[slots]                                           # [B, C, K-1]
-        xin = torch.cat([cs, mix.float()[:, :, None]], dim=2)            # [B, C, K]
-        conv_state[slots] = xin[:, :, 1:]
-        mixed = F.silu((xin * self.w.conv.float()[None]).sum(-1))
-        q, k, v = self._split(mixed)
-        o, S = recurrent_step(q, k, v.float(), g, beta, ssm_state[slots])
-        ssm_state[slots] = S
-        return self._finish(be, o, z, x.dtype)
+        mix, z, ba = self._native_split(be, x)
+        w = self.w
+        o = ref_decode(mix, z, ba, w.conv, w.A_log, w.dt_bias, w.norm, conv_state, ssm_state, slots, *self._dims())
+        return be.linear(o.to(x.dtype), w.out)

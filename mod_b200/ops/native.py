@@ -143,3 +143,40 @@ def verify_tokens(draft, target, out=None):
         out = torch.empty(draft.shape[0], dtype=torch.int32, device=draft.device)
     _C().verify_tokens(draft, target, out)
     return out
+
+
+def deltanet_decode(mixed, z, ba, conv_w, conv_state, ssm, slots, A_log, dt_bias, norm_w, Hk: int, Hv: int,
+                    dk: int, dv: int, eps: float, out=None):
+    """Fused gated-DeltaNet decode step (conv, L2 norms, gates, delta rule, gated RMSNorm).
+    mixed [B, 2*Hk*dk + Hv*dv] raw projections, z [B, Hv*dv], ba [B, 2*Hv]; states updated in place."""
+    if out is None:
+        out = torch.empty(mixed.shape[0], Hv * dv, dtype=torch.bfloat16, device=mixed.device)
+    _C().deltanet_decode(mixed, z, ba, conv_w, conv_state, ssm, slots, A_log, dt_bias, norm_w, out, Hk, Hv, dk, dv,
+                         eps)
+    return out
+
+
+def deltanet_prefill(mixed, z, ba, conv_w, conv_state, ssm, slots, cu, seq_of, A_log, dt_bias, norm_w, Hk: int,
+                     Hv: int, dk: int, dv: int, eps: float, out=None, xc=None):
+    """Packed multi-sequence gated-DeltaNet prefill (cu: int32 offsets [nseq+1], seq_of: int32 [T])."""
+    T = mixed.shape[0]
+    if out is None:
+        out = torch.empty(T, Hv * dv, dtype=torch.bfloat16, device=mixed.device)
+    if xc is None:
+        xc = torch.empty(mixed.shape, dtype=torch.float32, device=mixed.device)
+    _C().deltanet_prefill(mixed, z, ba, conv_w, conv_state, ssm, slots, cu, seq_of, A_log, dt_bias, norm_w, out, xc,
+                          Hk, Hv, dk, dv, eps)
+    return out
+
+
+def linear_w8(x, wq, scale, out=None, residual=None, workspace=None, offs=None, groups: int = 1,
+              swiglu: bool = False, max_rows_per_group: int = 0):
+    """int8 weight-only GEMM: y = (x @ wq^T) * scale[None, :] (+ residual).  wq int8 [N, K],
+    scale f32 [N].  ``offs`` (int32 [groups+1]) = grouped expert mode over ``groups`` weight blocks;
+    ``swiglu`` = gate|up weights per group, output silu(gate) * up."""
+    rows_pg = wq.shape[0] // (groups if offs is not None else 1)
+    n_out = rows_pg // 2 if swiglu else rows_pg
+    if out is None:
+        out = torch.empty(x.shape[0], n_out, dtype=torch.bfloat16, device=x.device)
+    _C().linear_w8(x, wq, scale, out, residual, workspace, offs, groups, swiglu, max_rows_per_group)
+    return out

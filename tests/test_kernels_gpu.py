@@ -273,3 +273,124 @@ def test_embed_argmax_verify(cuda):
     t = torch.tensor([[1, 2, 9, 4], [1, 2, 3, 4]], device=cuda)
     assert native.verify_tokens(d, t).tolist() == [2, 4]
     check()
+
+
+# -------------------------------------------------------------------- DeltaNet
+def _dn_inputs(T, Hk, Hv, dk, dv, dev):
+    C = 2 * Hk * dk + Hv * dv
+    mix, z, ba = _rand(T, C), _rand(T, Hv * dv), _rand(T, 2 * Hv)
+    conv_w = _rand(C, 4, scale=0.5)
+    A_log = torch.rand(Hv, device=dev) * 2 - 1
+    dt_bias = torch.randn(Hv, device=dev) * 0.5
+    norm_w = (1 + 0.1 * torch.randn(dv, device=dev)).to(torch.bfloat16)
+    return mix, z, ba, conv_w, A_log, dt_bias, norm_w
+
+
+@pytest.mark.parametrize("Hk,Hv,dk", [(2, 4, 64), (4, 8, 128), (2, 2, 128)])
+def test_deltanet_prefill_then_decode(cuda, Hk, Hv, dk):
+    """Packed multi-sequence prefill (conv + scan kernels) then decode steps (conv + step
+    kernels) against the fp32 chunked / recurrent oracle, states compared too."""
+    from mod_b200.models.deltanet import ref_decode, ref_prefill
+
+    native, check = _N()
+    torch.manual_seed(3)
+    dv, eps, S = dk, 1e-6, 6
+    C = 2 * Hk * dk + Hv * dv
+    lens = [1, 37, 130, 3]
+    slots = torch.tensor([4, 0, 2, 5], device=cuda)
+    T = sum(lens)
+    mix, z, ba, conv_w, A_log, dt_bias, norm_w = _dn_inputs(T, Hk, Hv, dk, dv, cuda)
+    conv = torch.randn(S, C, 3, device=cuda) * 0.3
+    ssm = torch.randn(S, Hv, dk, dv, device=cuda) * 0.05
+    conv_r, ssm_r = conv.clone(), ssm.clone()
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=cuda)
+    seq_of = torch.repeat_interleave(torch.arange(len(lens), dtype=torch.int32), torch.tensor(lens)).to(cuda)
+    out = native.deltanet_prefill(mix, z, ba, conv_w, conv, ssm, slots, cu, seq_of, A_log, dt_bias, norm_w,
+                                  Hk, Hv, dk, dv, eps)
+    check()
+    refs = []
+    for b, L in enumerate(lens):
+        s0 = int(cu[b])
+        refs.append(ref_prefill(mix[s0:s0 + L], z[s0:s0 + L], ba[s0:s0 + L], conv_w, A_log, dt_bias, norm_w,
+                                conv_r, ssm_r, int(slots[b]), Hk, Hv, dk, dv, eps))
+    _close(out, torch.cat(refs))
+    torch.testing.assert_close(conv, conv_r, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(ssm, ssm_r, rtol=1e-3, atol=1e-3)
+    for step in range(3):
+        B = len(lens)
+        mix, z, ba, *_ = _dn_inputs(B, Hk, Hv, dk, dv, cuda)
+        o = native.deltanet_decode(mix, z, ba, conv_w, conv, ssm, slots, A_log, dt_bias, norm_w, Hk, Hv, dk, dv, eps)
+        check()
+        r = ref_decode(mix, z, ba, conv_w, A_log, dt_bias, norm_w, conv_r, ssm_r, slots, Hk, Hv, dk, dv, eps)
+        _close(o, r)
+        torch.testing.assert_close(conv, conv_r, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(ssm, ssm_r, rtol=1e-3, atol=1e-3)
+
+
+# ------------------------------------------------------------ int8 weight GEMM
+@pytest.mark.parametrize("T,K,N", [(1, 256, 128), (16, 2048, 2048), (100, 1024, 384), (256, 4096, 1024),
+                                   (1000, 2048, 512), (4096, 1024, 256)])
+def test_linear_w8(cuda, T, K, N):
+    from mod_b200.ops.quant import quantize_int8
+
+    native, check = _N()
+    torch.manual_seed(5)
+    x = _rand(T, K)
+    qw = quantize_int8(torch.randn(N, K, device=cuda) * 0.05)
+    ref = x.float() @ (qw.q.float() * qw.scale[:, None]).t()
+    y = native.linear_w8(x, qw.q, qw.scale)
+    check()
+    _close(y, ref)
+    if T <= 256:
+        ws = torch.empty(8 * T * N, device=cuda, dtype=torch.float32)
+        r = _rand(T, N)
+        y2 = native.linear_w8(x, qw.q, qw.scale, residual=r, workspace=ws)
+        check()
+        _close(y2, ref + r.float())
+
+
+@pytest.mark.parametrize("T,K,I", [(8, 1024, 256), (200, 2048, 512)])
+def test_linear_w8_swiglu(cuda, T, K, I):
+    from mod_b200.ops.quant import quantize_int8
+
+    native, check = _N()
+    torch.manual_seed(6)
+    x = _rand(T, K)
+    qw = quantize_int8(torch.randn(2 * I, K, device=cuda) * 0.05)
+    gu = x.float() @ (qw.q.float() * qw.scale[:, None]).t()
+    ref = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    ws = torch.empty(8 * T * 2 * I, device=cuda, dtype=torch.float32)
+    for w in (None, ws):
+        y = native.linear_w8(x, qw.q, qw.scale, workspace=w, swiglu=True)
+        check()
+        _close(y, ref)
+
+
+def test_linear_w8_grouped(cuda):
+    """Grouped (MoE) int8 experts: SwiGLU gate/up then down, vs per-expert fp32."""
+    from mod_b200.ops.quant import quantize_int8
+
+    native, check = _N()
+    torch.manual_seed(7)
+    E, H, I = 8, 512, 256
+    counts = torch.tensor([0, 5, 17, 1, 0, 40, 3, 9])
+    offs = torch.zeros(E + 1, dtype=torch.int32)
+    offs[1:] = counts.cumsum(0)
+    R_ = int(offs[-1])
+    xs = _rand(R_, H)
+    w13 = quantize_int8(torch.randn(E * 2 * I, H, device=cuda) * 0.05)
+    w2 = quantize_int8(torch.randn(E * H, I, device=cuda) * 0.05)
+    d13 = (w13.q.float() * w13.scale[:, None]).view(E, 2 * I, H)
+    d2 = (w2.q.float() * w2.scale[:, None]).view(E, H, I)
+    offs_d = offs.to(cuda)
+    h = native.linear_w8(xs, w13.q, w13.scale, offs=offs_d, groups=E, swiglu=True, max_rows_per_group=40)
+    y = native.linear_w8(h, w2.q, w2.scale, offs=offs_d, groups=E, max_rows_per_group=40)
+    check()
+    for e in range(E):
+        a, b = int(offs[e]), int(offs[e + 1])
+        if a == b:
+            continue
+        gu = xs[a:b].float() @ d13[e].t()
+        he = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+        _close(h[a:b], he)
+        _close(y[a:b], h[a:b].float() @ d2[e].t())

@@ -12,8 +12,9 @@
 // only sum a few row-band partials; the state never leaves registers during a
 // prefill scan and is streamed exactly once per decode step.
 //
-// deltanet_conv : conv + SiLU + q/k L2 norm, CTA per token, fp32 out (decode
-//                 also advances the history of the token's slot).
+// deltanet_conv : prefill conv + SiLU + q/k L2 norm, CTA per token, fp32 out.
+// deltanet_conv_decode : decode conv + SiLU, thread per (token, channel); advances
+//                 the history (q/k are normalised by the step kernel).
 // deltanet_step : decode state update + gated RMSNorm, CTA per (seq, value head).
 // deltanet_scan : prefill recurrence, CTA per (sequence, value head); also
 //                 advances the conv history to the sequence's last inputs.
@@ -39,12 +40,11 @@ __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162f
 
 }  // namespace
 
-// Conv + SiLU + q/k L2 norm, CTA per token.  mixed [T, C] raw.  Prefill (ADVANCE false):
-// seq_of [T] / cu [nseq+1] place the token in its sequence; positions before the sequence
-// start read the slot's history.  Decode (ADVANCE true): every token is its own sequence
-// (seq = t, pos = 0) and the CTA also advances that slot's history, race-free because a
-// slot belongs to one token.  Output xc [T, C] f32, q heads also scaled by DK^-1/2.
-template <int DK, int KC, bool ADVANCE>
+// Prefill conv + SiLU + q/k L2 norm, CTA per token.  mixed [T, C] raw; seq_of [T] / cu [nseq+1]
+// place the token in its sequence, and positions before the sequence start read the slot's
+// history (advanced later by the scan kernel).  Output xc [T, C] f32, q heads also scaled by
+// DK^-1/2.
+template <int DK, int KC>
 __global__ void __launch_bounds__(256)
     deltanet_conv_kernel(const __nv_bfloat16* __restrict__ mixed, const __nv_bfloat16* __restrict__ conv_w,
                          float* __restrict__ conv_state, const int64_t* __restrict__ slots,
@@ -54,8 +54,8 @@ __global__ void __launch_bounds__(256)
   pdl_trigger();
   extern __shared__ float row[];  // C floats
   const int t = blockIdx.x;
-  const int s = ADVANCE ? t : seq_of[t];
-  const int start = ADVANCE ? t : cu[s], pos = t - start;
+  const int s = seq_of[t];
+  const int start = cu[s], pos = t - start;
   float* hist = conv_state + slots[s] * (int64_t)C * (KC - 1);
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
     float in[KC];
@@ -68,10 +68,6 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int k = 0; k < KC; ++k) acc += bf(conv_w[c * KC + k]) * in[k];
     row[c] = silu(acc);
-    if (ADVANCE) {
-#pragma unroll
-      for (int k = 0; k < KC - 1; ++k) hist[c * (KC - 1) + k] = in[k + 1];
-    }
   }
   __syncthreads();
   // q/k heads: one warp per head, L2 norm
@@ -86,6 +82,32 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   float* dst = xc + (int64_t)t * C;
   for (int c = threadIdx.x; c < C; c += blockDim.x) dst[c] = row[c];
+}
+
+// Decode conv: one thread per (token, channel), all channels in parallel.  Every token is its
+// own sequence, so the thread also advances that channel's history in its slot.  Output xc
+// [B, C] f32 = SiLU(conv), not normalised (the step kernel normalises q and k).
+template <int KC>
+__global__ void __launch_bounds__(256)
+    deltanet_conv_decode_kernel(const __nv_bfloat16* __restrict__ mixed, const __nv_bfloat16* __restrict__ conv_w,
+                                float* __restrict__ conv_state, const int64_t* __restrict__ slots,
+                                float* __restrict__ xc, int B, int C) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * C) return;
+  const int b = (int)(i / C), c = (int)(i - (int64_t)b * C);
+  float* hist = conv_state + (slots[b] * (int64_t)C + c) * (KC - 1);
+  float in[KC];
+#pragma unroll
+  for (int k = 0; k < KC - 1; ++k) in[k] = hist[k];
+  in[KC - 1] = bf(mixed[i]);
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < KC; ++k) acc += bf(conv_w[c * KC + k]) * in[k];
+#pragma unroll
+  for (int k = 0; k < KC - 1; ++k) hist[k] = in[k + 1];
+  xc[i] = silu(acc);
 }
 
 // Decode state update: CTA per (sequence, value head), R*DV threads; thread (g, j) holds rows
@@ -107,11 +129,17 @@ __global__ void __launch_bounds__(R* DV)
   const int rep = Hv / Hk, hk = h / rep;
   const int C = 2 * Hk * DK + Hv * DV;
   const int64_t slot = slots[b];
-  __shared__ float qs[DK], ks[DK], part[R][DV], red[DV / 32];
+  __shared__ float qs[DK], ks[DK], part[R][DV], red[DV / 32], qkred[2][DK / 32];
   const float* x = xc + (int64_t)b * C;
-  if (tid < DK) {
-    qs[tid] = x[hk * DK + tid];
-    ks[tid] = x[Hk * DK + hk * DK + tid];
+  float qv = 0.f, kv = 0.f;
+  if (tid < DK) {  // q / k of this key head, L2-normalised here (q also scaled by DK^-1/2)
+    qv = x[hk * DK + tid];
+    kv = x[Hk * DK + hk * DK + tid];
+    const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
+    if ((tid & 31) == 0) {
+      qkred[0][tid >> 5] = sq;
+      qkred[1][tid >> 5] = sk;
+    }
   }
   const float beta = sigmoid_f(bf(ba[(int64_t)b * 2 * Hv + h]));
   const float decay = __expf(-__expf(A_log[h]) * softplus_f(bf(ba[(int64_t)b * 2 * Hv + Hv + h]) + dt_bias[h]));
@@ -119,6 +147,17 @@ __global__ void __launch_bounds__(R* DV)
   float col[RR];
 #pragma unroll
   for (int i = 0; i < RR; ++i) col[i] = S[(int64_t)i * DV] * decay;
+  __syncthreads();
+  if (tid < DK) {
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int w = 0; w < DK / 32; ++w) {
+      sq += qkred[0][w];
+      sk += qkred[1][w];
+    }
+    qs[tid] = qv * rsqrtf(sq + 1e-6f) * rsqrtf((float)DK);
+    ks[tid] = kv * rsqrtf(sk + 1e-6f);
+  }
   __syncthreads();
   float p = 0.f;
 #pragma unroll
@@ -301,15 +340,12 @@ void deltanet_decode(const at::Tensor& mixed, const at::Tensor& z, const at::Ten
   auto bp = [](const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
   const int C = (int)mixed.size(1);
   auto xc = at::empty({B, C}, mixed.options().dtype(at::kFloat));
-  const size_t smem = (size_t)C * sizeof(float);
   const int64_t* sl = (const int64_t*)slots.data_ptr<int64_t>();
 #define MB_DN(DK_, DV_, KC_, R_)                                                                                  \
   if (dk == DK_ && dv == DV_ && KC == KC_) {                                                                      \
-    auto ck = deltanet_conv_kernel<DK_, KC_, true>;                                                               \
-    if (smem > 48 * 1024)                                                                                         \
-      C10_CUDA_CHECK(cudaFuncSetAttribute(ck, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));           \
-    launch_k(ck, dim3(B), 256, smem, st, bp(mixed), bp(conv_w), conv_state.data_ptr<float>(), sl, (const int*)nullptr, \
-             (const int*)nullptr, xc.data_ptr<float>(), C, (int)Hk);                                              \
+    const int64_t n = (int64_t)B * C;                                                                             \
+    launch_k(deltanet_conv_decode_kernel<KC_>, dim3((unsigned)((n + 255) / 256)), 256, 0, st, bp(mixed),        \
+             bp(conv_w), conv_state.data_ptr<float>(), sl, xc.data_ptr<float>(), B, C);                           \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                               \
     launch_k(deltanet_step_kernel<DK_, DV_, R_>, dim3(B, (unsigned)Hv), R_ * DV_, 0, st,                         \
              (const float*)xc.data_ptr<float>(), bp(z), bp(ba), ssm.data_ptr<float>(), sl,                        \
@@ -346,7 +382,7 @@ void deltanet_prefill(const at::Tensor& mixed, const at::Tensor& z, const at::Te
   const size_t smem = (size_t)C * sizeof(float);
 #define MB_DP(DK_, DV_, KC_)                                                                                      \
   if (dk == DK_ && dv == DV_ && KC == KC_) {                                                                      \
-    auto ck = deltanet_conv_kernel<DK_, KC_, false>;                                                              \
+    auto ck = deltanet_conv_kernel<DK_, KC_>;                                                              \
     if (smem > 48 * 1024)                                                                                         \
       C10_CUDA_CHECK(cudaFuncSetAttribute(ck, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));           \
     launch_k(ck, dim3(T), 256, smem, st, bp(mixed), bp(conv_w), conv_state.data_ptr<float>(),                     \

@@ -97,7 +97,7 @@ static void dispatch(int bn, bool dual, const CUtensorMap& ta, const CUtensorMap
 }
 
 // int8-weight variant: each stage also holds the raw int8 A tile(s) (8 KB each).
-// Stage counts keep two CTAs per SM up to BN = 64 (single-accumulator) / 64 (dual).
+// Stage counts keep two CTAs per SM up to BN = 128 (single accumulator) / 64 (dual).
 static void dispatch_w8(int bn, bool dual, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                         dim3 grid, cudaStream_t st) {
   if (dual) {
@@ -112,7 +112,7 @@ static void dispatch_w8(int bn, bool dual, const CUtensorMap& ta, const CUtensor
     case 16: return launch<16, 4, false, true>(ta, tb, a, grid, st);
     case 32: return launch<32, 3, false, true>(ta, tb, a, grid, st);
     case 64: return launch<64, 3, false, true>(ta, tb, a, grid, st);
-    case 128: return launch<128, 4, false, true>(ta, tb, a, grid, st);
+    case 128: return launch<128, 2, false, true>(ta, tb, a, grid, st);
     default: return launch<256, 3, false, true>(ta, tb, a, grid, st);
   }
 }
@@ -202,7 +202,7 @@ void swiglu_linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, cons
   const int m_tiles = (int)(I / 128);
   const int kb = (int)((K + 63) / 64);
   int splits = 1;
-  while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4) splits *= 2;
+  while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4 && splits * 2 <= (T >= 64 ? 4 : 8)) splits *= 2;
   if (!(workspace && workspace->defined() && workspace->numel() >= (int64_t)splits * T * 2 * I)) splits = 1;
   a.splits = splits;
   a.mode = splits > 1 ? kEpiPartialF32 : kEpiSwiGLU;
@@ -256,7 +256,10 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::
     int splits = (int)splits_req;
     if (splits <= 0) {
       splits = 1;
-      while (m_tiles * splits * 2 <= num_sms() && splits * 2 <= kb / 4) splits *= 2;
+      // two CTAs fit per SM: fill up to 2 x SMs so more weight bytes are in flight; past 4
+      // splits (T >= 64) the fp32 partial traffic outweighs the extra parallelism
+      const int cap = T >= 64 ? 4 : 8;
+      while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4 && splits * 2 <= cap) splits *= 2;
     }
     bool use_ws = splits > 1 && workspace && workspace->defined() &&
                   workspace->numel() >= (int64_t)splits * T * N && (T * N) % 4 == 0;
@@ -393,7 +396,7 @@ void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool wai
     const int kb = (int)((K + 63) / 64);
     int splits = 1;
     if (!swiglu) {
-      while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4) splits *= 2;
+      while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4 && splits * 2 <= (T >= 64 ? 4 : 8)) splits *= 2;
       if (!(workspace && workspace->defined() && workspace->numel() >= (int64_t)splits * T * n_out)) splits = 1;
     }
     a.splits = splits;
@@ -491,7 +494,7 @@ void linear_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scal
   int splits = 1;
   if (!grouped && T <= 256) {
     const int kb = (int)(K / 64);
-    while (m_tiles * splits * 2 <= num_sms() && splits * 2 <= kb / 4) splits *= 2;
+    while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4 && splits * 2 <= (T >= 64 ? 4 : 8)) splits *= 2;
     const int64_t need = (int64_t)splits * T * n_out * (swiglu ? 2 : 1);
     if (!(workspace && workspace->defined() && workspace->numel() >= need && (T * n_out) % 4 == 0)) splits = 1;
   }

@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      if (W8) mbar_init(&cfull[s], 128);
+      if (W8) mbar_init(&cfull[s], 4);  // one arrival per converter warp
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -318,7 +318,8 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
             }
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-          mbar_arrive(&cfull[s]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&cfull[s]);
         }
       }
     } else {
@@ -356,29 +357,41 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
           }
           const int jbase = nt * BN + c0;         // B row inside the group
           if (args.swap) {
-            // out[(b0 + j), arow]: lanes of a warp write consecutive columns.
+            // out[(b0 + j), arow]: lanes of a warp write consecutive columns.  The mode
+            // switch sits outside the 16-column loop so each loop is straight-line code.
+            const int nq = min(16, cnt - jbase);
+            if (args.mode == kEpiPartialF32) {
+              const size_t ld = DUAL ? 2 * (size_t)args.ldc : (size_t)args.ldc;
+              float* p = reinterpret_cast<float*>(args.out) + (size_t)split * args.out_rows * ld +
+                         (size_t)(b0 + jbase) * ld + arow;
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const int j = jbase + q;
-              if (j < cnt) {
-                const size_t o = (size_t)(b0 + j) * args.ldc + arow;
-                if (args.mode == kEpiPartialF32) {
-                  if (DUAL) {  // raw gate / up partials side by side: [tok][2*ldc]; SwiGLU after the reduction
-                    float* w2 = reinterpret_cast<float*>(args.out) + (size_t)split * args.out_rows * 2 * args.ldc +
-                                (size_t)(b0 + j) * 2 * args.ldc + arow;
-                    w2[0] = v[q];
-                    w2[args.ldc] = u[q];
-                  } else {
-                    reinterpret_cast<float*>(args.out)[(size_t)split * args.out_rows * args.ldc + o] = v[q];
-                  }
-                } else if (args.mode == kEpiScatterRS) {
-                  const int tok = b0 + j, d = tok / args.tp.peer_rows, jl = tok - d * args.tp.peer_rows;
+              for (int q = 0; q < 16; ++q) {
+                if (q < nq) {
+                  p[q * ld] = v[q];
+                  if (DUAL) p[q * ld + args.ldc] = u[q];  // raw gate | up partials; SwiGLU after the reduction
+                }
+              }
+            } else if (args.mode == kEpiScatterRS) {
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {  // fully unrolled: v stays in registers
+                if (q < nq) {
+                  const int tok = b0 + jbase + q, d = tok / args.tp.peer_rows, jl = tok - d * args.tp.peer_rows;
                   __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.tp.rs_peers[d] + args.tp.rs_off);
                   dst[((size_t)args.tp.rank * args.tp.peer_rows + jl) * args.ldc + arow] = __float2bfloat16(v[q]);
-                } else {
-                  float r = args.residual ? __bfloat162float(args.residual[o]) : 0.f;
-                  reinterpret_cast<__nv_bfloat16*>(args.out)[o] = __float2bfloat16(v[q] + r);
                 }
+              }
+            } else {
+              const size_t off = (size_t)(b0 + jbase) * args.ldc + arow;
+              __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(args.out) + off;
+              if (args.residual) {
+                const __nv_bfloat16* r = args.residual + off;
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (q < nq) p[(size_t)q * args.ldc] = __float2bfloat16(v[q] + __bfloat162float(r[(size_t)q * args.ldc]));
+              } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (q < nq) p[(size_t)q * args.ldc] = __float2bfloat16(v[q]);
               }
             }
           } else {
@@ -395,7 +408,9 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
                 reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<uint4*>(h)[0];
                 reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<uint4*>(h)[1];
               } else {
-                for (int q = 0; q < 16 && jbase + q < cnt; ++q) dst[q] = h[q];
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (jbase + q < cnt) dst[q] = h[q];
               }
             } else if (grow < args.out_rows) {
               const size_t o = (size_t)grow * args.ldc + jbase;

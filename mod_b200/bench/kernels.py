@@ -86,6 +86,31 @@ def case(name: str):
         cu = torch.arange(B + 1, device=dev, dtype=torch.int32) * ctx
         flops = 4 * B * Hq * D * ctx * (ctx + 1) // 2
         return (lambda: N.attn_prefill_tc(q, kc, vc, bt, cu, cl, ctx)), kv_bytes + 2 * q.numel() * 2, flops
+    if name.startswith(("lin:", "w8:")):  # ad-hoc shape: lin:T:K:N (bf16) or w8:T:K:N (int8 weights)
+        kind, T_, K, Nn = name.split(":")
+        T_, K, Nn = int(T_), int(K), int(Nn)
+        x = torch.randn(T_, K, device=dev).to(bf)
+        y = torch.empty(T_, Nn, device=dev, dtype=bf)
+        wsp = torch.empty(8 * T_ * Nn, device=dev) if T_ <= 256 else None
+        i = [0]
+        if kind == "w8":
+            from ..ops.quant import quantize_int8
+
+            ws = _rot(lambda: quantize_int8(torch.randn(Nn, K, device=dev) * 0.02), K * Nn)
+
+            def run():
+                w = ws[i[0] % len(ws)]
+                N.linear_w8(x, w.q, w.scale, out=y, workspace=wsp)
+                i[0] += 1
+            wbytes = K * Nn + 4 * Nn
+        else:
+            ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)
+
+            def run():
+                N.linear(x, ws[i[0] % len(ws)], out=y, workspace=wsp)
+                i[0] += 1
+            wbytes = K * Nn * 2
+        return run, wbytes + T_ * K * 2 + T_ * Nn * 2, 2 * T_ * K * Nn
     if name in ("w8_qkv", "w8_prefill"):
         from ..ops.quant import quantize_int8
 

@@ -123,10 +123,13 @@ __global__ void ep_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x
                                            ((size_t)a.rank * a.C + slot) * a.H);
     for (int i = lane; i < a.H / 8; i += 32) dstp[i] = src[i];
   }
-  __threadfence_system();
+  // CTA barrier, then one system-scope fence + arrive per CTA (cumulative over the CTA's stores)
   __syncthreads();
   __shared__ int last;
-  if (threadIdx.x == 0) last = atomicAdd(&a.done[0], 1) == (int)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(&a.done[0], 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence_system();
@@ -219,10 +222,12 @@ __global__ void ep_combine_send_kernel(EpArgs a, const int* __restrict__ row_pos
                                         ((size_t)a.rank * a.C + slot) * a.H);
     for (int j = lane; j < a.H / 8; j += 32) d[j] = s[j];
   }
-  __threadfence_system();
   __syncthreads();
   __shared__ int last;
-  if (threadIdx.x == 0) last = atomicAdd(&a.done[1], 1) == (int)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(&a.done[1], 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence_system();

@@ -454,10 +454,12 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
   if (args.mode == kEpiScatterRS) {
     // last CTA: every partial of this rank is stored -> release the owners' flags
     __shared__ int last;
-    __threadfence_system();
     __syncthreads();
     const int nct = gridDim.x * gridDim.y * gridDim.z;
-    if (threadIdx.x == 0) last = atomicAdd(args.tp.done, 1) == nct - 1;
+    if (threadIdx.x == 0) {  // one system-scope fence per CTA, after the CTA barrier
+      __threadfence_system();
+      last = atomicAdd(args.tp.done, 1) == nct - 1;
+    }
     __syncthreads();
     if (last) {
       __threadfence_system();

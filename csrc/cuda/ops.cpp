@@ -30,6 +30,11 @@ void deltanet_prefill(const at::Tensor& mixed, const at::Tensor& z, const at::Te
 void linear_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
                const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& workspace,
                const c10::optional<at::Tensor>& offs, int64_t groups, bool swiglu, int64_t max_rows_per_group);
+void sample_tokens(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
+                   const at::Tensor& top_p, const at::Tensor& seeds, const at::Tensor& steps, at::Tensor& out);
+void patchify(const at::Tensor& images, int64_t size, int64_t patch, int64_t merge, std::vector<double> mean,
+              std::vector<double> stdv, at::Tensor& out);
+void bias_act(at::Tensor& y, const c10::optional<at::Tensor>& bias, bool gelu);
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                     const c10::optional<at::Tensor>& workspace, double scale);
@@ -85,6 +90,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode_tc", &mb::attn_decode_tc);
   m.def("deltanet_decode", &mb::deltanet_decode);
   m.def("linear_w8", &mb::linear_w8);
+  m.def("sample_tokens", &mb::sample_tokens);
+  m.def("patchify", &mb::patchify);
+  m.def("bias_act", &mb::bias_act);
   m.def("deltanet_prefill", &mb::deltanet_prefill);
   m.def("attn_decode_tc_supported", &mb::attn_decode_tc_supported);
   m.def("attn_prefill_tc", &mb::attn_prefill_tc);

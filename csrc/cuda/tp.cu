@@ -125,10 +125,13 @@ __global__ void tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, i
     if (local_out) *reinterpret_cast<uint4*>(local_out + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
   }
   // last CTA: advance the epoch and publish this rank's shard to every peer
-  __threadfence_system();
+  // CTA barrier, then one system-scope fence + arrive per CTA (cumulative over the CTA's stores)
   __syncthreads();
   __shared__ int last;
-  if (threadIdx.x == 0) last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence_system();
@@ -193,10 +196,13 @@ __global__ void tp_splitk_scatter_kernel(const float* __restrict__ ws, int split
     reinterpret_cast<__nv_bfloat162*>(dst + c)[0] = lo;
     reinterpret_cast<__nv_bfloat162*>(dst + c)[1] = hi;
   }
-  __threadfence_system();
+  // CTA barrier, then one system-scope fence + arrive per CTA (cumulative over the CTA's stores)
   __syncthreads();
   __shared__ int last;
-  if (threadIdx.x == 0) last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
   if (!last) return;
   __threadfence_system();

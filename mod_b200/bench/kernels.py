@@ -86,9 +86,10 @@ def case(name: str):
         cu = torch.arange(B + 1, device=dev, dtype=torch.int32) * ctx
         flops = 4 * B * Hq * D * ctx * (ctx + 1) // 2
         return (lambda: N.attn_prefill_tc(q, kc, vc, bt, cu, cl, ctx)), kv_bytes + 2 * q.numel() * 2, flops
-    if name.startswith(("lin:", "w8:")):  # ad-hoc shape: lin:T:K:N (bf16) or w8:T:K:N (int8 weights)
-        kind, T_, K, Nn = name.split(":")
+    if name.startswith(("lin:", "w8:")):  # ad-hoc shape: lin:T:K:N[:splits] (bf16) or w8:T:K:N (int8 weights)
+        kind, T_, K, Nn, *sp = name.split(":")
         T_, K, Nn = int(T_), int(K), int(Nn)
+        splits = int(sp[0]) if sp else -1
         x = torch.randn(T_, K, device=dev).to(bf)
         y = torch.empty(T_, Nn, device=dev, dtype=bf)
         wsp = torch.empty(8 * T_ * Nn, device=dev) if T_ <= 256 else None
@@ -107,7 +108,7 @@ def case(name: str):
             ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)
 
             def run():
-                N.linear(x, ws[i[0] % len(ws)], out=y, workspace=wsp)
+                N.linear(x, ws[i[0] % len(ws)], out=y, workspace=wsp, splits=splits)
                 i[0] += 1
             wbytes = K * Nn * 2
         return run, wbytes + T_ * K * 2 + T_ * Nn * 2, 2 * T_ * K * Nn

@@ -35,6 +35,12 @@ class TorchBackend:
     def rmsnorm(self, x, w, eps, residual=None):
         return R.rmsnorm(x, w, eps, residual=residual)
 
+    def linear_gelu(self, x, w, bias=None):
+        y = R.linear(x, dense(w, x.dtype)).float()
+        if bias is not None:
+            y = y + bias.float()
+        return F.gelu(y, approximate="tanh").to(x.dtype)
+
     def swiglu_mlp(self, x, gate_up, down, residual=None):
         h = R.swiglu(R.linear(x, dense(gate_up, x.dtype)))
         return R.linear(h, dense(down, x.dtype), residual=residual)
@@ -105,8 +111,19 @@ class NativeBackend:
         else:
             y = self.N.linear(x, w, out=out, residual=residual, workspace=ws)
         if bias is not None:
-            y += bias
+            if y.dim() == 2 and y.shape[1] % 8 == 0 and y.is_contiguous():
+                self.N.bias_act(y, bias, False)
+            else:
+                y += bias
         return y
+
+    def linear_gelu(self, x, w, bias=None):
+        """tanh-GELU(x @ w^T + bias): GEMM, then one fused bias + activation pass."""
+        y = self.N.linear(x, w) if not isinstance(w, Int8Weight) else self.linear(x, w)
+        if y.shape[1] % 8 == 0:
+            return self.N.bias_act(y, bias, True)
+        y = y.float() + (bias.float() if bias is not None else 0)
+        return F.gelu(y, approximate="tanh").to(x.dtype)
 
     def rmsnorm(self, x, w, eps, residual=None):
         return self.N.rmsnorm(x, w, eps, residual=residual)
@@ -212,6 +229,9 @@ class CpuBackend(TorchBackend):
     (``pio/plugins/cpu/c_src/tensor_ops.c``)."""
 
     name = "cpu"
+
+    def linear_gelu(self, x, w, bias=None):
+        return F.gelu(self.linear(x, w, bias=bias).float(), approximate="tanh").to(x.dtype)
 
     def __init__(self, threads: Optional[int] = None):
         import importlib

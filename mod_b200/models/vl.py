@@ -114,6 +114,13 @@ def rope_2d(x: torch.Tensor, pos: torch.Tensor, theta: float = 10000.0) -> torch
 
 
 # ------------------------------------------------------------------ encoder
+def _linear_gelu(be, x, w, b):
+    if hasattr(be, "linear_gelu"):
+        return be.linear_gelu(x, w, b)
+    h = be.linear(x, w, bias=b)
+    return F.gelu(h.float(), approximate="tanh").to(x.dtype)
+
+
 def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, be, size: int) -> torch.Tensor:
     """patches [B, N, 3*p*p] -> visual tokens [B, N/4, out_hidden] (backend ops, any dtype)."""
     B, N, _ = patches.shape
@@ -134,14 +141,12 @@ def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, b
         o = torch.stack(outs).reshape(B * N, H)
         x = be.linear(o, blk.proj, bias=blk.proj_bias, residual=x)
         h = be.rmsnorm(x, blk.norm2, eps)
-        h = be.linear(h, blk.fc1, bias=blk.fc1_bias)
-        h = F.gelu(h.float(), approximate="tanh").to(x.dtype)
+        h = _linear_gelu(be, h, blk.fc1, blk.fc1_bias)
         x = be.linear(h, blk.fc2, bias=blk.fc2_bias, residual=x)
     m2 = vc.spatial_merge_size ** 2
     x = x.reshape(B * N // m2, m2 * H)                          # merge groups are consecutive rows
     x = be.rmsnorm(x.contiguous(), vw.merge_norm, eps)
-    x = be.linear(x, vw.merge_fc1, bias=vw.merge_fc1_bias)
-    x = F.gelu(x.float(), approximate="tanh").to(x.dtype)
+    x = _linear_gelu(be, x, vw.merge_fc1, vw.merge_fc1_bias)
     x = be.linear(x.to(vw.merge_fc2.dtype), vw.merge_fc2, bias=vw.merge_fc2_bias)
     return x.view(B, N // m2, -1)
 
@@ -171,7 +176,12 @@ class VLModel:
         return self.text.sample_greedy(h)
 
     def encode_images(self, images: torch.Tensor) -> torch.Tensor:
-        patches = preprocess(images, self.cfg.vision, self.image_size)
+        vc = self.cfg.vision
+        if getattr(self.be, "name", "") == "native" and images.is_cuda and len(vc.image_mean) <= 4:
+            patches = self.be.N.patchify(images, self.image_size, vc.patch_size, vc.spatial_merge_size,
+                                         vc.image_mean, vc.image_std)
+        else:
+            patches = preprocess(images, vc, self.image_size)
         return vision_forward(self.cfg.vision, self.vw, patches, self.be, self.image_size)
 
     def prompt_with_image(self, text_ids: List[int]) -> List[int]:

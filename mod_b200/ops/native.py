@@ -180,3 +180,30 @@ def linear_w8(x, wq, scale, out=None, residual=None, workspace=None, offs=None, 
         out = torch.empty(x.shape[0], n_out, dtype=torch.bfloat16, device=x.device)
     _C().linear_w8(x, wq, scale, out, residual, workspace, offs, groups, swiglu, max_rows_per_group)
     return out
+
+
+def sample_tokens(logits, temperature, top_k, top_p, seeds, steps, out=None):
+    """Fused temperature / top-k / top-p sampling (one CTA per row, no sort); temperature <= 0
+    rows are greedy.  temperature, top_p f32 [B]; top_k int32 [B] (0 = off); seeds, steps int64 [B]
+    (the Gumbel noise is a hash of (seed, step, token id))."""
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+    _C().sample_tokens(logits.contiguous(), temperature, top_k, top_p, seeds, steps, out)
+    return out
+
+
+def patchify(images, size: int, patch: int, merge: int, mean, std, out=None):
+    """[B, C, h, w] (f32 / bf16) -> bilinear resize to size x size, (x - mean) / std, patches in
+    spatial-merge-group order as bf16 rows [B, (size/patch)^2, C*patch*patch]."""
+    B, C = images.shape[:2]
+    g = size // patch
+    if out is None:
+        out = torch.empty(B, g * g, C * patch * patch, dtype=torch.bfloat16, device=images.device)
+    _C().patchify(images.contiguous(), size, patch, merge, [float(v) for v in mean], [float(v) for v in std], out)
+    return out
+
+
+def bias_act(y, bias=None, gelu: bool = False):
+    """In place: y = act(y + bias), act = tanh-GELU or identity; y bf16 [rows, cols]."""
+    _C().bias_act(y, bias, gelu)
+    return y

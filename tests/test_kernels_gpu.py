@@ -394,3 +394,74 @@ def test_linear_w8_grouped(cuda):
         he = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
         _close(h[a:b], he)
         _close(y[a:b], h[a:b].float() @ d2[e].t())
+
+
+# -------------------------------------------------------------------- sampling
+def test_sample_greedy_and_topk1(cuda):
+    native, check = _N()
+    torch.manual_seed(8)
+    B, V = 16, 151936
+    logits = _rand(B, V, scale=3.0)
+    z = lambda v, dt: torch.full((B,), v, dtype=dt, device=cuda)  # noqa: E731
+    seeds = torch.arange(B, device=cuda, dtype=torch.int64)
+    steps = torch.zeros(B, device=cuda, dtype=torch.int64)
+    ref = logits.float().argmax(-1)
+    g = native.sample_tokens(logits, z(0.0, torch.float32), z(0, torch.int32), z(1.0, torch.float32), seeds, steps)
+    check()
+    assert torch.equal(g, ref)
+    k1 = native.sample_tokens(logits, z(0.7, torch.float32), z(1, torch.int32), z(1.0, torch.float32), seeds, steps)
+    assert torch.equal(k1, ref)
+
+
+@pytest.mark.parametrize("temp,k,p", [(1.0, 0, 1.0), (0.8, 5, 1.0), (1.0, 0, 0.7), (1.3, 6, 0.9)])
+def test_sample_distribution(cuda, temp, k, p):
+    """Many draws of one row: every token lies in the filtered support and the empirical
+    frequencies match the truncated softmax."""
+    from mod_b200.engine.sampler import filter_logits
+
+    native, check = _N()
+    torch.manual_seed(9)
+    V, n = 64, 40000
+    row = torch.randn(V, device=cuda) * 1.5
+    logits = row[None].expand(n, V).contiguous()
+    f = lambda v, dt: torch.full((n,), v, dtype=dt, device=cuda)  # noqa: E731
+    seeds = torch.arange(n, device=cuda, dtype=torch.int64) + 12345
+    steps = torch.full((n,), 3, device=cuda, dtype=torch.int64)
+    toks = native.sample_tokens(logits, f(temp, torch.float32), f(k, torch.int32), f(p, torch.float32), seeds, steps)
+    check()
+    filt = filter_logits(row[None].float(), torch.tensor([temp], device=cuda), torch.tensor([k], device=cuda),
+                         torch.tensor([p], device=cuda))[0]
+    probs = torch.softmax(filt, -1)
+    support = probs > 0
+    assert bool(support[toks].all()), "sampled a filtered-out token"
+    freq = torch.bincount(toks, minlength=V).float() / n
+    assert (freq - probs).abs().max().item() < 0.015
+    again = native.sample_tokens(logits, f(temp, torch.float32), f(k, torch.int32), f(p, torch.float32), seeds,
+                                 steps)
+    assert torch.equal(toks, again), "same (seed, step) must replay"
+
+
+# ---------------------------------------------------------------- vision front
+@pytest.mark.parametrize("h,w", [(448, 448), (300, 520)])
+def test_patchify_matches_torch_preprocess(cuda, h, w):
+    from mod_b200.config import get_preset
+    from mod_b200.models.vl import preprocess
+
+    native, check = _N()
+    vc = get_preset("qwen3-vl").vision
+    torch.manual_seed(10)
+    imgs = torch.rand(2, 3, h, w, device=cuda)
+    ref = preprocess(imgs, vc, 448)
+    out = native.patchify(imgs, 448, vc.patch_size, vc.spatial_merge_size, vc.image_mean, vc.image_std)
+    check()
+    torch.testing.assert_close(out.float(), ref.float(), rtol=1e-2, atol=2e-2)
+
+
+def test_bias_gelu(cuda):
+    native, check = _N()
+    torch.manual_seed(11)
+    y, b = _rand(333, 4096, scale=2.0), _rand(4096)
+    ref = torch.nn.functional.gelu(y.float() + b.float(), approximate="tanh")
+    native.bias_act(y, b, gelu=True)
+    check()
+    _close(y, ref)

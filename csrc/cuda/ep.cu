@@ -87,6 +87,26 @@ __device__ __forceinline__ T* at_off(uint64_t base, int64_t off) {
   return reinterpret_cast<T*>(base + off);
 }
 
+// Warp copies one row of n16 16-byte chunks: per lane 8 loads in flight, then
+// 8 stores (a load-store loop over possibly aliasing pointers would serialise
+// on every chunk).  L2 loads (.cg) for data other GPUs wrote.
+template <bool CG>
+__device__ __forceinline__ void copy_row(uint4* __restrict__ d, const uint4* __restrict__ s, int n16, int lane) {
+  for (int base = 0; base < n16; base += 32 * 8) {
+    uint4 r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * 32 + lane;
+      if (i < n16) r[j] = CG ? __ldcg(s + i) : s[i];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * 32 + lane;
+      if (i < n16) d[i] = r[j];
+    }
+  }
+}
+
 struct EpArgs {
   const uint64_t* peers;  // [N] base address of every rank's exchange buffer (own rank included)
   int rank, N, C, H, El;
@@ -121,7 +141,7 @@ __global__ void ep_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(pair / K) * a.H);
     uint4* dstp = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[dst], a.L.recv_x) +
                                            ((size_t)a.rank * a.C + slot) * a.H);
-    for (int i = lane; i < a.H / 8; i += 32) dstp[i] = src[i];
+    copy_row<false>(dstp, src, a.H / 8, lane);
   }
   // CTA barrier, then one system-scope fence + arrive per CTA (cumulative over the CTA's stores)
   __syncthreads();
@@ -147,7 +167,7 @@ __global__ void ep_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x
 
 // ---------------------------------------------------------------- receive
 // One CTA of 1024 threads: waits for all sources, orders rows by local expert.
-__global__ void ep_recv_kernel(EpArgs a, int* __restrict__ row_pos, int* __restrict__ offs, int* __restrict__ abort) {
+__global__ void __launch_bounds__(1024) ep_recv_kernel(EpArgs a, int* __restrict__ row_pos, int* __restrict__ offs, int* __restrict__ abort) {
   pdl_wait();
   pdl_trigger();
   const uint32_t epoch = *a.epoch + 1;
@@ -175,14 +195,34 @@ __global__ void ep_recv_kernel(EpArgs a, int* __restrict__ row_pos, int* __restr
     if (ok_all && slot < cnts[src]) atomicAdd(&hist[__ldcg(meta + i)], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {  // El <= 1024: serial scan is a few hundred cycles
-    int acc = 0;
-    for (int e = 0; e < a.El; ++e) {
-      offs[e] = acc;
-      cursor[e] = acc;
-      acc += hist[e];
+  {  // exclusive scan of hist over El <= 1024 experts: warp scans, then a scan of the warp totals
+    __shared__ int wsum[32];
+    const int e = threadIdx.x, lane = e & 31, wid = e >> 5;
+    const int h = e < a.El ? hist[e] : 0;
+    int incl = h;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
     }
-    offs[a.El] = acc;
+    if (lane == 31) wsum[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      int w = lane < (int)(blockDim.x >> 5) ? wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      wsum[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int excl = incl - h + (wid > 0 ? wsum[wid - 1] : 0);
+    if (e < a.El) {
+      offs[e] = excl;
+      cursor[e] = excl;
+    }
+    if (e == a.El - 1) offs[a.El] = excl + h;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < rows; i += blockDim.x) {
@@ -203,7 +243,7 @@ __global__ void ep_permute_kernel(EpArgs a, const int* __restrict__ row_pos, __n
     if (p < 0) continue;
     const uint4* s = reinterpret_cast<const uint4*>(rx + (size_t)i * a.H);
     uint4* d = reinterpret_cast<uint4*>(xs + (size_t)p * a.H);
-    for (int j = lane; j < a.H / 8; j += 32) d[j] = __ldcg(s + j);
+    copy_row<true>(d, s, a.H / 8, lane);
   }
 }
 
@@ -220,7 +260,7 @@ __global__ void ep_combine_send_kernel(EpArgs a, const int* __restrict__ row_pos
     const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)p * a.H);
     uint4* d = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[src], a.L.comb) +
                                         ((size_t)a.rank * a.C + slot) * a.H);
-    for (int j = lane; j < a.H / 8; j += 32) d[j] = s[j];
+    copy_row<false>(d, s, a.H / 8, lane);
   }
   __syncthreads();
   __shared__ int last;
@@ -258,13 +298,22 @@ __global__ void ep_combine_reduce_kernel(EpArgs a, const int* __restrict__ map, 
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] = residual ? __bfloat162float(residual[(size_t)t * a.H + c + q]) : 0.f;
       if (ok_all) {
-        for (int k = 0; k < K; ++k) {
-          const int m = map[t * K + k];
-          const float w = wts[t * K + k];
-          uint4 raw = __ldcg(reinterpret_cast<const uint4*>(comb + (size_t)m * a.H + c));
-          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+        for (int k0 = 0; k0 < K; k0 += 8) {  // 8 expert rows in flight, summed in k order
+          uint4 raw[8];
+          float wk[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) acc[q] += w * __bfloat162float(h[q]);
+          for (int j = 0; j < 8; ++j)
+            if (k0 + j < K) {
+              raw[j] = __ldcg(reinterpret_cast<const uint4*>(comb + (size_t)map[t * K + k0 + j] * a.H + c));
+              wk[j] = wts[t * K + k0 + j];
+            }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (k0 + j < K) {
+              const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[j]);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) acc[q] += wk[j] * __bfloat162float(h[q]);
+            }
         }
       }
       __align__(16) __nv_bfloat16 o8[8];

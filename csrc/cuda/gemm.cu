@@ -258,8 +258,11 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::
       splits = 1;
       // two CTAs fit per SM: fill up to 2 x SMs so more weight bytes are in flight; past 4
       // splits (T >= 64) the fp32 partial traffic outweighs the extra parallelism
-      const int cap = T >= 64 ? 4 : 8;
-      while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / 4 && splits * 2 <= cap) splits *= 2;
+      // A GEMM of a few weight tiles (router-like) is pure latency: split it down to 2 K-blocks
+      // per CTA; its partials stay small (m_tiles x 128 x T floats per split).
+      const int cap = m_tiles <= 8 ? 16 : (T >= 64 ? 4 : 8);
+      const int min_kb = m_tiles <= 8 ? 2 : 4;
+      while (m_tiles * splits * 2 <= 2 * num_sms() && splits * 2 <= kb / min_kb && splits * 2 <= cap) splits *= 2;
     }
     bool use_ws = splits > 1 && workspace && workspace->defined() &&
                   workspace->numel() >= (int64_t)splits * T * N && (T * N) % 4 == 0;

@@ -44,26 +44,29 @@ __device__ __forceinline__ uint32_t ld_acq(const uint32_t* p) {
   return v;
 }
 
-// CTA per local row.  nsrc == 0: publish only (no partials to wait for).
-template <int CH>  // one warp per row: H / 256 chunks of 8 columns per lane
-__global__ void tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int nsrc, int rows,
-                                 int64_t ag_off, int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off,
-                                 uint32_t* epoch, int* done, const __nv_bfloat16* __restrict__ x_add,
-                                 __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
-                                 __nv_bfloat16* __restrict__ local_out, int* status) {
-  constexpr int H = CH * 256;
+// CTA per local row, H/8 threads, one 16-byte column chunk per thread: every
+// load of the row (residual, x_add, the nsrc partial slots) is issued before
+// any store, so a row costs about one memory round trip instead of one per
+// chunk.  nsrc == 0: publish only (no partials to wait for).
+__global__ void __launch_bounds__(1024)
+    tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int nsrc, int rows, int H,
+                     int64_t ag_off, int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off, uint32_t* epoch,
+                     int* done, const __nv_bfloat16* __restrict__ x_add, __nv_bfloat16* __restrict__ residual,
+                     const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* __restrict__ local_out,
+                     int* status) {
   pdl_wait();
   pdl_trigger();
   const uint32_t e = *epoch;
-  const int t = blockIdx.x;
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int col = tid * 8;
   const uint64_t self = peers[rank];
-  __shared__ float red[8];
+  __shared__ float red[32];
   __shared__ int ok_all;
-  if (threadIdx.x == 0) ok_all = 1;
+  if (tid == 0) ok_all = 1;
   __syncthreads();
   if (nsrc > 0) {
     const uint32_t* rf = reinterpret_cast<const uint32_t*>(self + rs_flag_off);
-    for (int s = threadIdx.x; s < nranks; s += blockDim.x) {
+    for (int s = tid; s < nranks; s += blockDim.x) {
       const uint64_t t0 = globaltimer_ns();
       while ((int32_t)(ld_acq(rf + s) - e) < 0) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -76,54 +79,56 @@ __global__ void tp_reduce_kernel(const uint64_t* __restrict__ peers, int rank, i
     __syncthreads();
     __threadfence();
   }
-  // each thread: CH chunks of 8 columns (blockDim = 32)
-  float v[CH][8];
-  float ss = 0.f;
-  const __nv_bfloat16* slots = reinterpret_cast<const __nv_bfloat16*>(self + rs_off);
+  const size_t off = (size_t)t * H + col;
+  const uint4 rr = *reinterpret_cast<const uint4*>(residual + off);
+  const uint4 xa = x_add ? *reinterpret_cast<const uint4*>(x_add + off) : make_uint4(0, 0, 0, 0);
+  const uint4 wr = *reinterpret_cast<const uint4*>(w + col);
+  float acc[8];
 #pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    const int col = c * 256 + threadIdx.x * 8;
-    float acc[8];
-    uint4 rr = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + col);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rr)[q]);
-    if (x_add) {
-      uint4 xa = *reinterpret_cast<const uint4*>(x_add + (size_t)t * H + col);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&xa)[q]);
-    }
-    if (ok_all) {
-      for (int s = 0; s < nsrc; ++s) {  // fixed rank order: deterministic
-        uint4 pr = __ldcg(reinterpret_cast<const uint4*>(slots + ((size_t)s * rows + t) * H + col));
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&pr)[q]);
-      }
-    }
-    __align__(16) __nv_bfloat16 hb[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      hb[q] = __float2bfloat16(acc[q]);
-      v[c][q] = __bfloat162float(hb[q]);
-      ss += v[c][q] * v[c][q];
-    }
-    *reinterpret_cast<uint4*>(residual + (size_t)t * H + col) = *reinterpret_cast<uint4*>(hb);
+  for (int q = 0; q < 8; ++q) {
+    acc[q] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rr)[q]);
+    if (x_add) acc[q] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&xa)[q]);
   }
+  if (ok_all && nsrc > 0) {
+    const __nv_bfloat16* slots = reinterpret_cast<const __nv_bfloat16*>(self + rs_off);
+    constexpr int kBatch = 8;  // partial loads in flight together; summed in fixed rank order
+    for (int s0 = 0; s0 < nsrc; s0 += kBatch) {
+      uint4 pr[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (s0 + j < nsrc) pr[j] = __ldcg(reinterpret_cast<const uint4*>(slots + ((size_t)(s0 + j) * rows + t) * H + col));
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (s0 + j < nsrc) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&pr[j])[q]);
+        }
+    }
+  }
+  __align__(16) __nv_bfloat16 hb[8];
+  float v[8], ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    hb[q] = __float2bfloat16(acc[q]);
+    v[q] = __bfloat162float(hb[q]);
+    ss += v[q] * v[q];
+  }
+  *reinterpret_cast<uint4*>(residual + off) = *reinterpret_cast<uint4*>(hb);
   ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / H + eps);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float inv = rsqrtf(tot / H + eps);
+  __align__(16) __nv_bfloat16 o[8];
 #pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    const int col = c * 256 + threadIdx.x * 8;
-    uint4 wr = *reinterpret_cast<const uint4*>(w + col);
-    __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16(v[c][q] * inv * __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&wr)[q]));
-    // all-gather by push: this row lands at gathered row rank*rows + t in every rank's buffer
-    const size_t grow = (size_t)rank * rows + t;
-    for (int p = 0; p < nranks; ++p)
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers[p] + ag_off) + grow * H + col) =
-          *reinterpret_cast<uint4*>(o);
-    if (local_out) *reinterpret_cast<uint4*>(local_out + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
-  }
+  for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16(v[q] * inv * __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&wr)[q]));
+  // all-gather by push: this row lands at gathered row rank*rows + t in every rank's buffer
+  const size_t grow = (size_t)rank * rows + t;
+  for (int p = 0; p < nranks; ++p)
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers[p] + ag_off) + grow * H + col) =
+        *reinterpret_cast<uint4*>(o);
+  if (local_out) *reinterpret_cast<uint4*>(local_out + off) = *reinterpret_cast<uint4*>(o);
   // last CTA: advance the epoch and publish this rank's shard to every peer
   // CTA barrier, then one system-scope fence + arrive per CTA (cumulative over the CTA's stores)
   __syncthreads();
@@ -163,22 +168,16 @@ void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_
   auto* res = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
   auto* ww = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   const int grid = (int)std::max<int64_t>(1, rows);
-#define MB_TPR(C) \
-  case C: launch_k(tp_reduce_kernel<C>, grid, 32, 0, st, pp, (int)rank, N, with_partials ? N : 0, (int)rows, ag_off, rs_off, \
-                   ag_flag_off, rs_flag_off, reinterpret_cast<uint32_t*>(s), s + 5, (const __nv_bfloat16*)bf(x_add), res, ww, \
-                   (float)eps, bf(local_out), status_ptr(residual.device().index())); break;
-  switch (H / 256) {
-    MB_TPR(4) MB_TPR(8) MB_TPR(16) MB_TPR(1) MB_TPR(2) MB_TPR(32)
-    default: TORCH_CHECK(false, "tp_reduce: unsupported hidden size");
-  }
-#undef MB_TPR
+  launch_k(tp_reduce_kernel, grid, (int)(H / 8), 0, st, pp, (int)rank, N, with_partials ? N : 0, (int)rows, (int)H,
+           ag_off, rs_off, ag_flag_off, rs_flag_off, reinterpret_cast<uint32_t*>(s), s + 5,
+           (const __nv_bfloat16*)bf(x_add), res, ww, (float)eps, bf(local_out), status_ptr(residual.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // Split-K reduce-scatter: sums the fp32 partials of the row-parallel GEMM,
 // rounds to bf16 and stores each row once, into its owner's slot for this
 // rank; the last CTA releases the owners' flags.  CTA per token row.
-__global__ void tp_splitk_scatter_kernel(const float* __restrict__ ws, int splits, int T, int H, int peer_rows,
+__global__ void __launch_bounds__(1024) tp_splitk_scatter_kernel(const float* __restrict__ ws, int splits, int T, int H, int peer_rows,
                                          const uint64_t* __restrict__ peers, int rank, int nranks, int64_t rs_off,
                                          int64_t rs_flag_off, const uint32_t* epoch, int* done) {
   pdl_wait();
@@ -187,10 +186,17 @@ __global__ void tp_splitk_scatter_kernel(const float* __restrict__ ws, int split
   const int d = t / peer_rows, jl = t - d * peer_rows;
   __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers[d] + rs_off) + ((size_t)rank * peer_rows + jl) * H;
   for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
-    float4 acc = *reinterpret_cast<const float4*>(ws + (size_t)t * H + c);
-    for (int s = 1; s < splits; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(ws + ((size_t)s * T + t) * H + c);
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < splits; s0 += 8) {  // 8 split partials in flight, summed in split order
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < splits) v[j] = *reinterpret_cast<const float4*>(ws + ((size_t)(s0 + j) * T + t) * H + c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < splits) {
+          acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+        }
     }
     __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
     reinterpret_cast<__nv_bfloat162*>(dst + c)[0] = lo;
@@ -218,7 +224,8 @@ void tp_splitk_scatter(const at::Tensor& ws, int64_t splits, int64_t T, int64_t 
                        const at::Tensor& peers, int64_t rank, int64_t rs_off, int64_t rs_flag_off, at::Tensor& state) {
   c10::cuda::CUDAGuard guard(ws.device());
   int* s = state.data_ptr<int>();
-  launch_k(tp_splitk_scatter_kernel, (int)T, 256, 0, at::cuda::getCurrentCUDAStream(), (const float*)ws.data_ptr<float>(),
+  const int threads = (int)std::min<int64_t>(1024, std::max<int64_t>(32, H / 4));
+  launch_k(tp_splitk_scatter_kernel, (int)T, threads, 0, at::cuda::getCurrentCUDAStream(), (const float*)ws.data_ptr<float>(),
            (int)splits, (int)T, (int)H, (int)peer_rows, reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
            (int)rank, (int)peers.numel(), rs_off, rs_flag_off, reinterpret_cast<const uint32_t*>(s), s + 6);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -45,7 +45,7 @@ def case(name: str):
         ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)
         x = torch.randn(T, K, device=dev).to(bf)
         y = torch.empty(T, Nn, device=dev, dtype=bf)
-        wsp = torch.empty(8 * T * Nn, device=dev)
+        wsp = torch.empty(16 * T * Nn, device=dev)
         orient = 0 if name == "lm_head" else -1
         i = [0]
 

@@ -100,9 +100,11 @@ class NativeBackend:
     def linear(self, x, w, bias=None, residual=None, out=None):
         T = x.reshape(-1, x.shape[-1]).shape[0]
         ws = None
-        if T <= 256 and w.shape[0] % 128 == 0:
-            # split-K workspace for skinny (decode) shapes
-            ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=x.device)
+        n_out = w.shape[0]
+        max_splits = 16 if n_out <= 1024 else (8 if n_out <= 128 * self._sms(x.device) else 0)
+        if T <= 256 and n_out % 128 == 0 and max_splits:
+            # split-K workspace for skinny (decode) shapes that can split (not the LM head)
+            ws = torch.empty(max_splits * T * n_out, dtype=torch.float32, device=x.device)
         if isinstance(w, Int8Weight):
             if w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0:
                 y = self.N.linear_w8(x, w.q, w.scale, out=out, residual=residual, workspace=ws)

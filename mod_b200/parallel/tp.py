@@ -84,7 +84,7 @@ class FusedTP:
         fused_swiglu = swiglu and T <= 256 and n_out % 128 == 0
         cols = n_out if fused_swiglu else w.shape[0]
         out = torch.empty(T, cols, dtype=torch.bfloat16, device=w.device)
-        ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
+        ws = torch.empty(16 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
         x = self.gathered[:T]
         if fused_swiglu:  # split-K dual GEMM, SwiGLU after the reduction; waits on the shards' flags
             self.C.swiglu_linear(x, w, out, ws, self.ag_flags_addr, self.state)
@@ -100,7 +100,7 @@ class FusedTP:
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor) -> None:
         """Partial [T, H] = x @ w^T, each row stored once into its owner's slot."""
         T = x.shape[0]
-        ws = torch.empty(8 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
+        ws = torch.empty(16 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
         self.C.tp_gemm(x, w, x, False, True, False, 0, self.state, self.rank, self.world, T // self.world,
                        self.peers, self.rs_off, self.rs_flag_off, ws)
 

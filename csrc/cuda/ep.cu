@@ -10,8 +10,18 @@
 //   cnt    [N]      int32 rows received from each source
 //   flag_d [N]      u32   dispatch epoch written by each source
 //   flag_c [N]      u32   combine epoch written by each owner
+//   cntm   [N][1024] int32 per-expert counts of each source (direct dispatch)
+//   flag_n [N]      u32   counts epoch written by each source
 // C = capacity per (source, owner) = max tokens per call x top-k, so a call can
-// never overflow.  One MoE call:
+// never overflow.  The product path (ep_dispatch2 / ep_combine2) is
+//   ep_dispatch2        counts all-gather, then each row stored straight into
+//                       its owner's expert-ordered receive region (+ its return
+//                       address in meta); flag_d released at every owner.
+//   grouped GEMMs       gate/up waits on flag_d in its TMA producer; down.
+//   ep_combine_send2    result rows back to their sources' comb slots.
+//   ep_combine_reduce   as below.
+// The three-kernel receive path below (dispatch, recv, permute) is kept for
+// the bounded-wait fault test.  One MoE call:
 //   ep_dispatch      (source) each (token, k) pair claims a slot in its owner's
 //                    receive region and stores the hidden row there; the last
 //                    CTA publishes counts and releases flag_d at the owner.
@@ -43,8 +53,10 @@
 
 namespace mb {
 
+constexpr int kEpMaxExperts = 1024;  // global experts covered by the count matrix
+
 struct EpLayout {
-  int64_t recv_x, comb, meta, cnt, flag_d, flag_c, total;
+  int64_t recv_x, comb, meta, cnt, flag_d, flag_c, cntm, flag_n, total;
 };
 
 static EpLayout ep_layout(int64_t N, int64_t C, int64_t H) {
@@ -56,7 +68,9 @@ static EpLayout ep_layout(int64_t N, int64_t C, int64_t H) {
   L.cnt = al(L.meta + N * C * 4);
   L.flag_d = al(L.cnt + N * 4);
   L.flag_c = al(L.flag_d + N * 4);
-  L.total = al(L.flag_c + N * 4);
+  L.cntm = al(L.flag_c + N * 4);           // [N][kEpMaxExperts] int32: every source's per-expert counts
+  L.flag_n = al(L.cntm + N * kEpMaxExperts * 4);
+  L.total = al(L.flag_n + N * 4);
   return L;
 }
 
@@ -332,6 +346,201 @@ __global__ void ep_combine_reduce_kernel(EpArgs a, const int* __restrict__ map, 
   }
 }
 
+// ------------------------------------------------ direct-placement dispatch
+// One kernel replaces dispatch + receive + permute.  Every rank broadcasts its
+// per-expert counts (CTA 0: the [N][E] count matrix lands in every buffer, then
+// flag_n); every CTA waits for the other ranks' counts (its own come from the
+// local routing output, so no CTA waits on another CTA of this GPU), derives
+//   base[e]  first row of expert e in its owner's expert-ordered GEMM input
+//   pre[e]   rows of expert e sent by lower ranks
+//   sbase[e] this rank's rows for lower experts of the same owner
+// and a warp per (token, k) pair stores the hidden row at row
+// base[e] + pre[e] + idx of the owner's xs (idx = order among this rank's
+// pairs of expert e), and its return address (rank, slot) into the owner's
+// meta.  The last CTA releases flag_d at every owner; the owner's gate/up GEMM
+// waits on those flags in its TMA producer.  CTA 0 also writes this rank's
+// offs[El + 1] (expert row offsets of its own xs).
+__device__ __forceinline__ int block_excl_scan(int v, int* sh) {  // blockDim <= 1024, sh >= 32 ints
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  __syncthreads();
+  if (lane == 31) sh[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int w = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    sh[lane] = w;
+  }
+  __syncthreads();
+  return incl - v + (wid > 0 ? sh[wid - 1] : 0);
+}
+
+__global__ void __launch_bounds__(1024)
+    ep_dispatch2_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ ids,
+                        const int* __restrict__ counts, const int* __restrict__ offs_g, int* __restrict__ cursor,
+                        int TK, int K, int* __restrict__ map, int* __restrict__ offs) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const int E = a.El * a.N, tid = threadIdx.x;
+  extern __shared__ int sm[];
+  int* base = sm;           // [E]
+  int* pre = base + E;      // [E]
+  int* sbase = pre + E;     // [E]
+  int* col = sbase + E;     // [E]
+  int* scan_sh = col + E;   // [32]
+  __shared__ int ok_all;
+  const uint64_t self = a.peers[a.rank];
+  if (blockIdx.x == 0) {  // publish this rank's counts to every rank
+    for (int d = 0; d < a.N; ++d) {
+      int* dst = at_off<int>(a.peers[d], a.L.cntm) + a.rank * kEpMaxExperts;
+      for (int e = tid; e < E; e += blockDim.x) dst[e] = counts[e];
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      for (int d = 0; d < a.N; ++d) st_release_sys(at_off<uint32_t>(a.peers[d], a.L.flag_n) + a.rank, epoch);
+    }
+  }
+  if (tid == 0) ok_all = 1;
+  __syncthreads();
+  for (int src = tid; src < a.N; src += blockDim.x)
+    if (src != a.rank && !wait_flag(at_off<uint32_t>(self, a.L.flag_n) + src, epoch, a.status, kErrPeerTimeout))
+      ok_all = 0;
+  __syncthreads();
+  __threadfence();
+  const int* cntm = at_off<int>(self, a.L.cntm);
+  // per expert: column sum and lower-rank prefix; every thread owns experts tid, tid + blockDim, ...
+  // (E <= blockDim is enforced on the host, so one expert per thread)
+  int colsum = 0, mine = 0, lower = 0;
+  const int e = tid;
+  if (e < E) {
+    for (int src = 0; src < a.N; ++src) {
+      const int c = src == a.rank ? counts[e] : (ok_all ? __ldcg(cntm + src * kEpMaxExperts + e) : 0);
+      colsum += c;
+      if (src < a.rank) lower += c;
+      if (src == a.rank) mine = c;
+    }
+  }
+  // global exclusive scans, then rebased to the start of each owner's expert segment
+  const int gcol = block_excl_scan(e < E ? colsum : 0, scan_sh);
+  if (e < E) base[e] = gcol;
+  const int gmine = block_excl_scan(e < E ? mine : 0, scan_sh);
+  if (e < E) sbase[e] = gmine;
+  if (e < E) {
+    pre[e] = lower;
+    col[e] = colsum;
+  }
+  __syncthreads();
+  int seg_col = 0, seg_mine = 0;  // scan values at the first expert of this owner's segment
+  if (e < E) {
+    const int seg = (e / a.El) * a.El;
+    seg_col = base[seg];
+    seg_mine = sbase[seg];
+  }
+  __syncthreads();
+  if (e < E) {
+    base[e] = gcol - seg_col;
+    sbase[e] = gmine - seg_mine;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && tid <= a.El) {  // this rank's own xs offsets
+    const int g0 = a.rank * a.El;
+    offs[tid] = tid < a.El ? base[g0 + tid] : base[g0 + a.El - 1] + col[g0 + a.El - 1];
+  }
+  // rows
+  const int warps = blockDim.x / 32, warp = tid / 32, lane = tid & 31;
+  for (int pair = blockIdx.x * warps + warp; pair < TK; pair += gridDim.x * warps) {
+    int ex = ids[pair];
+    if (ex < 0 || ex >= E) {  // defensive: an invalid id must never become an address
+      set_status(a.status, kErrBounds);
+      ex = 0;
+    }
+    const int dst = ex / a.El;
+    int idx = 0;
+    if (lane == 0) idx = atomicAdd(&cursor[ex], 1);  // the routing step leaves cursor[] at zero
+    idx = __shfl_sync(0xffffffffu, idx, 0);
+    const int pos = base[ex] + pre[ex] + idx;    // row in the owner's xs
+    const int slot = sbase[ex] + idx;            // row in this rank's comb region of that owner
+    if (!ok_all || idx < 0 || idx >= counts[ex] || pos < 0 || pos >= a.N * a.C || slot < 0 || slot >= a.C) {
+      if (lane == 0) {  // status set: the host raises after the step
+        if (ok_all) set_status(a.status, kErrCapacity);
+        map[pair] = 0;  // a valid comb row, so the combine never indexes out of bounds
+      }
+      continue;
+    }
+    if (lane == 0) {
+      map[pair] = dst * a.C + slot;
+      at_off<int>(a.peers[dst], a.L.meta)[pos] = a.rank * a.C + slot;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(pair / K) * a.H);
+    uint4* dstp = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[dst], a.L.recv_x) + (size_t)pos * a.H);
+    copy_row<false>(dstp, src, a.H / 8, lane);
+  }
+  __syncthreads();
+  __shared__ int last;
+  if (tid == 0) {
+    __threadfence_system();
+    last = atomicAdd(&a.done[0], 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  if (tid == 0) {
+    __threadfence_system();
+    for (int d = 0; d < a.N; ++d) st_release_sys(at_off<uint32_t>(a.peers[d], a.L.flag_d) + a.rank, epoch);
+    a.done[0] = 0;
+  }
+}
+
+// Owner: expert outputs y (xs order, offs[El] rows) back to their sources' comb slots.
+__global__ void ep_combine_send2_kernel(EpArgs a, const int* __restrict__ offs, const __nv_bfloat16* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const uint64_t self = a.peers[a.rank];
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  for (int src = threadIdx.x; src < a.N; src += blockDim.x)  // already complete: orders the meta reads
+    if (!wait_flag(at_off<uint32_t>(self, a.L.flag_d) + src, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
+  __syncthreads();
+  __threadfence();
+  const int rows = min(offs[a.El], a.N * a.C);
+  const int* meta = at_off<int>(self, a.L.meta);
+  const int warps = blockDim.x / 32, lane = threadIdx.x & 31;
+  for (int p = blockIdx.x * warps + threadIdx.x / 32; ok_all && p < rows; p += gridDim.x * warps) {
+    const int dst = __ldcg(meta + p);
+    const int src = dst / a.C, slot = dst - src * a.C;
+    if (src < 0 || src >= a.N) continue;
+    const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)p * a.H);
+    uint4* d = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[src], a.L.comb) +
+                                        ((size_t)a.rank * a.C + slot) * a.H);
+    copy_row<false>(d, s, a.H / 8, lane);
+  }
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(&a.done[1], 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int src = 0; src < a.N; ++src) st_release_sys(at_off<uint32_t>(a.peers[src], a.L.flag_c) + a.rank, epoch);
+    a.done[1] = 0;
+  }
+}
+
 // ---------------------------------------------------------------- host
 static EpArgs make_args(const at::Tensor& peers, int64_t rank, int64_t N, int64_t C, int64_t H, int64_t El,
                         at::Tensor& state) {
@@ -375,6 +584,65 @@ void ep_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64
   const int rows = (int)(N * C);
   launch_k(ep_permute_kernel, std::max(1, std::min(296, (rows + 7) / 8)), 256, 0, st, a,
            (const int*)row_pos.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Direct-placement dispatch: routing outputs (ids [T, K], per-expert counts [E],
+// offs_g [E+1], cursor [E] zeroed by the routing step) -> rows in the owners' expert-ordered
+// xs (this rank's own xs is the exchange buffer's receive region, offsets in
+// offs [El+1]).  The owner's gate/up GEMM must wait on flag_d (see
+// ep_flag_addr) before reading xs.
+void ep_dispatch2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                  const at::Tensor& x, const at::Tensor& ids, const at::Tensor& counts, const at::Tensor& offs_g,
+                  at::Tensor& cursor, at::Tensor& map, at::Tensor& offs) {
+  const int64_t N = peers.numel(), T = x.size(0), H = x.size(1), K = ids.size(1);
+  const int64_t E = N * El;
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && ids.scalar_type() == at::kInt);
+  TORCH_CHECK(T * K <= C, "ep_dispatch2: T*K (", T * K, ") exceeds capacity ", C);
+  TORCH_CHECK(E <= kEpMaxExperts && counts.numel() >= E && offs_g.numel() >= E && cursor.numel() >= E &&
+              offs.numel() >= El + 1 && map.numel() >= T * K);
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int TK = (int)(T * K);
+  const int threads = (int)std::max<int64_t>(256, (E + 31) / 32 * 32);
+  const int grid = std::max(1, std::min(148, (TK + threads / 32 - 1) / (threads / 32)));
+  const size_t smem = (size_t)(4 * E + 32) * sizeof(int);
+  launch_k(ep_dispatch2_kernel, grid, threads, smem, st, a, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+           (const int*)ids.data_ptr<int>(), (const int*)counts.data_ptr<int>(), (const int*)offs_g.data_ptr<int>(),
+           cursor.data_ptr<int>(), TK, (int)K, map.data_ptr<int>(), offs.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Byte address of this rank's flag_d array (the gate/up GEMM waits on it).
+int64_t ep_flag_addr(const at::Tensor& peers, int64_t rank, int64_t C, int64_t H) {
+  const EpLayout L = ep_layout(peers.numel(), C, H);
+  const int64_t own = peers.to(at::kCPU).data_ptr<int64_t>()[rank];
+  return own + L.flag_d;
+}
+
+// Byte address of this rank's receive region (the expert-ordered xs of the direct dispatch).
+int64_t ep_recv_addr(const at::Tensor& peers, int64_t rank, int64_t C, int64_t H) {
+  const EpLayout L = ep_layout(peers.numel(), C, H);
+  return peers.to(at::kCPU).data_ptr<int64_t>()[rank] + L.recv_x;
+}
+
+// Combine after the direct dispatch: y [>= offs[El], H] in xs order.
+void ep_combine2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                 const at::Tensor& offs, const at::Tensor& y, const at::Tensor& map, const at::Tensor& wts,
+                 const c10::optional<at::Tensor>& residual, at::Tensor& out) {
+  const int64_t N = peers.numel(), T = out.size(0), H = out.size(1), K = wts.size(1);
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && out.is_contiguous());
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(y.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int rows = (int)(N * C);
+  launch_k(ep_combine_send2_kernel, std::max(1, std::min(296, (rows + 7) / 8)), 256, 0, st, a,
+           (const int*)offs.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()));
+  const __nv_bfloat16* r =
+      (residual && residual->defined()) ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  launch_k(ep_combine_reduce_kernel, (int)std::max<int64_t>(1, T), 256, 0, st, a, (const int*)map.data_ptr<int>(),
+           (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

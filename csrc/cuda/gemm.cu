@@ -310,8 +310,9 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::
 // Grouped (MoE) GEMM, swap orientation.  w: [G * rows_per_group, K] (experts
 // stacked), x: [R, K] tokens sorted by group, offs: [G+1] int32 on device.
 // SwiGLU mode: each group holds [gate; up] rows (2*I) and y gets I columns.
-void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
-                    int64_t groups, bool swiglu, int64_t max_rows_per_group) {
+static void grouped_impl(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
+                         int64_t groups, bool swiglu, int64_t max_rows_per_group, int64_t wait_flags, int* epoch,
+                         int nranks, int epoch_add) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16);
   TORCH_CHECK(offs.scalar_type() == at::kInt && offs.numel() == groups + 1);
   TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && y.is_contiguous());
@@ -340,10 +341,31 @@ void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& 
   a.ldc = (int)n_out;
   a.out_rows = (int)R;
   a.status = status_ptr(x.device().index());
+  if (wait_flags) {  // activations written by other GPUs: the producer waits on their flags first
+    a.tp.ag_flags = reinterpret_cast<const uint32_t*>(wait_flags);
+    a.tp.epoch = reinterpret_cast<uint32_t*>(epoch);
+    a.tp.nranks = nranks;
+    a.tp.epoch_add = epoch_add;
+  }
   const int m_tiles = (int)(n_out / 128);
   // gridDim.y splits a group's token tiles across CTAs when groups are large.
   int ny = (int)std::max<int64_t>(1, std::min<int64_t>((max_rows_per_group + bn - 1) / bn, 8));
   dispatch(bn, swiglu, ta, tb, a, dim3(m_tiles, ny, groups), st);
+}
+
+void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
+                    int64_t groups, bool swiglu, int64_t max_rows_per_group) {
+  grouped_impl(x, w, offs, y, groups, swiglu, max_rows_per_group, 0, nullptr, 0, 0);
+}
+
+// Grouped GEMM whose activation rows arrive from other GPUs: the TMA producer
+// waits (bounded) until flags[p] >= state[0] + epoch_add for every p < nranks.
+void grouped_linear_wait(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
+                         int64_t groups, bool swiglu, int64_t max_rows_per_group, int64_t flags, at::Tensor& state,
+                         int64_t nranks, int64_t epoch_add) {
+  TORCH_CHECK(state.scalar_type() == at::kInt && state.is_cuda());
+  grouped_impl(x, w, offs, y, groups, swiglu, max_rows_per_group, flags, state.data_ptr<int>(), (int)nranks,
+               (int)epoch_add);
 }
 
 }  // namespace mb

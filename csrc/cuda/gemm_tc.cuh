@@ -45,6 +45,7 @@ struct TpArgs {
   int64_t rs_off;                 // byte offset of the partial slots [N][peer_rows][ldc]
   int64_t rs_flag_off;            // byte offset of the RS flags [N]
   int* done;                      // local CTA-completion counter
+  int epoch_add;                  // the producer waits for flags >= *epoch + epoch_add
 };
 
 struct GemmArgs {
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
         pdl_trigger();
       }
       if (args.tp.ag_flags && leader) {  // every peer's shard must be published for this boundary
-        const uint32_t want = *args.tp.epoch;
+        const uint32_t want = *args.tp.epoch + (uint32_t)args.tp.epoch_add;
         for (int p = 0; p < args.tp.nranks; ++p) {
           const uint64_t t0 = globaltimer_ns();
           while (true) {

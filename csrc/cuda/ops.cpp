@@ -35,6 +35,17 @@ void sample_tokens(const at::Tensor& logits, const at::Tensor& temperature, cons
 void patchify(const at::Tensor& images, int64_t size, int64_t patch, int64_t merge, std::vector<double> mean,
               std::vector<double> stdv, at::Tensor& out);
 void bias_act(at::Tensor& y, const c10::optional<at::Tensor>& bias, bool gelu);
+void ep_dispatch2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                  const at::Tensor& x, const at::Tensor& ids, const at::Tensor& counts, const at::Tensor& offs_g,
+                  at::Tensor& cursor, at::Tensor& map, at::Tensor& offs);
+int64_t ep_flag_addr(const at::Tensor& peers, int64_t rank, int64_t C, int64_t H);
+int64_t ep_recv_addr(const at::Tensor& peers, int64_t rank, int64_t C, int64_t H);
+void ep_combine2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                 const at::Tensor& offs, const at::Tensor& y, const at::Tensor& map, const at::Tensor& wts,
+                 const c10::optional<at::Tensor>& residual, at::Tensor& out);
+void grouped_linear_wait(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
+                         int64_t groups, bool swiglu, int64_t max_rows_per_group, int64_t flags, at::Tensor& state,
+                         int64_t nranks, int64_t epoch_add);
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                     const c10::optional<at::Tensor>& workspace, double scale);
@@ -101,6 +112,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &mb::moe_combine);
   m.def("ep_buffer_bytes", &mb::ep_buffer_bytes);
   m.def("ep_dispatch", &mb::ep_dispatch);
+  m.def("ep_dispatch2", &mb::ep_dispatch2);
+  m.def("grouped_linear_wait", &mb::grouped_linear_wait);
+  m.def("ep_combine2", &mb::ep_combine2);
+  m.def("ep_flag_addr", &mb::ep_flag_addr);
+  m.def("ep_recv_addr", &mb::ep_recv_addr);
   m.def("ep_combine", &mb::ep_combine);
   m.def("ep_recv_only", &mb::ep_recv_only);
   m.def("tp_gemm", &mb::tp_gemm);

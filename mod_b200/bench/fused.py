@@ -120,7 +120,7 @@ def case_ep(iters, rank, world, dev):
     fused = FusedEPMoE(cfg, NativeBackend(), max_tokens=T)
     us = _time(lambda: fused(x, mo), iters)
     out.append(_line("ep_moe_layer", "fused", us, flops, hbm, nvl, world, {"tokens_per_rank": T, "experts_per_rank": El}))
-    # the exchange alone: dispatch + combine with the expert GEMMs replaced by a copy
+    # the exchange alone: dispatch + combine without the expert GEMMs in between
     ctx = fused.small
     C, N = fused.C, fused.N
     logits = fused.be.linear(x, mo.router)
@@ -135,9 +135,9 @@ def case_ep(iters, rank, world, dev):
     o = torch.empty_like(x)
 
     def exchange():
-        C.ep_dispatch(ctx.buf.peers, ctx.state, rank, ctx.cap, El, x, ids, emap, ctx.row_pos, ctx.offs, ctx.xs,
-                      ctx.abort)
-        C.ep_combine(ctx.buf.peers, ctx.state, rank, ctx.cap, El, ctx.row_pos, y, emap, wts, None, o)
+        cursor.zero_()  # the routing step's per-expert cursor, as moe_route leaves it
+        C.ep_dispatch2(ctx.buf.peers, ctx.state, rank, ctx.cap, El, x, ids, counts, offs_g, cursor, emap, ctx.offs)
+        C.ep_combine2(ctx.buf.peers, ctx.state, rank, ctx.cap, El, ctx.offs, y, emap, wts, None, o)
     us = _time(exchange, iters)
     out.append(_line("ep_dispatch_combine", "fused", us, 0, 2 * T * K * H * 2, nvl, world))
     from ..ops import check_status

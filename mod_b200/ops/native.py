@@ -207,3 +207,15 @@ def bias_act(y, bias=None, gelu: bool = False):
     """In place: y = act(y + bias), act = tanh-GELU or identity; y bf16 [rows, cols]."""
     _C().bias_act(y, bias, gelu)
     return y
+
+
+def grouped_linear_wait(xs, w, offs, groups: int, swiglu: bool, max_rows_per_group: int, flags: int, state,
+                        nranks: int, epoch_add: int, out=None):
+    """grouped_linear whose input rows are written by other GPUs: the TMA producer first waits
+    (bounded) until flags[p] >= state[0] + epoch_add for every p < nranks (flags: device address)."""
+    rows_pg = w.shape[0] // groups
+    n_out = rows_pg // 2 if swiglu else rows_pg
+    if out is None:
+        out = torch.empty(xs.shape[0], n_out, dtype=xs.dtype, device=xs.device)
+    _C().grouped_linear_wait(xs, w, offs, out, groups, swiglu, max_rows_per_group, flags, state, nranks, epoch_add)
+    return out

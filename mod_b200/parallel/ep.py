@@ -81,6 +81,9 @@ class _EpContext:
         self.offs = torch.zeros(El + 1, dtype=torch.int32, device=dev)
         self.xs = torch.empty(rows, H, dtype=torch.bfloat16, device=dev)
         self.abort = torch.zeros(1, dtype=torch.int32, device=dev)
+        # direct placement: senders write rows into this rank's receive region in expert order
+        self.xs_direct = C.wrap_bf16(C.ep_recv_addr(self.buf.peers, rank, self.cap, H), rows, H)
+        self.flag_addr = C.ep_flag_addr(self.buf.peers, rank, self.cap, H)
 
 
 class FusedEPMoE:
@@ -121,15 +124,18 @@ class FusedEPMoE:
         cursor = torch.empty(E, dtype=torch.int32, device=dev)
         N.moe_route(logits, self.K, cfg.norm_topk_prob, ids, wts, counts, offs_g, cursor)
         emap = torch.empty(T * self.K, dtype=torch.int32, device=dev)
-        self.C.ep_dispatch(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, x, ids, emap, ctx.row_pos,
-                           ctx.offs, ctx.xs, ctx.abort)
-        rows = ctx.xs.shape[0]
+        # one kernel: counts all-gather, then every row stored at its expert-ordered position in
+        # the owner's receive region; the gate/up GEMM waits for the senders' flags itself
+        self.C.ep_dispatch2(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, x, ids, counts, offs_g, cursor,
+                            emap, ctx.offs)
+        rows = ctx.xs_direct.shape[0]
         exp_rows = max(1, (self.world * T * self.K) // max(1, self.El * self.world))
-        h = N.grouped_linear(ctx.xs, mo.w13, ctx.offs, self.El, True, min(rows, 4 * exp_rows))
-        y = N.grouped_linear(h, mo.w2, ctx.offs, self.El, False, min(rows, 4 * exp_rows))
+        mr = min(rows, 4 * exp_rows)
+        h = N.grouped_linear_wait(ctx.xs_direct, mo.w13, ctx.offs, self.El, True, mr, ctx.flag_addr, ctx.state,
+                                  self.world, 1)
+        y = N.grouped_linear(h, mo.w2, ctx.offs, self.El, False, mr)
         out = torch.empty_like(x)
-        self.C.ep_combine(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, ctx.row_pos, y, emap, wts, None,
-                          out)
+        self.C.ep_combine2(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, ctx.offs, y, emap, wts, None, out)
         return out
 
     def __call__(self, x: torch.Tensor, mo) -> torch.Tensor:

@@ -39,11 +39,13 @@ def run(rank, world, impl, port, device_kind):
         moe = NcclEPMoE(cfg, be)
     else:
         moe = FusedEPMoE(cfg, be, max_tokens=16)
+    scale = ref.float().abs().max().item()
+    assert scale > 0, "reference MoE output is all zeros"
     for rep in range(3):  # repeated calls exercise the epoch / buffer reuse
         out = moe(x, shard.layers[0].moe)
         err = (out.float() - ref.float()).abs().max().item()
-        tol = 1e-4 if dtype == torch.float32 else 3e-2
-        assert err < tol, f"rank {rank} rep {rep}: max err {err}"
+        tol = 1e-4 if dtype == torch.float32 else 3e-2  # relative to the output's magnitude
+        assert err < tol * scale, f"rank {rank} rep {rep}: max err {err} vs scale {scale}"
     if device_kind != "cpu":
         from mod_b200.ops import check_status
         torch.cuda.synchronize()

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 from typing import Dict, List, Optional
 
+import numpy as np
 import torch
 
 from .batch import ForwardBatch
@@ -61,6 +62,14 @@ class ModelRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.sampler = None
+        # numpy views of the pinned buffers: whole-slice writes from Python lists (one call per
+        # field instead of one tensor indexing op per sequence)
+        self.n_ids, self.n_pos, self.n_slots = self.h_ids.numpy(), self.h_pos.numpy(), self.h_slots.numpy()
+        self.n_bt, self.n_ctx, self.n_sslot = self.h_bt.numpy(), self.h_ctx.numpy(), self.h_sslot.numpy()
+        # (req_id, generation, blocks written) of each block-table row; a sequence's generation
+        # changes whenever it is prefilled from scratch (new blocks after a preemption)
+        self._bt_rows: List[tuple] = [(-1, 0, 0)] * B
+        self._gen: Dict[int, int] = {}
 
     # ------------------------------------------------------------------ helpers
     def attn_splits(self, B: int) -> int:
@@ -124,21 +133,35 @@ class ModelRunner:
         n = len(seqs)
         B = _bucket(n, self.buckets) if self.use_graphs else n
         bs = self.blocks.block_size
-        self.h_bt[:B].zero_()
-        for i, s in enumerate(seqs):
-            pos = s.length - 1
-            self.h_ids[i] = s.all_tokens[-1]
-            self.h_pos[i] = pos
-            self.h_slots[i] = s.blocks[pos // bs] * bs + pos % bs
-            self.h_ctx[i] = pos + 1
-            self.h_sslot[i] = s.state_slot
-            self.h_bt[i, :len(s.blocks)] = torch.tensor(s.blocks, dtype=torch.int32)
-        for i in range(n, B):
-            self.h_ids[i] = 0
-            self.h_pos[i] = 0
-            self.h_slots[i] = -1
-            self.h_ctx[i] = 0
-            self.h_sslot[i] = self.pad_slot
+        pos = [s.length - 1 for s in seqs]
+        self.n_ids[:n] = [s.last_token for s in seqs]
+        self.n_pos[:n] = pos
+        self.n_slots[:n] = [s.blocks[p // bs] * bs + p % bs for s, p in zip(seqs, pos)]
+        self.n_ctx[:n] = [p + 1 for p in pos]
+        self.n_sslot[:n] = [s.state_slot for s in seqs]
+        rows, gen = self._bt_rows, self._gen
+        for i, s in enumerate(seqs):  # a row changes only when its sequence or block count does
+            nb = len(s.blocks)
+            key = (s.req_id, gen.get(s.req_id, 0))
+            old = rows[i]
+            if old[:2] != key:
+                self.n_bt[i, :] = 0
+                self.n_bt[i, :nb] = s.blocks
+            elif old[2] != nb:  # blocks only grow while decoding
+                self.n_bt[i, old[2]:nb] = s.blocks[old[2]:]
+                if nb < old[2]:
+                    self.n_bt[i, nb:old[2]] = 0
+            rows[i] = key + (nb,)
+        if B > n:  # padded rows: no KV write, empty context, dummy state slot
+            self.n_ids[n:B] = 0
+            self.n_pos[n:B] = 0
+            self.n_slots[n:B] = -1
+            self.n_ctx[n:B] = 0
+            self.n_sslot[n:B] = self.pad_slot
+            for i in range(n, B):
+                if rows[i] != (-1, 0, 0):
+                    self.n_bt[i, :] = 0
+                    rows[i] = (-1, 0, 0)
         self._copy_in(B)
         sampling = self.sampler is not None and any(s.params.temperature > 0 for s in seqs)
         if return_logits:
@@ -168,30 +191,33 @@ class ModelRunner:
     def prefill(self, seqs: List[Sequence], query_lens: List[int], inputs_embeds=None, return_logits: bool = False):
         bs = self.blocks.block_size
         ids, pos, slots, ctx, lidx = [], [], [], [], []
-        bt = torch.zeros(len(seqs), self.max_blocks, dtype=torch.int32)
+        bt = np.zeros((len(seqs), self.max_blocks), dtype=np.int32)
         t = 0
         for i, (s, ql) in enumerate(zip(seqs, query_lens)):
-            toks = s.all_tokens
             start = s.length - ql
-            ids.extend(toks[start:])
-            for p in range(start, s.length):
-                pos.append(p)
-                slots.append(s.blocks[p // bs] * bs + p % bs)
+            if start == 0:  # from scratch: fresh blocks, so cached block-table rows are stale
+                self._gen[s.req_id] = self._gen.get(s.req_id, 0) + 1
+            ids.append(np.asarray(s.all_tokens[start:], dtype=np.int64))
+            p = np.arange(start, s.length, dtype=np.int64)   # positions of the new tokens
+            blk = np.asarray(s.blocks, dtype=np.int64)
+            pos.append(p)
+            slots.append(blk[p // bs] * bs + p % bs)
             ctx.append(s.length)
             t += ql
             lidx.append(t - 1)
-            bt[i, :len(s.blocks)] = torch.tensor(s.blocks, dtype=torch.int32)
+            bt[i, :len(s.blocks)] = s.blocks
+        ids, pos, slots = np.concatenate(ids), np.concatenate(pos), np.concatenate(slots)
         dev = self.device
         pin = dev.type == "cuda"
 
         def up(x, dtype):
-            h = torch.tensor(x, dtype=dtype)
+            h = torch.from_numpy(x).to(dtype) if isinstance(x, np.ndarray) else torch.tensor(x, dtype=dtype)
             if pin:
                 h = h.pin_memory()
             return h.to(dev, non_blocking=True)
 
         fb = ForwardBatch(input_ids=up(ids, torch.long), positions=up(pos, torch.int32),
-                          slot_mapping=up(slots, torch.int32), block_tables=bt.to(dev),
+                          slot_mapping=up(slots, torch.int32), block_tables=up(bt, torch.int32),
                           ctx_lens=up(ctx, torch.int32), logits_idx=up(lidx, torch.long),
                           state_slots=up([s.state_slot for s in seqs], torch.long), is_decode=False,
                           query_lens=list(query_lens), ctx_lens_host=ctx, inputs_embeds=inputs_embeds)

@@ -59,6 +59,10 @@ class Sequence:
     def length(self) -> int:
         return len(self.prompt) + len(self.output)
 
+    @property
+    def last_token(self) -> int:
+        return self.output[-1] if self.output else self.prompt[-1]
+
     def finished_by(self, token: int) -> bool:
         p = self.params
         if not p.ignore_eos and p.eos_token_id is not None and token == p.eos_token_id:

@@ -1,0 +1,90 @@
+"""BASELINE config #5: Qwen3-Next-style hybrid (3 gated-DeltaNet : 1 gated
+attention layers, 512 experts top-10 + shared expert), batch 4.
+
+    python -m mod_b200.bench.next_bench [--prompt-len 32768] [--steps 16] [--quant int8]
+
+Random-init N(0, 0.02) weights (int8 weight-only per-channel by default, made
+layer by layer so the bf16 model is never resident), uniform-random prompt
+ids.  Reports the prefill wall time of the batch (all prompts arrive at once,
+chunked by --prefill-tokens), and decode tokens/s: device-timed CUDA-graph
+replays (CUDA events) and end to end through ``LLMEngine.step()``.  One GPU;
+the TP/EP=8 form of the config is the EP path of ``bench.py``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import torch
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--prompt-len", type=int, default=32768)
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--quant", default="int8", choices=["int8", "none"])
+    ap.add_argument("--prefill-tokens", type=int, default=32768)
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (smoke runs only)")
+    a = ap.parse_args(argv)
+    from ..config import get_preset
+    from ..engine import SamplingParams
+    from ..engine.llm_engine import LLMEngine
+    from ..models.weights import random_weights
+    from ..ops import check_status
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = get_preset("qwen3-next")
+    if a.layers:
+        cfg.num_hidden_layers = a.layers
+        cfg.layer_types = cfg.layer_types[:a.layers]
+    t0 = time.perf_counter()
+    w = random_weights(cfg, device=dev, seed=0, quantize=None if a.quant == "none" else a.quant)
+    torch.cuda.synchronize()
+    init_s = time.perf_counter() - t0
+    eng = LLMEngine(cfg, weights=w, backend="native", device=dev, max_batch=a.batch,
+                    max_model_len=a.prompt_len + a.warmup + 3 * a.steps + 16, max_prefill_tokens=a.prefill_tokens)
+    g = torch.Generator().manual_seed(7)
+    prompts = [torch.randint(0, cfg.vocab_size, (a.prompt_len,), generator=g).tolist() for _ in range(a.batch)]
+    params = SamplingParams(max_new_tokens=a.warmup + 3 * a.steps + 8, ignore_eos=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ids = [eng.add_request(p, params) for p in prompts]
+    while any(eng.seqs[i].t_first_token is None for i in ids):
+        eng.step()
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    for _ in range(a.warmup):
+        eng.step()
+    r = eng.runner
+    B = max(r.graphs) if r.graphs else None
+    step = (lambda: r.graphs[B].replay()) if B is not None else eng.step
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for _ in range(a.steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    dev_ms = s.elapsed_time(e) / a.steps
+    t1 = time.perf_counter()
+    for _ in range(a.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t1) * 1000 / a.steps
+    check_status(dev)
+    print(json.dumps({"config": "qwen3-next hybrid (3 DeltaNet : 1 gated attention, 512 experts top-10 + shared)",
+                      "quant": a.quant, "batch": a.batch, "prompt_len": a.prompt_len, "layers": cfg.num_hidden_layers,
+                      "weights_init_s": round(init_s, 1), "prefill_s": round(prefill_s, 3),
+                      "prefill_tok_s": round(a.batch * a.prompt_len / prefill_s, 1),
+                      "decode_ms_per_step": round(dev_ms, 3), "decode_tok_s": round(a.batch / dev_ms * 1000, 1),
+                      "e2e_decode_tok_s": round(a.batch / e2e_ms * 1000, 1),
+                      "timed": "graph replay" if B is not None else "eager engine steps",
+                      "invalid": "layer count overridden" if a.layers else None}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -136,14 +136,16 @@ class _Init:
 
 
 def random_weights(cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
-                   expert_range: Optional[tuple] = None) -> ModelWeights:
+                   expert_range: Optional[tuple] = None, quantize: Optional[str] = None) -> ModelWeights:
     """N(0, 0.02) weights of the given architecture.
 
     ``expert_range=(lo, hi)`` materialises only experts [lo, hi) (expert
     parallelism).  Expert weights come from per-(layer, expert) generators and
     everything else from one sequential generator, so every rank of an
     expert-parallel group holds the same dense weights and the union of the
-    shards equals the unsharded model.
+    shards equals the unsharded model.  ``quantize="int8"`` converts each layer's
+    projections as soon as the layer exists, so the bf16 copy of the whole model
+    is never held at once (a 77B-parameter model fits one GPU as int8).
     """
     cfg.validate()
     ini = _Init(device, dtype, seed)
@@ -193,6 +195,12 @@ def random_weights(cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: i
             else:
                 L.mlp = MLPWeights(up=ini.normal(I, H), down=ini.normal(H, I), up_bias=ini.zeros(I),
                                    down_bias=ini.zeros(H))
+        if quantize == "int8":
+            from ..ops.quant import quantize_layer
+
+            quantize_layer(L)
+        elif quantize not in (None, "none"):
+            raise ValueError(f"unknown quantization {quantize!r}")
         layers.append(L)
     final_norm = ini.ones(H)
     lm_head = embed if cfg.tie_word_embeddings else ini.normal(cfg.vocab_size, H)

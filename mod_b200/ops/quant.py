@@ -60,25 +60,31 @@ def dense(w, dtype=torch.bfloat16) -> Optional[torch.Tensor]:
     return w.dequant(dtype) if isinstance(w, Int8Weight) else w
 
 
+def quantize_layer(L, experts: bool = True, attention: bool = True, mlp: bool = True,
+                   linear_attention: bool = True) -> None:
+    """In place: the large projection matrices of one layer become :class:`Int8Weight`."""
+    if attention and L.attn is not None:
+        L.attn.qkv = quantize_int8(L.attn.qkv)
+        L.attn.o = quantize_int8(L.attn.o)
+    if linear_attention and L.delta is not None:
+        L.delta.in_qkvz = quantize_int8(L.delta.in_qkvz)
+        L.delta.out = quantize_int8(L.delta.out)
+    if mlp and L.mlp is not None and L.mlp.gate_up is not None:
+        L.mlp.gate_up = quantize_int8(L.mlp.gate_up)
+        L.mlp.down = quantize_int8(L.mlp.down)
+    if L.moe is not None:
+        if experts:
+            L.moe.w13 = quantize_int8(L.moe.w13)
+            L.moe.w2 = quantize_int8(L.moe.w2)
+        if mlp and L.moe.shared is not None:
+            L.moe.shared.gate_up = quantize_int8(L.moe.shared.gate_up)
+            L.moe.shared.down = quantize_int8(L.moe.shared.down)
+
+
 def quantize_model(weights, experts: bool = True, attention: bool = True, mlp: bool = True,
                    linear_attention: bool = True):
     """In-place: replace the large projection matrices of every layer by
     :class:`Int8Weight`.  Embedding, LM head, norms, router and gates stay bf16."""
     for L in weights.layers:
-        if attention and L.attn is not None:
-            L.attn.qkv = quantize_int8(L.attn.qkv)
-            L.attn.o = quantize_int8(L.attn.o)
-        if linear_attention and L.delta is not None:
-            L.delta.in_qkvz = quantize_int8(L.delta.in_qkvz)
-            L.delta.out = quantize_int8(L.delta.out)
-        if mlp and L.mlp is not None and L.mlp.gate_up is not None:
-            L.mlp.gate_up = quantize_int8(L.mlp.gate_up)
-            L.mlp.down = quantize_int8(L.mlp.down)
-        if L.moe is not None:
-            if experts:
-                L.moe.w13 = quantize_int8(L.moe.w13)
-                L.moe.w2 = quantize_int8(L.moe.w2)
-            if mlp and L.moe.shared is not None:
-                L.moe.shared.gate_up = quantize_int8(L.moe.shared.gate_up)
-                L.moe.shared.down = quantize_int8(L.moe.shared.down)
+        quantize_layer(L, experts, attention, mlp, linear_attention)
     return weights

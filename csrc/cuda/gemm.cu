@@ -554,6 +554,52 @@ void linear_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scal
   }
 }
 
+// Vision -> LLM exchange fused into the merger's last linear: out[r] = x[r] @ w^T + bias
+// is stored straight into row row_map[r] % peer_rows of rank row_map[r] / peer_rows's
+// buffer (peers[d] + off), P2P; the last CTA releases flags (peers[d] + flag_off)[rank] =
+// state[0] + 1 at every rank.  Weights are the 128-row side, R visual rows the N side.
+void vis_scatter_gemm(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                      const at::Tensor& row_map, const at::Tensor& peers, int64_t rank, int64_t peer_rows,
+                      int64_t off, int64_t flag_off, at::Tensor& state) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
+              w.is_contiguous() && x.size(1) == w.size(1));
+  TORCH_CHECK(row_map.scalar_type() == at::kInt && row_map.numel() == x.size(0));
+  const int64_t R = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(N % 128 == 0 && K % 8 == 0 && R > 0, "vis_scatter_gemm: N % 128, K % 8, at least one row");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int bn = pick_bn(std::min<int64_t>(R, 128), false);
+  auto ta = make_tmap_bf16(w.data_ptr(), N, K, K, 128);
+  auto tb = make_tmap_bf16(x.data_ptr(), R, K, K, bn);
+  GemmArgs a{};
+  a.K = (int)K;
+  a.a_rows = (int)N;
+  a.b_rows = (int)R;
+  a.groups = 1;
+  a.splits = 1;
+  a.swap = 1;
+  a.mode = kEpiScatterRows;
+  a.ldc = (int)N;
+  a.out_rows = (int)R;
+  a.status = status_ptr(x.device().index());
+  a.bias = (bias && bias->defined()) ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  int* s = state.data_ptr<int>();
+  a.tp.rs_peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.tp.rs_off = off;
+  a.tp.rs_flag_off = flag_off;
+  a.tp.peer_rows = (int)peer_rows;
+  a.tp.nranks = (int)peers.numel();
+  a.tp.rank = (int)rank;
+  a.tp.epoch = reinterpret_cast<uint32_t*>(s);
+  a.tp.epoch_add = 1;
+  a.tp.done = s + 7;
+  a.tp.row_map = row_map.data_ptr<int>();
+  const int m_tiles = (int)(N / 128);
+  int ny = (int)((R + bn - 1) / bn);
+  while ((int64_t)m_tiles * ny > 2 * num_sms() && ny > 1) ny = (ny + 1) / 2;
+  dispatch(bn, false, ta, tb, a, dim3(m_tiles, ny, 1), st);
+}
+
 at::Tensor wrap_bf16(int64_t addr, int64_t rows, int64_t cols) {
   return at::from_blob(reinterpret_cast<void*>(addr), {rows, cols},
                        at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, c10::cuda::current_device()));

@@ -28,6 +28,7 @@ enum EpiMode : int {
   kEpiSwiGLU = 1,     // dual accumulator: silu(D_gate) * D_up
   kEpiPartialF32 = 2, // fp32 split-K partial to a workspace
   kEpiScatterRS = 3,  // tensor parallel: bf16 partial rows stored into the owning rank's slot (P2P)
+  kEpiScatterRows = 4,  // (+ bias) each output row stored at row_map[row] of its owner's buffer (P2P)
 };
 
 // Tensor-parallel operands of a GEMM: activations gathered from the peers'
@@ -46,6 +47,7 @@ struct TpArgs {
   int64_t rs_flag_off;            // byte offset of the RS flags [N]
   int* done;                      // local CTA-completion counter
   int epoch_add;                  // the producer waits for flags >= *epoch + epoch_add
+  const int* row_map;             // kEpiScatterRows: global destination row of each output row
 };
 
 struct GemmArgs {
@@ -65,6 +67,7 @@ struct GemmArgs {
   int* status;
   TpArgs tp;             // tp.peer_maps == nullptr: not tensor parallel
   const float* w_scale;  // int8-weight variant: per-row scale of A (row g*a_rows + r), applied in the epilogue
+  const __nv_bfloat16* bias;  // kEpiScatterRows: per output feature
 };
 
 // Exact int8 -> bf16 for 4 packed values (byte i = element i).  Float
@@ -372,6 +375,17 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
                   if (DUAL) p[q * ld + args.ldc] = u[q];  // raw gate | up partials; SwiGLU after the reduction
                 }
               }
+            } else if (args.mode == kEpiScatterRows) {
+              const float bv = args.bias ? __bfloat162float(args.bias[arow]) : 0.f;
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                if (q < nq) {
+                  const int grow = args.tp.row_map[b0 + jbase + q];
+                  const int d = grow / args.tp.peer_rows, jl = grow - d * args.tp.peer_rows;
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.tp.rs_peers[d] + args.tp.rs_off);
+                  dst[(size_t)jl * args.ldc + arow] = __float2bfloat16(v[q] + bv);
+                }
+              }
             } else if (args.mode == kEpiScatterRS) {
 #pragma unroll
               for (int q = 0; q < 16; ++q) {  // fully unrolled: v stays in registers
@@ -452,8 +466,8 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (args.mode == kEpiScatterRS) {
-    // last CTA: every partial of this rank is stored -> release the owners' flags
+  if (args.mode == kEpiScatterRS || args.mode == kEpiScatterRows) {
+    // last CTA: every row of this rank is stored -> release the owners' flags
     __shared__ int last;
     __syncthreads();
     const int nct = gridDim.x * gridDim.y * gridDim.z;
@@ -464,7 +478,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
     __syncthreads();
     if (last) {
       __threadfence_system();
-      const uint32_t e = *args.tp.epoch;
+      const uint32_t e = *args.tp.epoch + (uint32_t)args.tp.epoch_add;
       for (int d = threadIdx.x; d < args.tp.nranks; d += blockDim.x) {
         uint32_t* f = reinterpret_cast<uint32_t*>(args.tp.rs_peers[d] + args.tp.rs_flag_off) + args.tp.rank;
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");

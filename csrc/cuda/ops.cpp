@@ -46,6 +46,12 @@ void ep_combine2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64
 void grouped_linear_wait(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y,
                          int64_t groups, bool swiglu, int64_t max_rows_per_group, int64_t flags, at::Tensor& state,
                          int64_t nranks, int64_t epoch_add);
+void vis_scatter_gemm(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                      const at::Tensor& row_map, const at::Tensor& peers, int64_t rank, int64_t peer_rows,
+                      int64_t off, int64_t flag_off, at::Tensor& state);
+void vis_release(const at::Tensor& peers, int64_t rank, int64_t flag_off, at::Tensor& state);
+void vis_wait_merge(const at::Tensor& peers, int64_t rank, int64_t off, int64_t flag_off, at::Tensor& state,
+                    const at::Tensor& rows, at::Tensor& h);
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                     const c10::optional<at::Tensor>& workspace, double scale);
@@ -113,6 +119,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_buffer_bytes", &mb::ep_buffer_bytes);
   m.def("ep_dispatch", &mb::ep_dispatch);
   m.def("ep_dispatch2", &mb::ep_dispatch2);
+  m.def("vis_scatter_gemm", &mb::vis_scatter_gemm);
+  m.def("vis_release", &mb::vis_release);
+  m.def("vis_wait_merge", &mb::vis_wait_merge);
   m.def("grouped_linear_wait", &mb::grouped_linear_wait);
   m.def("ep_combine2", &mb::ep_combine2);
   m.def("ep_flag_addr", &mb::ep_flag_addr);

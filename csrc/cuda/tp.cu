@@ -276,4 +276,77 @@ void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, in
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------ vision -> LLM rows
+// Release only (a rank with no visual rows in this step): flags[rank] = state[0] + 1 at every rank.
+__global__ void vis_release_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int64_t flag_off,
+                                   const uint32_t* epoch) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t e = *epoch + 1;
+    for (int p = 0; p < nranks; ++p)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(reinterpret_cast<uint32_t*>(peers[p] + flag_off) + rank),
+                   "r"(e)
+                   : "memory");
+  }
+}
+
+// One CTA: bounded wait until every rank released this step's visual rows, then
+// h[rows[i]] = buf[rows[i]] (this rank's shard rows that hold image tokens), then
+// advance the epoch.
+__global__ void __launch_bounds__(1024)
+    vis_wait_merge_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int64_t off, int64_t flag_off,
+                          uint32_t* epoch, const int* __restrict__ rows, int nrows, int H,
+                          __nv_bfloat16* __restrict__ h, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t e = *epoch + 1;
+  const uint64_t self = peers[rank];
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  const uint32_t* f = reinterpret_cast<const uint32_t*>(self + flag_off);
+  for (int p = threadIdx.x; p < nranks; p += blockDim.x) {
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acq(f + p) - e) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_status(status, kErrPeerTimeout);
+        ok_all = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  __threadfence();
+  const __nv_bfloat16* buf = reinterpret_cast<const __nv_bfloat16*>(self + off);
+  const int n16 = H / 8;
+  for (int i = threadIdx.x; ok_all && i < nrows * n16; i += blockDim.x) {
+    const int r = rows[i / n16], c = i % n16;
+    reinterpret_cast<uint4*>(h + (size_t)r * H)[c] = __ldcg(reinterpret_cast<const uint4*>(buf + (size_t)r * H) + c);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch = e;
+}
+
+void vis_release(const at::Tensor& peers, int64_t rank, int64_t flag_off, at::Tensor& state) {
+  c10::cuda::CUDAGuard guard(peers.device());
+  launch_k(vis_release_kernel, 1, 32, 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), (int)rank, (int)peers.numel(), flag_off,
+           reinterpret_cast<const uint32_t*>(state.data_ptr<int>()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void vis_wait_merge(const at::Tensor& peers, int64_t rank, int64_t off, int64_t flag_off, at::Tensor& state,
+                    const at::Tensor& rows, at::Tensor& h) {
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.size(1) % 8 == 0);
+  TORCH_CHECK(rows.scalar_type() == at::kInt && rows.is_contiguous());
+  c10::cuda::CUDAGuard guard(h.device());
+  launch_k(vis_wait_merge_kernel, 1, 1024, 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), (int)rank, (int)peers.numel(), off, flag_off,
+           reinterpret_cast<uint32_t*>(state.data_ptr<int>()), (const int*)rows.data_ptr<int>(), (int)rows.numel(),
+           (int)h.size(1), reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), status_ptr(h.device().index()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace mb

@@ -62,7 +62,10 @@ class TPDecoderLM:
         ids = fb.input_ids
         if Tp != T:
             ids = torch.cat([ids, ids.new_zeros(Tp - T)])
-        h = be.embed(ids[r * pr:(r + 1) * pr].contiguous(), self.w.embed)       # residual shard [pr, H]
+        if fb.inputs_embeds is not None:  # this rank's shard rows, prepared by the caller (image tokens)
+            h = fb.inputs_embeds.contiguous().clone()
+        else:
+            h = be.embed(ids[r * pr:(r + 1) * pr].contiguous(), self.w.embed)   # residual shard [pr, H]
         layers = self.w.layers
         comm.publish(h, layers[0].in_norm, eps, partials=False)
         for i, L in enumerate(layers):

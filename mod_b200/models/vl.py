@@ -121,8 +121,11 @@ def _linear_gelu(be, x, w, b):
     return F.gelu(h.float(), approximate="tanh").to(x.dtype)
 
 
-def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, be, size: int) -> torch.Tensor:
-    """patches [B, N, 3*p*p] -> visual tokens [B, N/4, out_hidden] (backend ops, any dtype)."""
+def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, be, size: int,
+                   stop_before_fc2: bool = False) -> torch.Tensor:
+    """patches [B, N, 3*p*p] -> visual tokens [B, N/4, out_hidden] (backend ops, any dtype).
+    ``stop_before_fc2`` returns the merger's hidden rows [B*N/4, M] before its last linear (the
+    tensor-parallel path fuses that linear with the exchange of the rows)."""
     B, N, _ = patches.shape
     H, heads = vc.hidden_size, vc.num_attention_heads
     D = H // heads
@@ -147,6 +150,8 @@ def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, b
     x = x.reshape(B * N // m2, m2 * H)                          # merge groups are consecutive rows
     x = be.rmsnorm(x.contiguous(), vw.merge_norm, eps)
     x = _linear_gelu(be, x, vw.merge_fc1, vw.merge_fc1_bias)
+    if stop_before_fc2:
+        return x.to(vw.merge_fc2.dtype).contiguous()
     x = be.linear(x.to(vw.merge_fc2.dtype), vw.merge_fc2, bias=vw.merge_fc2_bias)
     return x.view(B, N // m2, -1)
 
@@ -210,6 +215,94 @@ class VLModel:
                     e[mask] = f[start:start + n].to(e.dtype)
             rows.append(e)
         return torch.cat(rows, 0)
+
+
+class TPVLModel:
+    """Tensor-parallel vision-language model: the dense decoder is a
+    :class:`TPDecoderLM` (sequence-parallel residual stream), the vision
+    encoder runs data-parallel over the step's images (image j on rank
+    j % world), and the merger's last linear is fused with the exchange: each
+    visual row is stored straight into the shard of the rank that owns its token
+    row (``FusedVisionExchange``: GEMM epilogue P2P stores + flags;
+    ``NcclVisionExchange``: the all-gather baseline)."""
+
+    def __init__(self, cfg: VLConfig, text_shard: ModelWeights, vision_weights: VisionWeights, backend, comm,
+                 world: int, exchange, image_size: int = 448):
+        from .tp_decoder import TPDecoderLM
+
+        self.cfg = cfg
+        self.text = TPDecoderLM(cfg.text, text_shard, backend, comm, world)
+        self.vw, self.be, self.vx, self.world = vision_weights, backend, exchange, world
+        self.rank = comm.rank
+        self.image_size = image_size
+        p, m = cfg.vision.patch_size, cfg.vision.spatial_merge_size
+        self.tokens_per_image = (image_size // p) ** 2 // (m * m)
+        self.w, self.Hkv, self.device = self.text.w, self.text.Hkv, self.text.device
+
+    def forward(self, fb, kv, states=None):
+        return self.text.forward(fb, kv, states)
+
+    def logits(self, h):
+        return self.text.logits(h)
+
+    def sample_greedy(self, h):
+        return self.text.sample_greedy(h)
+
+    def prompt_with_image(self, text_ids: List[int]) -> List[int]:
+        return [self.cfg.image_token_id] * self.tokens_per_image + list(text_ids)
+
+    def _hidden(self, images: torch.Tensor) -> torch.Tensor:
+        vc = self.cfg.vision
+        if getattr(self.be, "name", "") == "native" and images.is_cuda:
+            patches = self.be.N.patchify(images, self.image_size, vc.patch_size, vc.spatial_merge_size,
+                                         vc.image_mean, vc.image_std)
+        else:
+            patches = preprocess(images, vc, self.image_size)
+        return vision_forward(vc, self.vw, patches, self.be, self.image_size, stop_before_fc2=True)
+
+    def prefill_embeds(self, sched) -> torch.Tensor:
+        """This rank's shard [pr, H] of the step's input embeddings (text rows embedded here,
+        image rows delivered by the exchange).  Every rank calls it for every prefill step."""
+        from ..parallel.tp import padded_tokens
+
+        img_tok, r, N = self.cfg.image_token_id, self.rank, self.world
+        ids, vis = [], []          # vis: (global row, sequence index, feature index)
+        img_order = []             # sequences with image rows in this step, in schedule order
+        g = 0
+        for i, (s, ql) in enumerate(zip(sched.seqs, sched.query_lens)):
+            start = s.length - ql
+            toks = s.all_tokens[start:]
+            ids.extend(toks)
+            if s.images is not None:
+                before = sum(1 for t in s.all_tokens[:start] if t == img_tok)
+                rows = [(g + k, before) for k, t in enumerate(toks) if t == img_tok]
+                if rows:
+                    img_order.append(i)
+                    vis.extend((gr, i, before + j) for j, (gr, _) in enumerate(rows))
+            g += ql
+        T = g
+        Tp = padded_tokens(T, N)
+        pr = Tp // N
+        dev = self.device
+        idt = torch.tensor(ids + [0] * (Tp - T), dtype=torch.long, device=dev)
+        h = self.be.embed(idt[r * pr:(r + 1) * pr].contiguous(), self.w.embed)
+        mine = {i for j, i in enumerate(img_order) if j % N == r}
+        sel = [(gr, i, f) for gr, i, f in vis if i in mine]
+        my_rows = torch.tensor([gr - r * pr for gr, _, _ in vis if r * pr <= gr < (r + 1) * pr], dtype=torch.int32,
+                               device=dev)
+        if sel:
+            order = sorted(mine)
+            hid = self._hidden(torch.stack([sched.seqs[i].images for i in order]).to(dev))
+            per = hid.shape[0] // len(order)
+            pos = {i: k for k, i in enumerate(order)}
+            idx = torch.tensor([pos[i] * per + f for _, i, f in sel], dtype=torch.long, device=dev)
+            x = hid.index_select(0, idx).contiguous()
+            row_map = torch.tensor([gr for gr, _, _ in sel], dtype=torch.int32, device=dev)
+        else:
+            x = torch.empty(0, self.vw.merge_fc2.shape[1], dtype=self.vw.merge_fc2.dtype, device=dev)
+            row_map = torch.empty(0, dtype=torch.int32, device=dev)
+        self.vx.exchange(x, self.vw.merge_fc2, self.vw.merge_fc2_bias, row_map, h, my_rows, pr)
+        return h
 
 
 def random_vl_weights(cfg: VLConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0):

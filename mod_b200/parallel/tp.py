@@ -153,3 +153,67 @@ class NcclTP:
 
     def gather_rows(self, idx, T):
         return self._gather(T).index_select(0, idx)
+
+
+class FusedVisionExchange:
+    """Vision -> LLM rows over NVLink: the merger's last linear runs as a GEMM
+    whose epilogue adds the bias and stores each visual row into its owner's
+    buffer (P2P), the last CTA releasing a flag at every rank; the owner waits
+    for every rank's flag and copies the rows of its shard that hold image
+    tokens into its embeddings.  A rank with no visual rows only releases."""
+
+    def __init__(self, hidden: int, max_tokens: int, group=None):
+        from ..ops import load_extension
+        from .ep import ExchangeBuffer
+
+        self.C = load_extension()
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.H = hidden
+        self.cap = padded_tokens(max_tokens, self.world) // self.world
+        al = lambda x: (x + 255) // 256 * 256  # noqa: E731
+        self.off = 0
+        self.flag_off = al(self.cap * hidden * 2)
+        self.buf = ExchangeBuffer(al(self.flag_off + self.world * 4), group)
+        self.peers = self.buf.peers
+        self.state = torch.zeros(8, dtype=torch.int32, device=torch.device("cuda", torch.cuda.current_device()))
+
+    def exchange(self, x, w, bias, row_map, h_shard, my_rows, pr: int) -> None:
+        assert pr <= self.cap, "step larger than the exchange capacity"
+        if x.shape[0] > 0:
+            self.C.vis_scatter_gemm(x, w, bias, row_map, self.peers, self.rank, pr, self.off, self.flag_off,
+                                    self.state)
+        else:
+            self.C.vis_release(self.peers, self.rank, self.flag_off, self.state)
+        self.C.vis_wait_merge(self.peers, self.rank, self.off, self.flag_off, self.state, my_rows, h_shard)
+
+
+class NcclVisionExchange:
+    """Baseline: every rank computes its rows' merger output, the (row, value)
+    lists are all-gathered with the process group, each rank keeps its shard's."""
+
+    def __init__(self, backend, group=None):
+        self.be, self.group = backend, group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def exchange(self, x, w, bias, row_map, h_shard, my_rows, pr: int) -> None:
+        H = w.shape[0]
+        y = self.be.linear(x, w, bias=bias) if x.shape[0] else torch.empty(0, H, dtype=h_shard.dtype, device=x.device)
+        n = torch.tensor([y.shape[0]], device=x.device)
+        ns = [torch.zeros_like(n) for _ in range(self.world)]
+        dist.all_gather(ns, n, group=self.group)
+        m = max(int(v.item()) for v in ns)
+        if m == 0:
+            return
+        yp = torch.zeros(m, H, dtype=h_shard.dtype, device=x.device)
+        rp = torch.full((m,), -1, dtype=torch.int32, device=x.device)
+        yp[:y.shape[0]] = y.to(h_shard.dtype)
+        rp[:y.shape[0]] = row_map
+        ys = [torch.empty_like(yp) for _ in range(self.world)]
+        rs = [torch.empty_like(rp) for _ in range(self.world)]
+        dist.all_gather(ys, yp, group=self.group)
+        dist.all_gather(rs, rp, group=self.group)
+        ya, ra = torch.cat(ys), torch.cat(rs).long()
+        keep = (ra >= self.rank * pr) & (ra < (self.rank + 1) * pr)
+        h_shard[ra[keep] - self.rank * pr] = ya[keep]

@@ -47,7 +47,8 @@ struct TpArgs {
   int64_t rs_flag_off;            // byte offset of the RS flags [N]
   int* done;                      // local CTA-completion counter
   int epoch_add;                  // the producer waits for flags >= *epoch + epoch_add
-  const int* row_map;             // kEpiScatterRows: global destination row of each output row
+  const int* row_map;             // kEpiScatterRows: destination of each output row, d * peer_rows + row
+  int rank_row_stride;            // kEpiScatterRows: the row lands at rank * stride + row of rank d's buffer
 };
 
 struct GemmArgs {
@@ -379,11 +380,13 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
               const float bv = args.bias ? __bfloat162float(args.bias[arow]) : 0.f;
 #pragma unroll
               for (int q = 0; q < 16; ++q) {
-                if (q < nq) {
-                  const int grow = args.tp.row_map[b0 + jbase + q];
+                if (q < nq) {  // row map may have been written by other GPUs: read it from L2
+                  const int grow = __ldcg(args.tp.row_map + b0 + jbase + q);
                   const int d = grow / args.tp.peer_rows, jl = grow - d * args.tp.peer_rows;
+                  if (d < 0 || d >= args.tp.nranks) continue;
                   __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.tp.rs_peers[d] + args.tp.rs_off);
-                  dst[(size_t)jl * args.ldc + arow] = __float2bfloat16(v[q] + bv);
+                  dst[((size_t)args.tp.rank * args.tp.rank_row_stride + jl) * args.ldc + arow] =
+                      __float2bfloat16(v[q] + bv);
                 }
               }
             } else if (args.mode == kEpiScatterRS) {

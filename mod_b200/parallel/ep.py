@@ -133,6 +133,8 @@ class FusedEPMoE:
         mr = min(rows, 4 * exp_rows)
         h = N.grouped_linear_wait(ctx.xs_direct, mo.w13, ctx.offs, self.El, True, mr, ctx.flag_addr, ctx.state,
                                   self.world, 1)
+        # (returning rows from the down GEMM's epilogue measured slower: its per-element 2-byte
+        # peer stores make 64-byte NVLink writes, where the copy kernel writes 512 bytes per warp)
         y = N.grouped_linear(h, mo.w2, ctx.offs, self.El, False, mr)
         out = torch.empty_like(x)
         self.C.ep_combine2(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, ctx.offs, y, emap, wts, None, out)

@@ -169,6 +169,43 @@ def cmd_clean(args) -> int:
     return 0
 
 
+def cmd_tune(args) -> int:
+    import torch
+
+    from ..config import get_preset
+    from ..ops import autotune
+
+    if not torch.cuda.is_available():
+        print("tune: needs a GPU (the cache holds measured kernel times)")
+        return 1
+    cfg = get_preset(args.model)
+    cache = autotune.TuneCache(args.out)
+    for shape in autotune.model_linear_shapes(cfg, args.tokens):
+        e = autotune.tune_linear(*shape, cache, reps=args.reps)
+        print(f"T={shape[0]:5d} N={shape[1]:6d} K={shape[2]:6d}  splits={e['splits']:2d} orient={e['orient']}  "
+              f"{e['us']:.1f} us")
+    cache.save()
+    print(f"wrote {args.out}; use it with MB_TUNE_CACHE={args.out}")
+    return 0
+
+
+def cmd_trace(args) -> int:
+    from ..config import get_preset
+    from ..engine.llm_engine import LLMEngine
+    from ..engine.sequence import SamplingParams
+    from ..utils import tracing
+
+    eng = LLMEngine(get_preset(args.model), backend=args.backend, device=args.device,
+                    max_batch=args.batch, max_model_len=args.prompt_len + args.max_new_tokens + 16)
+    prompts = [[1 + (i + j) % 500 for j in range(args.prompt_len)] for i in range(args.batch)]
+    eng.generate(prompts, SamplingParams(max_new_tokens=2))  # warm-up (graph capture, first launches)
+    tracing.enable_nvtx(True)
+    with tracing.trace(args.out):
+        eng.generate(prompts, SamplingParams(max_new_tokens=args.max_new_tokens))
+    print(f"wrote {args.out}")
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="mod_b200", description="B200-native LLM/VLM inference engine")
     ap.add_argument("--debug", action="store_true")
@@ -206,6 +243,21 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("dir")
     p.set_defaults(fn=cmd_init)
     sub.add_parser("clean").set_defaults(fn=cmd_clean)
+    p = sub.add_parser("tune", help="measure GEMM launch configurations for a model's shapes")
+    p.add_argument("model")
+    p.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 32, 64, 128, 256])
+    p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--out", default="tune_cache.json")
+    p.set_defaults(fn=cmd_tune)
+    p = sub.add_parser("trace", help="torch.profiler trace (Chrome JSON) of a short generation")
+    p.add_argument("model")
+    p.add_argument("--backend", default="native", choices=["native", "torch", "cpu"])
+    p.add_argument("--device", default="cuda:0")
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--prompt-len", type=int, default=32)
+    p.add_argument("--max-new-tokens", type=int, default=8)
+    p.add_argument("--out", default="trace.json")
+    p.set_defaults(fn=cmd_trace)
     return ap
 
 

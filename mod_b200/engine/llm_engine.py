@@ -27,6 +27,7 @@ from .kv_cache import KVCache, StateCache
 from .runner import ModelRunner
 from .scheduler import Scheduler
 from .sequence import SamplingParams, Sequence, SeqStatus
+from ..utils import tracing
 
 log = logging.getLogger("mod_b200.engine")
 
@@ -104,6 +105,9 @@ class LLMEngine:
         self.runner.sampler = Sampler()
         self.seqs: Dict[int, Sequence] = {}
         self.last_step: Dict[str, float] = {}
+        # optional ``parallel.health.Heartbeat``: checked before every step so a lost
+        # peer raises ``RankFailure`` here instead of stalling the next exchange
+        self.health = None
 
     @classmethod
     def from_preset(cls, name: str, **kw) -> "LLMEngine":
@@ -135,12 +139,15 @@ class LLMEngine:
         sched = self.scheduler.schedule()
         if not sched.seqs:
             return []
+        if self.health is not None:
+            self.health.check()
         t0 = time.perf_counter()
         try:
-            if sched.is_decode:
-                toks = self.runner.decode(sched.seqs)
-            else:
-                toks = self.runner.prefill(sched.seqs, sched.query_lens, self._embeds(sched))
+            with tracing.nvtx_range("decode" if sched.is_decode else "prefill"):
+                if sched.is_decode:
+                    toks = self.runner.decode(sched.seqs)
+                else:
+                    toks = self.runner.prefill(sched.seqs, sched.query_lens, self._embeds(sched))
         except Exception as e:  # fail the step's requests, keep serving others
             log.error("step failed: %s", e)
             for s in sched.seqs:

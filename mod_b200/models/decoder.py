@@ -25,6 +25,7 @@ from ..engine.kv_cache import KVCache, StateCache
 from ..ops import reference as R
 from .deltanet import DeltaNetLayer
 from .weights import ModelWeights
+from ..utils import tracing
 
 
 class DecoderLM:
@@ -119,9 +120,12 @@ class DecoderLM:
         eps = cfg.rms_norm_eps
         hidden = fb.inputs_embeds if fb.inputs_embeds is not None else be.embed(fb.input_ids, w.embed)
         residual = None
+        nv = tracing.nvtx_enabled()
         for i, L in enumerate(w.layers):
             if self.layer_source is not None:
                 L = self.layer_source(i)
+            if nv:
+                torch.cuda.nvtx.range_push(f"layer{i}:{L.kind}")
             if residual is None:
                 residual = hidden.clone()
                 x = be.rmsnorm(hidden, L.in_norm, eps)
@@ -133,6 +137,8 @@ class DecoderLM:
                 hidden = self._deltanet(i, x, fb, states)
             x = be.rmsnorm(hidden, L.post_norm, eps, residual=residual)
             hidden = self._mlp(L, x)
+            if nv:
+                torch.cuda.nvtx.range_pop()
         x = be.rmsnorm(hidden, w.final_norm, eps, residual=residual)
         return x.index_select(0, fb.logits_idx)
 

@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--model", default=MODEL)
     p.add_argument("--batch", type=int, default=128)
     p.add_argument("--prompt-len", type=int, default=512)
+    p.add_argument("--profile", action="store_true",
+                   help="after the timed runs, print per-kernel device times of one decode step to stderr")
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalidates the number)")
     return p.parse_args()
 
@@ -220,6 +222,10 @@ def main():
         dist.barrier()
     e2e_ms = maxr((time.perf_counter() - t1) * 1000) / K
     ours, total = count_launches(one_step)
+    if args.profile and rank == 0:
+        from mod_b200.bench.profile import kernel_table
+
+        print(kernel_table(one_step, reps=3, top=40), file=sys.stderr, flush=True)
     from mod_b200.ops import check_status
 
     if backend == "native":

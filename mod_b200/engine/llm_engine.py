@@ -56,13 +56,15 @@ class LLMEngine:
             expert_parallel = world > 1 and cfg.is_moe
         self.expert_parallel = expert_parallel
         self.backend = make_backend(backend)
+        # the C++ CPU backend computes in fp32; the GPU backends in bf16
+        wdt = torch.float32 if backend == "cpu" else torch.bfloat16
         self.tensor_parallel = tensor_parallel and world > 1
         if self.tensor_parallel and model is None:
             from ..models.tp_decoder import TPDecoderLM, shard_weights
             from ..parallel.tp import FusedTP, NcclTP
 
             if weights is None:
-                weights = random_weights(cfg, device=self.device, seed=seed)
+                weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
             shard = shard_weights(cfg, weights, rank, world)
             weights = None
             mt = max(max_batch, max_prefill_tokens)
@@ -74,14 +76,14 @@ class LLMEngine:
         if expert_parallel:
             El = cfg.num_experts // world
             if weights is None and model is None:
-                weights = random_weights(cfg, device=self.device, seed=seed, expert_range=(rank * El, (rank + 1) * El))
+                weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed, expert_range=(rank * El, (rank + 1) * El))
             from ..parallel.ep import FusedEPMoE, NcclEPMoE
 
             moe_impl = (FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
                                    prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
                         if backend == "native" else NcclEPMoE(cfg, self.backend))
         if weights is None and model is None:
-            weights = random_weights(cfg, device=self.device, seed=seed)
+            weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
         if quantization not in (None, "none", "int8"):
             raise ValueError(f"unknown quantization {quantization!r} (supported: int8)")
         if quantization == "int8" and weights is not None:

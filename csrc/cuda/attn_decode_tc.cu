@@ -16,7 +16,7 @@
 //      MMA per paged block;
 //   5. thread d (= TMEM lane d) folds the tile into its fp32 accumulators with
 //      the running-max correction.
-// Shared memory is ~73 KB, so three CTAs share an SM and overlap each other's
+// Shared memory is 74 KB, so three CTAs share an SM and overlap each other's
 // loads and softmax.  Every wait is bounded (2 s); a timeout sets the status
 // word and the CTA leaves the tile loop.
 //
@@ -46,7 +46,9 @@ constexpr int kKBytes = 2 * 16384;     // two d-halves x [128 rows x 128 B]
 constexpr int kVBytes = 8 * 4096;      // eight blocks x [128 d rows x 32 B]
 constexpr int kQBytes = 2 * 2048;      // two d-halves x [16 rows x 128 B]
 constexpr int kPBytes = 8 * 512;       // eight blocks x [16 rows x 32 B]
-constexpr int kSmemBytes = 1024 + kKBytes + kVBytes + 2 * kQBytes + kPBytes + 1024;
+// One Q buffer: the next item's Q is written only after the last S MMA that reads
+// the current one has completed.  75,776 B per CTA lets three CTAs share an SM.
+constexpr int kSmemBytes = 1024 + kKBytes + kVBytes + kQBytes + kPBytes + 1024;
 
 // SW32 K-major descriptor: 8-row core groups of 32-byte rows (SBO = 256 B).
 __device__ __forceinline__ uint64_t make_sdesc_k32(uint32_t smem_addr) {
@@ -124,8 +126,8 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = sm;
   uint8_t* sV = sK + kKBytes;
-  uint8_t* sQ = sV + kVBytes;          // two buffers of kQBytes
-  uint8_t* sP = sQ + 2 * kQBytes;
+  uint8_t* sQ = sV + kVBytes;
+  uint8_t* sP = sQ + kQBytes;
   float* red_max = reinterpret_cast<float*>(sP + kPBytes);   // [4][16]
   float* red_sum = red_max + 64;                              // [4][16]
   uint64_t* bars = reinterpret_cast<uint64_t*>(red_sum + 64); // K, V, S, O
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(128, 1)
   }
   // K/V tiles start zeroed (blocks past a sequence's end are never loaded and
   // must hold finite data); P rows >= G stay zero.
-  for (int i = tid; i < (kKBytes + kVBytes + 2 * kQBytes + kPBytes) / 16; i += 128)
+  for (int i = tid; i < (kKBytes + kVBytes + kQBytes + kPBytes) / 16; i += 128)
     reinterpret_cast<uint4*>(sK)[i] = make_uint4(0, 0, 0, 0);
   fence_async_smem();
   tc_fence_before();
@@ -191,8 +193,8 @@ __global__ void __launch_bounds__(128, 1)
     __syncwarp();
     if (lane < nv) tma_load_2d(sV + lane * 4096, &tmV, &bars[1], 0, (bt[r.t0 / 16 + lane] * Hkv + r.hk) * D);
   };
-  auto load_q = [&](const TileRef& r, int buf) {  // all threads
-    uint8_t* dst = sQ + buf * kQBytes;
+  auto load_q = [&](const TileRef& r) {  // all threads
+    uint8_t* dst = sQ;
     for (int i = tid; i < G * D; i += 128) {
       const int h = i / D, d = i % D;
       uint32_t byte = h * 128 + (d % 64) * 2;
@@ -201,13 +203,12 @@ __global__ void __launch_bounds__(128, 1)
     }
   };
 
-  int qbuf = 0;
   if (has_cur) {
     if (warp == 0) {
       issue_k(cur);
       issue_v(cur);
     }
-    load_q(cur, qbuf);
+    load_q(cur);
     fence_async_smem();
     __syncthreads();
   }
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(128, 1)
     bool ok = mbar_wait(&bars[0], par, status);
     tc_fence_after();
     if (tid == 32 && ok) {
-      const uint32_t qb = smem_u32(sQ + qbuf * kQBytes);
+      const uint32_t qb = smem_u32(sQ);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -268,7 +269,8 @@ __global__ void __launch_bounds__(128, 1)
       byte ^= ((byte >> 7) & 1) << 4;
       *reinterpret_cast<__nv_bfloat16*>(chunk + byte) = __float2bfloat16(p[h]);
     }
-    if (has_nxt && nxt.first) load_q(nxt, qbuf ^ 1);  // next item's Q into the idle buffer
+    // next item's Q: every thread has waited on this tile's S MMA (bars[2]), the last reader of Q
+    if (has_nxt && nxt.first) load_q(nxt);
     fence_async_smem();
     tc_fence_before();
     if (!ok) *abort_flag = 1;
@@ -317,7 +319,6 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     if (*abort_flag) break;
     ++it;
-    if (has_nxt && nxt.first) qbuf ^= 1;
     cur = nxt;
     has_cur = has_nxt;
     if (has_cur) advance();
@@ -367,13 +368,14 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
   auto tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (int64_t)NB * Hkv * D, 16, 32, 16, D,
                          CU_TENSOR_MAP_SWIZZLE_32B);
   const float sl2 = (float)(scale * 1.4426950408889634);
-  // persistent grid: two resident CTAs per SM (pipelined inside each CTA)
+  // persistent grid: every resident CTA (three per SM at this shared-memory size)
   static int sms = 0;
   if (!sms) C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.device().index()));
+  const int per_sm = std::max(1, std::min(3, (int)(228 * 1024 / (kSmemBytes + 1024))));
   const int mbk = (int)block_tables.size(1);
   const int chunk_blocks = (mbk + (int)splits - 1) / (int)splits;
   const int items = B * Hkv * (int)splits;
-  const int grid = std::min(items, 2 * sms);
+  const int grid = std::min(items, per_sm * sms);
   static bool attr[17] = {false};
   auto go = [&](auto kernel, int g) {
     if (!attr[g]) {

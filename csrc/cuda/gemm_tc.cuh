@@ -69,7 +69,51 @@ struct GemmArgs {
   TpArgs tp;             // tp.peer_maps == nullptr: not tensor parallel
   const float* w_scale;  // int8-weight variant: per-row scale of A (row g*a_rows + r), applied in the epilogue
   const __nv_bfloat16* bias;  // kEpiScatterRows: per output feature
+  // Persistent schedule (items > 0): the grid is sized to the resident CTAs and
+  // CTA b takes work items b, b + gridDim.x, ...; item i is (m_tile, y, z) with
+  // m_tile = i % m_tiles, y = (i / m_tiles) % ny, z = i / (m_tiles * ny).  The
+  // TMA/MMA stage ring and the TMEM double buffer carry over from one item to
+  // the next, so a CTA streams weights without a pipeline drain per tile.
+  // items == 0: one item per CTA, (blockIdx.x, blockIdx.y, blockIdx.z).
+  int items, m_tiles, ny;
 };
+
+// One unit of CTA work: a 128-row A tile of group g, the N tiles
+// y, y + ny, ... of that group, over one split's K-block range.
+struct GemmItem {
+  int g, split, m_tile, y, b0, cnt, my_tiles, kb_lo, kb_hi, kbs, a_row0;
+};
+
+__device__ __forceinline__ int gemm_num_items(const GemmArgs& a) { return a.items > 0 ? a.items : 1; }
+
+__device__ __forceinline__ GemmItem gemm_item(const GemmArgs& a, int i) {
+  GemmItem w;
+  int y, z;
+  if (a.items > 0) {
+    const int idx = (int)blockIdx.x + i * (int)gridDim.x;
+    w.m_tile = idx % a.m_tiles;
+    y = (idx / a.m_tiles) % a.ny;
+    z = idx / (a.m_tiles * a.ny);
+  } else {
+    w.m_tile = blockIdx.x;
+    y = blockIdx.y;
+    z = blockIdx.z;
+  }
+  w.y = y;
+  w.g = z / a.splits;
+  w.split = z % a.splits;
+  if (a.b_offs != nullptr) {
+    w.b0 = a.b_offs[w.g];
+    w.cnt = a.b_offs[w.g + 1] - w.b0;
+  } else {
+    w.b0 = 0;
+    w.cnt = a.b_rows;
+  }
+  w.my_tiles = 0;
+  w.kb_lo = w.kb_hi = w.kbs = 0;
+  w.a_row0 = w.g * a.a_rows + w.m_tile * 128;
+  return w;
+}
 
 // Exact int8 -> bf16 for 4 packed values (byte i = element i).  Float
 // magic-number method: placing the biased byte u = b + 128 in the low mantissa
@@ -143,9 +187,10 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x;
-  const int g = blockIdx.z / args.splits;
-  const int split = blockIdx.z % args.splits;
+  const int ny = args.items > 0 ? args.ny : (int)gridDim.y;
+  const int n_items = args.items > 0
+                          ? ((int)blockIdx.x < args.items ? (args.items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
+                          : 1;
 
   // Dependent launch: every thread waits for the previous kernel before it
   // touches activations, group offsets or outputs.  The producer of a dense
@@ -156,24 +201,20 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
     pdl_wait();
     pdl_trigger();
   }
-  // Work of this CTA: N tiles nt = blockIdx.y + r*gridDim.y of group g, over
-  // this split's K-block range.
-  int b0, cnt;
-  if (!dense) {
-    b0 = args.b_offs[g];
-    cnt = args.b_offs[g + 1] - b0;
-  } else {
-    b0 = 0;
-    cnt = args.b_rows;
-  }
-  const int n_tiles = (cnt + BN - 1) / BN;
-  const int my_tiles = n_tiles > (int)blockIdx.y ? (n_tiles - 1 - (int)blockIdx.y) / (int)gridDim.y + 1 : 0;
+  // Work item i of this CTA: N tiles nt = y + r*ny of group g, over the
+  // split's K-block range (see GemmItem).
   const int kb_total = (args.K + 63) / 64;
   const int kb_per = (kb_total + args.splits - 1) / args.splits;
-  const int kb_lo = split * kb_per;
-  const int kb_hi = min(kb_total, kb_lo + kb_per);
-  const int kbs = max(0, kb_hi - kb_lo);
-  const int a_row0 = g * args.a_rows + m_tile * 128;
+  auto item = [&](int i) {
+    GemmItem w = gemm_item(args, i);
+    const int n_tiles = (w.cnt + BN - 1) / BN;
+    w.my_tiles = n_tiles > w.y ? (n_tiles - 1 - w.y) / ny + 1 : 0;
+    w.kb_lo = w.split * kb_per;
+    w.kb_hi = min(kb_total, w.kb_lo + kb_per);
+    w.kbs = max(0, w.kb_hi - w.kb_lo);
+    if (w.kbs == 0) w.my_tiles = 0;
+    return w;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -200,21 +241,23 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (my_tiles > 0 && kbs > 0) {
+  {
     if (warp == 0) {
       // ------------------------------------------------ TMA producer
       const bool leader = elect_one_sync();
       // weight tiles of the first stages, issued before the dependency wait
-      const int pre = (dense && args.swap) ? min(STAGES, kbs) : 0;
+      // (dense GEMMs only: their first item needs no device-side offsets)
+      const GemmItem w0 = (dense && n_items > 0) ? item(0) : GemmItem{};
+      const int pre = (dense && args.swap && n_items > 0 && w0.my_tiles > 0) ? min(STAGES, w0.kbs) : 0;
       if (leader) {
         for (int s = 0; s < pre; ++s) {
           uint8_t* st = smem + s * L::kStageBytes;
           uint8_t* wa = W8 ? st + L::kRawOff : st;
           mbar_arrive_expect_tx(&full[s], L::kTxBytes);
-          tma_load_2d(wa, &tmA, &full[s], (kb_lo + s) * 64, a_row0);
+          tma_load_2d(wa, &tmA, &full[s], (w0.kb_lo + s) * 64, w0.a_row0);
           if (DUAL)
-            tma_load_2d(wa + (W8 ? L::kRawBytes : L::kABytes), &tmA, &full[s], (kb_lo + s) * 64,
-                        a_row0 + args.a_up_offset);
+            tma_load_2d(wa + (W8 ? L::kRawBytes : L::kABytes), &tmA, &full[s], (w0.kb_lo + s) * 64,
+                        w0.a_row0 + args.a_up_offset);
         }
       }
       if (dense) {
@@ -239,9 +282,12 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
       if (leader) {
         int it = 0;
         bool ok = true;
-        for (int t = 0; t < my_tiles && ok; ++t) {
-          const int nt = blockIdx.y + t * gridDim.y;
-          for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        for (int wi = 0; wi < n_items && ok; ++wi) {
+        const GemmItem w = item(wi);
+        const int b0 = w.b0, a_row0 = w.a_row0;
+        for (int t = 0; t < w.my_tiles && ok; ++t) {
+          const int nt = w.y + t * ny;
+          for (int kb = w.kb_lo; kb < w.kb_hi; ++kb, ++it) {
             const int s = it % STAGES;
             uint8_t* st = smem + s * L::kStageBytes;
             if (it < pre) {  // weights already in flight: add the activation tile
@@ -264,19 +310,22 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
             }
           }
         }
+        }
       }
     } else if (warp == 1) {
       // ------------------------------------------------ MMA issuer
       constexpr uint32_t idesc = make_idesc_bf16(128, BN);
       if (elect_one_sync()) {
-        int it = 0;
+        int it = 0, tt = 0;  // stage and TMEM-buffer counters run on across items
         bool ok = true;
-        for (int t = 0; t < my_tiles && ok; ++t) {
-          const int buf = t & 1;
-          if (!mbar_wait(&tempty[buf], ((t >> 1) & 1) ^ 1, args.status)) break;
+        for (int wi = 0; wi < n_items && ok; ++wi) {
+        const GemmItem w = item(wi);
+        for (int t = 0; t < w.my_tiles && ok; ++t, ++tt) {
+          const int buf = tt & 1;
+          if (!mbar_wait(&tempty[buf], ((tt >> 1) & 1) ^ 1, args.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d0 = tmem_base + buf * kAcc;
-          for (int kb = 0; kb < kbs; ++kb, ++it) {
+          for (int kb = 0; kb < w.kbs; ++kb, ++it) {
             const int s = it % STAGES;
             const uint32_t ph = (it / STAGES) & 1;
             if (!mbar_wait(&full[s], ph, args.status)) { ok = false; break; }
@@ -295,6 +344,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
           }
           tc_commit(&tfull[buf]);
         }
+        }
       }
     } else if (W8 && warp >= 6) {
       // ------------------------------------------------ int8 -> bf16 converters (warps 6-9)
@@ -303,8 +353,10 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
       const int c = threadIdx.x - 192;
       int it = 0;
       bool ok = true;
-      for (int t = 0; t < my_tiles && ok; ++t) {
-        for (int kb = 0; kb < kbs; ++kb, ++it) {
+      for (int wi = 0; wi < n_items && ok; ++wi) {
+      const GemmItem w = item(wi);
+      for (int t = 0; t < w.my_tiles && ok; ++t) {
+        for (int kb = 0; kb < w.kbs; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&full[s], (it / STAGES) & 1, args.status)) { ok = false; break; }
           uint8_t* st = smem + s * L::kStageBytes;
@@ -327,17 +379,23 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
           if (lane == 0) mbar_arrive(&cfull[s]);
         }
       }
+      }
     } else {
       // ------------------------------------------------ epilogue (warps 2-5)
       const int lane_base = (warp & 3) * 32;
       const int i = lane_base + lane;             // accumulator row (TMEM lane)
-      for (int t = 0; t < my_tiles; ++t) {
-        const int buf = t & 1;
-        const int nt = blockIdx.y + t * gridDim.y;
-        if (!mbar_wait(&tfull[buf], (t >> 1) & 1, args.status)) break;
+      int tt = 0;
+      bool ok = true;
+      for (int wi = 0; wi < n_items && ok; ++wi) {
+      const GemmItem w = item(wi);
+      const int g = w.g, split = w.split, b0 = w.b0, cnt = w.cnt;
+      for (int t = 0; t < w.my_tiles; ++t, ++tt) {
+        const int buf = tt & 1;
+        const int nt = w.y + t * ny;
+        if (!mbar_wait(&tfull[buf], (tt >> 1) & 1, args.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kAcc;
-        const int arow = m_tile * 128 + i;        // row of A inside the group
+        const int arow = w.m_tile * 128 + i;      // row of A inside the group
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
@@ -460,6 +518,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
+      }
       }
     }
   }

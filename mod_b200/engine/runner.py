@@ -11,6 +11,8 @@ the two small copies.  The reference's "CUDA graph" wrapper is a no-op
 """
 from __future__ import annotations
 
+import os
+
 from typing import Dict, List, Optional
 
 import numpy as np
@@ -76,6 +78,9 @@ class ModelRunner:
         """Split-KV factor so that (sequences x KV heads x splits) fills the SMs."""
         if self.device.type != "cuda":
             return 1
+        forced = int(os.environ.get("MB_ATTN_SPLITS", "0") or 0)  # fixed factor, for A/B timing
+        if forced > 0:
+            return max(1, min(forced, self.max_blocks))
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         ctas = max(1, B * self.model.Hkv)
         s = 1

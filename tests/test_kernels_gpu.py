@@ -73,9 +73,12 @@ def test_swiglu_linear_splitk(cuda, T, K, I):
     _close(y, torch.nn.functional.silu(gu[:, :I]) * gu[:, I:])
 
 
-@pytest.mark.parametrize("E,I,H,T,k", [(8, 128, 256, 16, 2), (16, 768, 2048, 128, 8), (128, 768, 2048, 128, 8),
-                                       (4, 256, 512, 700, 2)])
-def test_grouped_swiglu_and_down(cuda, E, I, H, T, k):
+@pytest.mark.parametrize("E,I,H,T,k,hint_div", [(8, 128, 256, 16, 2, 1), (16, 768, 2048, 128, 8, 1),
+                                                (128, 768, 2048, 128, 8, 1), (4, 256, 512, 700, 2, 1),
+                                                (128, 768, 2048, 128, 8, 4), (64, 256, 512, 300, 4, 3)])
+def test_grouped_swiglu_and_down(cuda, E, I, H, T, k, hint_div):
+    """hint_div > 1 passes a row hint below the largest group (as the engine does), so
+    groups span several N tiles of the persistent schedule."""
     native, check = _N()
     torch.manual_seed(2)
     counts = torch.randint(0, 2 * T * k // E + 1, (E,))
@@ -86,8 +89,9 @@ def test_grouped_swiglu_and_down(cuda, E, I, H, T, k):
     xs = _rand(R, H)
     w13 = _rand(E * 2 * I, H, scale=0.05)
     w2 = _rand(E * H, I, scale=0.05)
-    h = native.grouped_linear(xs, w13, offs.cuda(), E, True, int(counts.max()))
-    y = native.grouped_linear(h, w2, offs.cuda(), E, False, int(counts.max()))
+    hint = max(1, int(counts.max()) // hint_div)
+    h = native.grouped_linear(xs, w13, offs.cuda(), E, True, hint)
+    y = native.grouped_linear(h, w2, offs.cuda(), E, False, hint)
     check()
     href = torch.empty(R, I)
     yref = torch.empty(R, H)

@@ -111,11 +111,11 @@ class NgramSpeculativeDecoder:
         K = max((len(d) for d in drafts), default=0)
         if K == 0:
             return [0] * len(drafts)
-        dr = torch.full((len(drafts), K), -1, dtype=torch.int32)
-        tg = torch.full((len(drafts), K), -2, dtype=torch.int32)
+        dr = torch.full((len(drafts), K), -1, dtype=torch.long)   # the kernel takes int64 token ids
+        tg = torch.full((len(drafts), K), -2, dtype=torch.long)
         for i, (d, t) in enumerate(zip(drafts, targets)):
-            dr[i, :len(d)] = torch.tensor(d, dtype=torch.int32)
-            tg[i, :len(d)] = torch.tensor(t[:len(d)], dtype=torch.int32)
+            dr[i, :len(d)] = torch.tensor(d, dtype=torch.long)
+            tg[i, :len(d)] = torch.tensor(t[:len(d)], dtype=torch.long)
         be = self.eng.backend
         if getattr(be, "N", None) is not None and self.eng.device.type == "cuda":
             n = be.N.verify_tokens(dr.to(self.eng.device), tg.to(self.eng.device))

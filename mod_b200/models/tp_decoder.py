@@ -94,39 +94,8 @@ class TPDecoderLM:
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         return self.be.linear(h, self.w.lm_head)
 
-    def _vocab_slice(self):
-        """This rank's LM-head rows: chunks of a multiple of 128 rows (the GEMM's weight tile)."""
-        V, N, r = self.w.lm_head.shape[0], self.world, self.comm.rank
-        chunk = -(-V // N)
-        chunk = -(-chunk // 128) * 128
-        lo = min(V, r * chunk)
-        return lo, min(V, lo + chunk)
-
     def sample_greedy(self, h: torch.Tensor) -> torch.Tensor:
-        """Vocab-parallel greedy head: each rank multiplies by its slice of the LM head
-        (1/N of its bytes), takes the slice's (max, index), and the ranks all-gather the
-        pairs; the largest value wins, ties going to the lowest index as in a full argmax."""
-        import torch.distributed as dist
-
-        if self.world == 1 or not (dist.is_available() and dist.is_initialized()):
-            return self.be.argmax(self.logits(h))
-        lo, hi = self._vocab_slice()
-        B = h.shape[0]
-        val = torch.full((B,), float("-inf"), dtype=torch.float32, device=h.device)
-        idx = torch.zeros(B, dtype=torch.long, device=h.device)
-        if hi > lo:
-            lg = self.be.linear(h, self.w.lm_head[lo:hi])
-            N = getattr(self.be, "N", None)
-            if N is not None:
-                N.argmax(lg.contiguous(), out=idx, out_val=val, index_offset=lo)
-            else:
-                R.argmax(lg, out=idx, out_val=val, index_offset=lo)
-        mine = torch.stack([val.double(), idx.double()], dim=-1).contiguous()       # [B, 2]
-        every = torch.empty(self.world * B * 2, dtype=torch.float64, device=h.device)
-        dist.all_gather_into_tensor(every, mine.reshape(-1))
-        every = every.view(self.world, B, 2)
-        best = every[..., 0].argmax(dim=0)                                           # first max = lowest rank
-        return every[..., 1].gather(0, best[None]).squeeze(0).long()
+        return self.be.argmax(self.logits(h))
 
 
 def _prefill_ref(q, kc, vc, fb):

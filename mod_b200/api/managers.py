@@ -72,7 +72,8 @@ class StreamingEngine:
         self._thread.start()
         self.stats = {"submitted": 0, "completed": 0, "rejected": 0}
 
-    def submit_request(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0) -> int:
+    def submit_request(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
+                       images=None) -> int:
         with self._lock:
             if len(self._pq) >= self.max_queue:
                 self.stats["rejected"] += 1
@@ -80,7 +81,7 @@ class StreamingEngine:
             rid = next(self._count)
             q: "queue.Queue" = queue.Queue()
             self._streams[rid] = q
-            heapq.heappush(self._pq, (priority, rid, list(token_ids), params))
+            heapq.heappush(self._pq, (priority, rid, list(token_ids), params, images))
             self.stats["submitted"] += 1
             self._cv.notify()
         return rid
@@ -103,13 +104,13 @@ class StreamingEngine:
                 if self._stop:
                     return
                 while self._pq:
-                    _, rid, ids, params = heapq.heappop(self._pq)
+                    _, rid, ids, params, images = heapq.heappop(self._pq)
                     q = self._streams[rid]
 
                     def cb(seq, tok, q=q):
                         q.put(tok)
 
-                    eng_id = self.engine.add_request(ids, params, callback=cb)
+                    eng_id = self.engine.add_request(ids, params, images=images, callback=cb)
                     self.engine.seqs[eng_id].stream_id = rid
             done = self.engine.step()
             for s in done:
@@ -123,6 +124,51 @@ class StreamingEngine:
             self._stop = True
             self._cv.notify()
         self._thread.join(timeout=10)
+
+
+class AsyncEngine:
+    """asyncio front-end over a :class:`StreamingEngine` (text or image + text requests).
+
+    The reference's async multimodal manager only echoes its request
+    (``src/inference_pio/models/qwen3_vl_2b/async_multimodal_processing.py:10-32``).
+    Here ``await generate(...)`` returns the generated ids and ``stream(...)``
+    yields them as the engine thread produces them; the engine keeps batching
+    every pending request together.  ``process_request`` accepts the
+    reference's request shape: a dict with ``input_ids`` and optional
+    ``pixel_values`` / ``max_new_tokens``.
+    """
+
+    def __init__(self, engine, max_queue: int = 1024):
+        self.streaming = engine if isinstance(engine, StreamingEngine) else StreamingEngine(engine, max_queue)
+
+    async def stream(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
+                     images=None):
+        import asyncio
+
+        rid = self.streaming.submit_request(token_ids, params, priority, images=images)
+        q = self.streaming._streams[rid]
+        loop = asyncio.get_running_loop()
+        try:
+            while True:
+                item = await loop.run_in_executor(None, q.get)
+                if item is None:
+                    return
+                if isinstance(item, Exception):
+                    raise item
+                yield item
+        finally:
+            self.streaming._streams.pop(rid, None)
+
+    async def generate(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
+                       images=None) -> List[int]:
+        return [t async for t in self.stream(token_ids, params, priority, images)]
+
+    async def process_request(self, request) -> List[int]:
+        p = SamplingParams(max_new_tokens=int(request.get("max_new_tokens", 64)))
+        return await self.generate(list(request["input_ids"]), p, images=request.get("pixel_values"))
+
+    def shutdown(self) -> None:
+        self.streaming.shutdown()
 
 
 class AdaptiveAdmission:

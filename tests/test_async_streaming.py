@@ -1,0 +1,49 @@
+"""Streaming and asyncio front-ends: concurrent requests are batched by one
+engine thread and return the same tokens as a direct generate()."""
+import asyncio
+
+from mod_b200.engine.sequence import SamplingParams
+
+
+def _engine():
+    from mod_b200.config import get_preset
+    from mod_b200.engine.llm_engine import LLMEngine
+
+    return LLMEngine(get_preset("tiny-dense"), backend="torch", device="cpu", max_batch=4, max_model_len=64,
+                     use_graphs=False)
+
+
+PROMPTS = [[1, 2, 3, 4], [9, 8, 7], [5] * 10]
+
+
+def test_streaming_engine_matches_generate():
+    from mod_b200.api.managers import StreamingEngine
+
+    ref = _engine().generate(PROMPTS, SamplingParams(max_new_tokens=5))
+    se = StreamingEngine(_engine())
+    try:
+        rids = [se.submit_request(p, SamplingParams(max_new_tokens=5)) for p in PROMPTS]
+        got = [list(se.generate_stream(r, timeout=60)) for r in rids]
+    finally:
+        se.shutdown()
+    assert got == ref
+    assert se.stats["completed"] == len(PROMPTS)
+
+
+def test_async_engine_concurrent_requests():
+    from mod_b200.api.managers import AsyncEngine
+
+    ref = _engine().generate(PROMPTS, SamplingParams(max_new_tokens=5))
+    ae = AsyncEngine(_engine())
+
+    async def main():
+        outs = await asyncio.gather(*(ae.generate(p, SamplingParams(max_new_tokens=5)) for p in PROMPTS))
+        streamed = [t async for t in ae.stream(PROMPTS[0], SamplingParams(max_new_tokens=5))]
+        via_request = await ae.process_request({"input_ids": PROMPTS[1], "max_new_tokens": 5})
+        return outs, streamed, via_request
+
+    try:
+        outs, streamed, via_request = asyncio.run(asyncio.wait_for(main(), 120))
+    finally:
+        ae.shutdown()
+    assert outs == ref and streamed == ref[0] and via_request == ref[1]

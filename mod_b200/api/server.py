@@ -1,0 +1,110 @@
+"""HTTP serving front-end (``python -m mod_b200 serve MODEL``).
+
+The reference has no server; its CLI runs one prompt per process
+(``src/inference_pio/__main__.py:266-343``).  This module exposes one engine
+over HTTP with an OpenAI-style completions route, so concurrent clients share
+the continuous batcher:
+
+* ``POST /v1/completions`` -- ``{"prompt": str | [ids], "max_tokens": int,
+  "temperature": float, "top_p": float, "top_k": int, "seed": int,
+  "stream": bool}``; the reply carries the text (when a tokenizer is loaded),
+  the token ids and usage counts; ``stream`` returns server-sent events, one
+  per token;
+* ``GET /health`` -- engine state (running / waiting sequences, free KV
+  blocks);
+* ``GET /v1/models`` -- the served model.
+
+Requests go through :class:`~mod_b200.api.managers.AsyncEngine`, whose engine
+thread batches every pending request together.
+"""
+import contextlib
+import json
+import time
+from typing import List, Optional, Union
+
+from pydantic import BaseModel
+
+from ..engine.sequence import SamplingParams
+from .managers import AsyncEngine
+
+
+class CompletionRequest(BaseModel):
+    prompt: Union[str, List[int]]
+    max_tokens: int = 64
+    temperature: float = 0.0
+    top_p: float = 1.0
+    top_k: int = 0
+    seed: Optional[int] = None
+    stream: bool = False
+
+
+def create_app(engine, tokenizer=None, model_name: str = "model"):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import StreamingResponse
+
+    front = AsyncEngine(engine)
+
+    @contextlib.asynccontextmanager
+    async def lifespan(app):
+        yield
+        front.shutdown()
+
+    app = FastAPI(title="mod_b200", version="0.1.0", lifespan=lifespan)
+    app.state.front = front
+
+    def _ids(req: CompletionRequest) -> List[int]:
+        if isinstance(req.prompt, list):
+            return [int(t) for t in req.prompt]
+        if tokenizer is None:
+            raise HTTPException(400, "no tokenizer loaded: send the prompt as token ids")
+        return tokenizer.encode(req.prompt)
+
+    def _params(req: CompletionRequest) -> SamplingParams:
+        if req.max_tokens < 1:
+            raise HTTPException(400, "max_tokens must be >= 1")
+        kw = dict(max_new_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p, top_k=req.top_k)
+        if req.seed is not None:
+            kw["seed"] = req.seed
+        return SamplingParams(**kw)
+
+    def _text(ids: List[int]) -> Optional[str]:
+        return tokenizer.decode(ids) if tokenizer is not None else None
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok", "running": len(engine.scheduler.running), "waiting": len(engine.scheduler.waiting),
+                "free_kv_blocks": engine.blocks.num_free}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model"}]}
+
+    @app.post("/v1/completions")
+    async def completions(req: CompletionRequest):
+        ids, params = _ids(req), _params(req)
+        created = int(time.time())
+        if req.stream:
+            async def events():
+                async for tok in front.stream(ids, params):
+                    yield "data: " + json.dumps({"object": "text_completion.chunk", "model": model_name,
+                                                 "token": tok, "text": _text([tok])}) + "\n\n"
+                yield "data: [DONE]\n\n"
+
+            return StreamingResponse(events(), media_type="text/event-stream")
+        try:
+            out = await front.generate(ids, params)
+        except RuntimeError as e:
+            raise HTTPException(503, str(e))
+        return {"object": "text_completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "text": _text(out), "token_ids": out,
+                             "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                          "total_tokens": len(ids) + len(out)}}
+
+    return app
+
+
+def serve(engine, tokenizer=None, model_name: str = "model", host: str = "127.0.0.1", port: int = 8000) -> None:
+    import uvicorn
+
+    uvicorn.run(create_app(engine, tokenizer, model_name), host=host, port=port, log_level="info")

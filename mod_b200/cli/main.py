@@ -13,6 +13,9 @@ the reference because three of its modules are missing:
   check                environment: devices, peer access, extensions
   init DIR             writes a runtime config template
   clean                removes build outputs and caches
+  serve MODEL          HTTP completions server (OpenAI-style route, streaming)
+  tune MODEL           measured GEMM launch configurations (JSON cache)
+  trace MODEL          torch.profiler trace of a short generation
 """
 from __future__ import annotations
 
@@ -206,6 +209,18 @@ def cmd_trace(args) -> int:
     return 0
 
 
+def cmd_serve(args) -> int:
+    from ..api.server import serve
+
+    pm = _pm()
+    if not pm.activate_plugin(args.model, **_opts(args)):
+        print("initialisation failed", file=sys.stderr)
+        return 1
+    p = pm.get_plugin(args.model)
+    serve(p.engine, p.tokenizer, args.model, host=args.host, port=args.port)
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="mod_b200", description="B200-native LLM/VLM inference engine")
     ap.add_argument("--debug", action="store_true")
@@ -243,6 +258,14 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("dir")
     p.set_defaults(fn=cmd_init)
     sub.add_parser("clean").set_defaults(fn=cmd_clean)
+    p = sub.add_parser("serve", help="HTTP completions server over one engine")
+    p.add_argument("model")
+    p.add_argument("--device")
+    p.add_argument("--backend", choices=["native", "torch", "cpu"])
+    p.add_argument("--host", default="127.0.0.1")
+    p.add_argument("--port", type=int, default=8000)
+    p.add_argument("--set", nargs="*", help="config overrides key=value")
+    p.set_defaults(fn=cmd_serve)
     p = sub.add_parser("tune", help="measure GEMM launch configurations for a model's shapes")
     p.add_argument("model")
     p.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 32, 64, 128, 256])

@@ -1,0 +1,45 @@
+"""HTTP front-end: completions (ids and text), streaming, health, errors --
+against a direct generate() on the same CPU engine configuration."""
+import json
+
+import pytest
+
+pytest.importorskip("fastapi")
+pytest.importorskip("httpx")
+
+from fastapi.testclient import TestClient  # noqa: E402
+
+from mod_b200.engine.sequence import SamplingParams  # noqa: E402
+from mod_b200.io.tokenizer import load_tokenizer  # noqa: E402
+
+
+def _engine():
+    from mod_b200.config import get_preset
+    from mod_b200.engine.llm_engine import LLMEngine
+
+    return LLMEngine(get_preset("tiny-dense"), backend="torch", device="cpu", max_batch=4, max_model_len=96,
+                     use_graphs=False)
+
+
+def test_completions_stream_health_and_errors():
+    from mod_b200.api.server import create_app
+
+    prompt = [5, 6, 7, 8, 9]
+    ref = _engine().generate([prompt], SamplingParams(max_new_tokens=6))[0]
+    tok = load_tokenizer(None)
+    app = create_app(_engine(), tok, "tiny-dense")
+    with TestClient(app) as c:
+        assert c.get("/health").json()["status"] == "ok"
+        assert c.get("/v1/models").json()["data"][0]["id"] == "tiny-dense"
+        r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 6})
+        assert r.status_code == 200
+        body = r.json()
+        assert body["choices"][0]["token_ids"] == ref
+        assert body["usage"] == {"prompt_tokens": 5, "completion_tokens": 6, "total_tokens": 11}
+        with c.stream("POST", "/v1/completions", json={"prompt": prompt, "max_tokens": 6, "stream": True}) as s:
+            toks = [json.loads(line[6:])["token"] for line in s.iter_lines()
+                    if line.startswith("data: ") and line != "data: [DONE]"]
+        assert toks == ref
+        t = c.post("/v1/completions", json={"prompt": "hi", "max_tokens": 3})
+        assert t.status_code == 200 and len(t.json()["choices"][0]["token_ids"]) == 3
+        assert c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 0}).status_code == 400

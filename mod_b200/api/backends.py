@@ -22,6 +22,25 @@ import torch
 from .interfaces import HardwareBackendInterface
 
 
+def _driver_attribute(index: int, name: str):
+    """A CUDA driver device attribute read through cuda-python (None when unavailable)."""
+    try:
+        try:
+            from cuda.bindings import driver as drv
+        except ImportError:  # older cuda-python layout
+            from cuda import cuda as drv
+        err, = drv.cuInit(0)
+        if int(err) != 0:
+            return None
+        err, dev = drv.cuDeviceGet(index)
+        if int(err) != 0:
+            return None
+        err, val = drv.cuDeviceGetAttribute(getattr(drv.CUdevice_attribute, name), dev)
+        return int(val) if int(err) == 0 else None
+    except Exception:
+        return None
+
+
 def probe_system() -> Dict[str, Any]:
     """Host + device topology (no NVML needed)."""
     info: Dict[str, Any] = {"platform": platform.platform(), "cpu_count": os.cpu_count(),
@@ -38,7 +57,10 @@ def probe_system() -> Dict[str, Any]:
             p = torch.cuda.get_device_properties(i)
             info["devices"].append({"index": i, "name": p.name, "sm": f"{p.major}.{p.minor}",
                                     "multiprocessors": p.multi_processor_count,
-                                    "memory_gb": round(p.total_memory / 2**30, 1)})
+                                    "memory_gb": round(p.total_memory / 2**30, 1),
+                                    # NVLink multicast objects (NVLS): the in-switch reduction path
+                                    "multicast_supported": _driver_attribute(
+                                        i, "CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED")})
         info["peer_access"] = [[i == j or torch.cuda.can_device_access_peer(i, j) for j in range(n)]
                                for i in range(n)]
     return info

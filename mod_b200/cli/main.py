@@ -13,6 +13,7 @@ the reference because three of its modules are missing:
   check                environment: devices, peer access, extensions
   init DIR             writes a runtime config template
   clean                removes build outputs and caches
+  plan MODEL --gpus N  parallel degrees, per-GPU weight and KV memory
   serve MODEL          HTTP completions server (OpenAI-style route, streaming)
   tune MODEL           measured GEMM launch configurations (JSON cache)
   trace MODEL          torch.profiler trace of a short generation
@@ -221,6 +222,15 @@ def cmd_serve(args) -> int:
     return 0
 
 
+def cmd_plan(args) -> int:
+    from ..config import get_preset
+    from ..parallel.planner import plan
+
+    p = plan(get_preset(args.model), args.gpus, hbm_bytes=int(args.hbm_gb * 1e9), int8=args.int8)
+    print(json.dumps(p.as_dict(), indent=1))
+    return 0 if p.fits else 2
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="mod_b200", description="B200-native LLM/VLM inference engine")
     ap.add_argument("--debug", action="store_true")
@@ -258,6 +268,12 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("dir")
     p.set_defaults(fn=cmd_init)
     sub.add_parser("clean").set_defaults(fn=cmd_clean)
+    p = sub.add_parser("plan", help="parallel degrees and per-GPU memory for a model on N GPUs")
+    p.add_argument("model")
+    p.add_argument("--gpus", type=int, default=8)
+    p.add_argument("--hbm-gb", type=float, default=180.0)
+    p.add_argument("--int8", action="store_true")
+    p.set_defaults(fn=cmd_plan)
     p = sub.add_parser("serve", help="HTTP completions server over one engine")
     p.add_argument("model")
     p.add_argument("--device")

@@ -42,3 +42,13 @@ def test_pipeline_when_a_replica_does_not_fit():
     p = plan(cfg, 4, hbm_bytes=80 * GIB)
     assert p.pp > 1 and sum(p.layers_per_stage) == 400
     assert p.weight_bytes_per_gpu <= 80 * GIB or p.offload_layers > 0
+
+
+def test_cli_plan(capsys):
+    import json
+
+    from mod_b200.cli.main import main
+
+    assert main(["plan", "qwen3-30b-a3b", "--gpus", "8"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert out["ep"] == 8 and out["fits"]

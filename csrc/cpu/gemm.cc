@@ -1,9 +1,10 @@
 // fp32 GEMM  y[M, N] = x[M, K] * w[N, K]^T  (both operands K-contiguous).
 //
-// Register-blocked dot-product kernel: a 4 x 4 tile of outputs keeps 16 AVX2
-// accumulators of 8 lanes each along K; the 8 loads per k-step (4 rows of x,
-// 4 rows of w) feed 16 FMAs.  OpenMP splits the tile grid; the single-row
-// case (decode GEMV, weight-bandwidth bound) splits N.
+// Register-blocked dot-product kernel: a 4 x 4 tile of outputs keeps 16
+// accumulators along K (AVX-512 where the CPU has it, chosen at run time: 16
+// lanes; else AVX2: 8 lanes); the 8 loads per k-step (4 rows of x, 4 rows of w)
+// feed 16 FMAs.  OpenMP splits the tile grid; the single-row case (decode GEMV,
+// weight-bandwidth bound) splits N.
 #include <immintrin.h>
 #include <omp.h>
 #include <algorithm>
@@ -45,6 +46,41 @@ static void tile(const float* x, const float* w, float* y, int64_t K, int64_t N,
     }
 }
 
+// AVX-512 tile of MR x NR outputs (32 vector registers: up to 24 accumulators plus the
+// operand loads).  Compiled for AVX-512 through the function's target attribute and
+// chosen at run time, so the library still loads on hosts without AVX-512.
+template <int MR, int NR>
+__attribute__((target("avx512f"))) static void tile512(const float* x, const float* w, float* y, int64_t K,
+                                                       int64_t N, int64_t m0, int mr, int64_t n0, int nr) {
+  __m512 acc[MR][NR];
+  for (int i = 0; i < MR; ++i)
+    for (int j = 0; j < NR; ++j) acc[i][j] = _mm512_setzero_ps();
+  const float* xr[MR];
+  const float* wr[NR];
+  for (int i = 0; i < MR; ++i) xr[i] = x + (m0 + (i < mr ? i : 0)) * K;
+  for (int j = 0; j < NR; ++j) wr[j] = w + (n0 + (j < nr ? j : 0)) * K;
+  int64_t k = 0;
+  for (; k + 16 <= K; k += 16) {
+    __m512 xv[MR];
+    for (int i = 0; i < MR; ++i) xv[i] = _mm512_loadu_ps(xr[i] + k);
+    for (int j = 0; j < NR; ++j) {
+      const __m512 wv = _mm512_loadu_ps(wr[j] + k);
+      for (int i = 0; i < MR; ++i) acc[i][j] = _mm512_fmadd_ps(xv[i], wv, acc[i][j]);
+    }
+  }
+  for (int i = 0; i < mr; ++i)
+    for (int j = 0; j < nr; ++j) {
+      float s = _mm512_reduce_add_ps(acc[i][j]);
+      for (int64_t kk = k; kk < K; ++kk) s += xr[i][kk] * wr[j][kk];
+      y[(m0 + i) * N + n0 + j] = s;
+    }
+}
+
+static bool has_avx512() {
+  static const bool v = __builtin_cpu_supports("avx512f");
+  return v;
+}
+
 static void gemv(const float* x, const float* w, float* y, int64_t K, int64_t N) {
 #pragma omp parallel for schedule(static)
   for (int64_t n0 = 0; n0 < N; n0 += 4) {
@@ -83,6 +119,21 @@ void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y) {
   }
   const int64_t MB = 64, NB = 64;
   const int64_t mt = (M + MB - 1) / MB, nt = (N + NB - 1) / NB;
+  if (has_avx512()) {
+    constexpr int TM = 4, TN = 4;  // 4 x 6 measured the same within noise; 4 x 4 held up better at K = 3072
+    const int64_t NB5 = 16 * TN;  // column block: a multiple of the tile width
+    const int64_t nt5 = (N + NB5 - 1) / NB5;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < mt; ++bi)
+      for (int64_t bj = 0; bj < nt5; ++bj) {
+        const int64_t m_end = std::min(M, (bi + 1) * MB), n_end = std::min(N, (bj + 1) * NB5);
+        for (int64_t n0 = bj * NB5; n0 < n_end; n0 += TN)
+          for (int64_t m0 = bi * MB; m0 < m_end; m0 += TM)
+            tile512<TM, TN>(px, pw, py, K, N, m0, (int)std::min<int64_t>(TM, m_end - m0), n0,
+                            (int)std::min<int64_t>(TN, n_end - n0));
+      }
+    return;
+  }
 #pragma omp parallel for collapse(2) schedule(dynamic, 1)
   for (int64_t bi = 0; bi < mt; ++bi)
     for (int64_t bj = 0; bj < nt; ++bj) {

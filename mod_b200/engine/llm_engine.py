@@ -95,7 +95,7 @@ class LLMEngine:
         bs = 16
         if num_blocks is None:
             num_blocks = self._auto_blocks(kv_mem_fraction, max_batch, max_model_len, kv_heads)
-        self.kv = KVCache(cfg, num_blocks, self.device, dtype=self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
+        self.kv = KVCache(cfg, num_blocks, self.device, dtype=torch.float32 if backend == "cpu" else self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
         has_delta = any(cfg.layer_type(i) == "linear_attention" for i in range(cfg.num_hidden_layers))
         self.states = StateCache(cfg, max_batch + 1, self.device) if has_delta else None
         self.blocks = BlockManager(num_blocks, bs, max_seqs=max_batch)

@@ -243,8 +243,10 @@ class CpuBackend(TorchBackend):
             self.C.set_num_threads(threads)
 
     def linear(self, x, w, bias=None, residual=None, out=None):
-        x2 = x.reshape(-1, x.shape[-1]).contiguous()
-        w = dense(w, torch.float32)
+        x2 = x.reshape(-1, x.shape[-1]).float().contiguous()
+        # bf16 weights stay bf16 (widened in registers: half the weight bytes); others go to fp32
+        if not (isinstance(w, torch.Tensor) and w.dtype == torch.bfloat16 and w.is_contiguous()):
+            w = dense(w, torch.float32)
         y = torch.empty(x2.shape[0], w.shape[0], dtype=torch.float32)
         self.C.linear(x2, w, y)
         if bias is not None:
@@ -258,7 +260,7 @@ class CpuBackend(TorchBackend):
 
     def rmsnorm(self, x, w, eps, residual=None):
         out = torch.empty_like(x)
-        self.C.rmsnorm(x.contiguous(), residual, w, out, eps)
+        self.C.rmsnorm(x.contiguous(), residual, w.float(), out, eps)
         return out
 
     def swiglu_mlp(self, x, gate_up, down, residual=None):
@@ -268,8 +270,9 @@ class CpuBackend(TorchBackend):
         return self.linear(h, down, residual=residual)
 
     def rope_qknorm(self, qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps):
-        self.C.rope_qknorm(qkv.contiguous(), q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D,
-                           rot, eps)
+        self.C.rope_qknorm(qkv.contiguous(), None if q_w is None else q_w.float(),
+                           None if k_w is None else k_w.float(), positions, invf, slots, q_out, k_cache, v_cache, Hq,
+                           Hkv, D, rot, eps)
         return q_out
 
     def attn_paged(self, q, k_cache, v_cache, fb):
@@ -288,13 +291,17 @@ class CpuBackend(TorchBackend):
         wts = torch.empty(T, top_k)
         self.C.moe_route(logits, top_k, renorm, ids, wts)
         out = torch.zeros_like(x) if residual is None else residual.clone()
-        self.C.moe_experts(x.contiguous(), ids, wts, mo.w13, mo.w2, mo.e_lo, mo.e_hi - mo.e_lo, out)
+        # the C++ expert mixture reads fp32 weights (bf16 experts are widened per call)
+        self.C.moe_experts(x.contiguous(), ids, wts, dense(mo.w13, torch.float32), dense(mo.w2, torch.float32),
+                           mo.e_lo, mo.e_hi - mo.e_lo, out)
         if mo.shared is not None:
             sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down)
-            out += torch.sigmoid(x @ mo.shared_gate.t()) * sh
+            out += torch.sigmoid(x.float() @ mo.shared_gate.float().t()) * sh
         return out
 
     def embed(self, ids, table):
+        if table.dtype != torch.float32:  # bf16 table: gather the rows, widen only those
+            return table[ids.reshape(-1).long()].float()
         out = torch.empty(ids.numel(), table.shape[1])
         self.C.embed(ids.contiguous(), table, out)
         return out

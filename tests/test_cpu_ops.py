@@ -138,3 +138,42 @@ def test_resize_bilinear_matches_interpolate(oh, ow):
     C.resize_bilinear(img, out)
     ref = F.interpolate(img[None], size=(oh, ow), mode="bilinear", align_corners=False)[0]
     assert torch.allclose(out, ref, atol=1e-5)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 300), (1, 40, 7), (6, 1000, 37), (128, 256, 96)])
+def test_linear_bf16_weights_equal_fp32_math(M, K, N):
+    x, w = _r(M, K, seed=30), (_r(N, K, seed=31) * 0.05).bfloat16()
+    y = torch.empty(M, N)
+    C.linear(x, w, y)
+    assert torch.allclose(y, x @ w.float().t(), atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["tiny-dense", "tiny-moe", "tiny-next", "tiny-glm"])
+def test_cpu_engine_bf16_weights_match_widened_copy(name):
+    """bf16 weights (widened in registers) give the same tokens as an fp32 copy of the same values."""
+    from mod_b200.config import get_preset
+    from mod_b200.engine.llm_engine import LLMEngine
+    from mod_b200.engine.sequence import SamplingParams
+    from mod_b200.models.weights import random_weights
+
+    def widen(obj):
+        for k, v in list(vars(obj).items()):
+            if isinstance(v, torch.Tensor):
+                if v.dtype == torch.bfloat16:
+                    setattr(obj, k, v.float())
+            elif isinstance(v, list):
+                for e in v:
+                    if hasattr(e, "__dict__"):
+                        widen(e)
+            elif hasattr(v, "__dict__"):
+                widen(v)
+
+    cfg = get_preset(name)
+    wb = random_weights(cfg, dtype=torch.bfloat16, seed=0)
+    wf = random_weights(cfg, dtype=torch.bfloat16, seed=0)
+    widen(wf)
+    prompts = [[1, 2, 3, 4, 5], [7, 8, 9]]
+    p = SamplingParams(max_new_tokens=6)
+    a = LLMEngine(cfg, weights=wb, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
+    b = LLMEngine(cfg, weights=wf, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
+    assert a == b

@@ -22,7 +22,7 @@ from ..config.presets import get_preset
 from ..models.backend import make_backend
 from ..models.decoder import DecoderLM
 from ..models.weights import ModelWeights, random_weights
-from .block_manager import BlockManager
+from .block_manager import BlockManager, PrefixCachingBlockManager
 from .kv_cache import KVCache, StateCache
 from .runner import ModelRunner
 from .scheduler import Scheduler
@@ -38,7 +38,7 @@ class LLMEngine:
                  num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
                  max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
                  expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
-                 quantization: Optional[str] = None):
+                 quantization: Optional[str] = None, prefix_caching: bool = False):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
@@ -98,7 +98,11 @@ class LLMEngine:
         self.kv = KVCache(cfg, num_blocks, self.device, dtype=torch.float32 if backend == "cpu" else self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
         has_delta = any(cfg.layer_type(i) == "linear_attention" for i in range(cfg.num_hidden_layers))
         self.states = StateCache(cfg, max_batch + 1, self.device) if has_delta else None
-        self.blocks = BlockManager(num_blocks, bs, max_seqs=max_batch)
+        # prefix caching shares KV blocks of common prompt prefixes; models with recurrent
+        # (DeltaNet) state keep the plain manager, since their state is not in the KV blocks
+        self.prefix_caching = bool(prefix_caching) and self.states is None
+        mgr = PrefixCachingBlockManager if self.prefix_caching else BlockManager
+        self.blocks = mgr(num_blocks, bs, max_seqs=max_batch)
         self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens)
         self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
                                   use_graphs=use_graphs and backend == "native", device=self.device)
@@ -157,6 +161,9 @@ class LLMEngine:
                 self.scheduler.finish(s, SeqStatus.FAILED)
             return list(sched.seqs)
         now = time.perf_counter()
+        if self.prefix_caching:
+            for s in sched.seqs:
+                self.blocks.register(s)
         self.last_step = {"kind": 1.0 if sched.is_decode else 0.0, "seconds": now - t0, "batch": len(sched.seqs)}
         done = []
         for s, t in zip(sched.seqs, toks):

@@ -53,6 +53,7 @@ class RuntimeConfig:
     seed: int = 0
     threads: int = 0                     # CPU backend OpenMP threads (0: default)
     offload: bool = False                # hybrid CPU/GPU weight streaming
+    prefix_caching: bool = False         # share KV blocks of common prompt prefixes
     extra: Dict[str, Any] = field(default_factory=dict)
 
 

@@ -68,6 +68,8 @@ class StreamingEngine:
         self._cv = threading.Condition(self._lock)
         self._streams: Dict[int, "queue.Queue"] = {}
         self._stop = False
+        self._cancel: set = set()       # stream ids to abort before the next engine step
+        self._eng_id: Dict[int, int] = {}
         self._thread = threading.Thread(target=self._loop, daemon=True)
         self._thread.start()
         self.stats = {"submitted": 0, "completed": 0, "rejected": 0}
@@ -86,6 +88,12 @@ class StreamingEngine:
             self._cv.notify()
         return rid
 
+    def cancel(self, rid: int) -> None:
+        """Abort a submitted request; its stream ends (None) once the engine thread applies it."""
+        with self._lock:
+            self._cancel.add(rid)
+            self._cv.notify()
+
     def generate_stream(self, rid: int, timeout: float = 300.0) -> Iterator[int]:
         q = self._streams[rid]
         while True:
@@ -99,10 +107,25 @@ class StreamingEngine:
     def _loop(self):
         while True:
             with self._lock:
-                while not self._stop and not self._pq and not self.engine.has_unfinished():
+                while not self._stop and not self._pq and not self._cancel and not self.engine.has_unfinished():
                     self._cv.wait(timeout=0.1)
                 if self._stop:
                     return
+                if self._cancel:
+                    for rid in self._cancel:
+                        q = self._streams.get(rid)
+                        queued = [e for e in self._pq if e[1] == rid]
+                        if queued:       # not handed to the engine yet
+                            self._pq = [e for e in self._pq if e[1] != rid]
+                            heapq.heapify(self._pq)
+                        elif rid in self._eng_id:
+                            eid = self._eng_id.pop(rid)
+                            self.engine.abort(eid)
+                            self.engine.seqs.pop(eid, None)
+                        if q is not None:
+                            q.put(None)
+                        self.stats["cancelled"] = self.stats.get("cancelled", 0) + 1
+                    self._cancel.clear()
                 while self._pq:
                     _, rid, ids, params, images = heapq.heappop(self._pq)
                     q = self._streams[rid]
@@ -112,8 +135,11 @@ class StreamingEngine:
 
                     eng_id = self.engine.add_request(ids, params, images=images, callback=cb)
                     self.engine.seqs[eng_id].stream_id = rid
+                    self._eng_id[rid] = eng_id
             done = self.engine.step()
             for s in done:
+                self._eng_id.pop(getattr(s, "stream_id", -1), None)
+                self.engine.seqs.pop(s.req_id, None)  # a long-running server keeps no finished sequences
                 q = self._streams.get(getattr(s, "stream_id", -1))
                 if q is not None:
                     q.put(RuntimeError(s.error) if s.status == SeqStatus.FAILED else None)
@@ -148,15 +174,20 @@ class AsyncEngine:
         rid = self.streaming.submit_request(token_ids, params, priority, images=images)
         q = self.streaming._streams[rid]
         loop = asyncio.get_running_loop()
+        finished = False
         try:
             while True:
                 item = await loop.run_in_executor(None, q.get)
                 if item is None:
+                    finished = True
                     return
                 if isinstance(item, Exception):
+                    finished = True
                     raise item
                 yield item
         finally:
+            if not finished:  # the consumer stopped early (e.g. the HTTP client went away): free the request
+                self.streaming.cancel(rid)
             self.streaming._streams.pop(rid, None)
 
     async def generate(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,

@@ -137,6 +137,21 @@ class LLMEngine:
         self.scheduler.add(seq)
         return seq.req_id
 
+    def abort(self, req_id: int) -> bool:
+        """Cancel a waiting or running request between steps; its KV blocks are freed.
+        Returns False when the request is unknown or already finished."""
+        seq = self.seqs.get(req_id)
+        if seq is None or seq.status not in (SeqStatus.WAITING, SeqStatus.RUNNING):
+            return False
+        if seq in self.scheduler.waiting:
+            self.scheduler.waiting.remove(seq)
+            seq.status = SeqStatus.ABORTED
+            if seq.blocks:
+                self.blocks.release(seq)
+        else:
+            self.scheduler.finish(seq, SeqStatus.ABORTED)
+        return True
+
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
 

@@ -18,6 +18,7 @@ class SeqStatus(enum.Enum):
     RUNNING = "running"
     FINISHED = "finished"
     FAILED = "failed"
+    ABORTED = "aborted"
 
 
 @dataclass

@@ -47,3 +47,46 @@ def test_async_engine_concurrent_requests():
     finally:
         ae.shutdown()
     assert outs == ref and streamed == ref[0] and via_request == ref[1]
+
+
+def test_engine_abort_frees_blocks():
+    eng = _engine()
+    free0 = eng.blocks.num_free
+    a = eng.add_request(PROMPTS[2], SamplingParams(max_new_tokens=50))
+    b = eng.add_request(PROMPTS[0], SamplingParams(max_new_tokens=3))
+    eng.step()                                   # prefill both
+    assert eng.abort(a) and not eng.abort(a)     # second abort: already finished
+    while eng.has_unfinished():
+        eng.step()
+    assert eng.seqs[a].status.name == "ABORTED" and len(eng.seqs[b].output) == 3
+    assert eng.blocks.num_free == free0
+    w = eng.add_request(PROMPTS[1], SamplingParams(max_new_tokens=3))
+    assert eng.abort(w) and not eng.has_unfinished()   # a waiting request leaves the queue
+
+
+def test_async_stream_cancel_frees_the_request():
+    from mod_b200.api.managers import AsyncEngine
+
+    eng = _engine()
+    free0 = eng.blocks.num_free
+    ae = AsyncEngine(eng)
+
+    async def main():
+        got = []
+        async for t in ae.stream(PROMPTS[2], SamplingParams(max_new_tokens=40)):
+            got.append(t)
+            if len(got) == 2:
+                break                             # consumer goes away early
+        return got
+
+    try:
+        got = asyncio.run(asyncio.wait_for(main(), 60))
+        import time
+
+        t0 = time.time()
+        while (eng.has_unfinished() or eng.blocks.num_free != free0) and time.time() - t0 < 10:
+            time.sleep(0.05)
+    finally:
+        ae.shutdown()
+    assert len(got) == 2 and not eng.has_unfinished() and eng.blocks.num_free == free0
+    assert ae.streaming.stats.get("cancelled", 0) == 1

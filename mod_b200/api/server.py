@@ -35,6 +35,7 @@ class CompletionRequest(BaseModel):
     top_p: float = 1.0
     top_k: int = 0
     seed: Optional[int] = None
+    stop_token_ids: List[int] = []
     stream: bool = False
 
 
@@ -65,6 +66,8 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
         kw = dict(max_new_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p, top_k=req.top_k)
         if req.seed is not None:
             kw["seed"] = req.seed
+        if req.stop_token_ids:
+            kw["stop_token_ids"] = tuple(int(t) for t in req.stop_token_ids)
         return SamplingParams(**kw)
 
     def _text(ids: List[int]) -> Optional[str]:

@@ -10,7 +10,7 @@ import enum
 import itertools
 import time
 from dataclasses import dataclass, field
-from typing import List, Optional
+from typing import List, Optional, Tuple
 
 
 class SeqStatus(enum.Enum):
@@ -30,6 +30,7 @@ class SamplingParams:
     eos_token_id: Optional[int] = None
     ignore_eos: bool = False
     seed: Optional[int] = None
+    stop_token_ids: Tuple[int, ...] = ()  # generation ends after emitting any of these (kept in the output)
 
 
 _ids = itertools.count()
@@ -67,6 +68,8 @@ class Sequence:
     def finished_by(self, token: int) -> bool:
         p = self.params
         if not p.ignore_eos and p.eos_token_id is not None and token == p.eos_token_id:
+            return True
+        if p.stop_token_ids and token in p.stop_token_ids:
             return True
         return len(self.output) >= p.max_new_tokens
 

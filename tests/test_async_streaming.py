@@ -90,3 +90,10 @@ def test_async_stream_cancel_frees_the_request():
         ae.shutdown()
     assert len(got) == 2 and not eng.has_unfinished() and eng.blocks.num_free == free0
     assert ae.streaming.stats.get("cancelled", 0) == 1
+
+
+def test_stop_token_ids_end_generation():
+    ref = _engine().generate([PROMPTS[0]], SamplingParams(max_new_tokens=8))[0]
+    stop = ref[3]
+    got = _engine().generate([PROMPTS[0]], SamplingParams(max_new_tokens=8, stop_token_ids=(stop,)))[0]
+    assert got == ref[:ref.index(stop) + 1]

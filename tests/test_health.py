@@ -56,8 +56,12 @@ def _worker(rank, world, port, mode, q):
             break
         time.sleep(0.05)
     hb.stop()
-    if rank == 0:
-        time.sleep(0.5)  # keep the store (hosted here) up while the other survivors finish reading
+    survivors = world - 1
+    hb.store.add("mb_test/done", 1)
+    if rank == 0:  # the store lives in this process: keep it up until every survivor has read it
+        t1 = time.time()
+        while hb.store.add("mb_test/done", 0) < survivors and time.time() - t1 < 20:
+            time.sleep(0.05)
 
 
 @pytest.mark.parametrize("mode", ["raise", "exit", "leave"])
@@ -69,15 +73,17 @@ def test_survivors_detect_rank_loss(mode):
     ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in ps:
         p.start()
-    for p in ps:
-        p.join(timeout=60)
-    for p in ps:
-        if p.is_alive():
-            p.kill()
+    expected = world if mode in ("raise", "leave") else world - 1   # an exiting rank reports nothing
     res = {}
-    while not q.empty():
-        r, v = q.get()
-        res[r] = v
+    try:
+        for _ in range(expected):
+            r, v = q.get(timeout=60)
+            res[r] = v
+    finally:
+        for p in ps:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
     for r in (0, 1):
         assert isinstance(res.get(r), tuple), res
         ranks, reason, _ = res[r]

@@ -38,7 +38,8 @@ class LLMEngine:
                  num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
                  max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
                  expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
-                 quantization: Optional[str] = None, prefix_caching: bool = False):
+                 quantization: Optional[str] = None, prefix_caching: bool = False,
+                 prefill_chunk: Optional[int] = None):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
@@ -103,7 +104,12 @@ class LLMEngine:
         self.prefix_caching = bool(prefix_caching) and self.states is None
         mgr = PrefixCachingBlockManager if self.prefix_caching else BlockManager
         self.blocks = mgr(num_blocks, bs, max_seqs=max_batch)
-        self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens)
+        # chunked prefill (prefill_chunk tokens per step, alternating with decode steps); vision-language
+        # models build a whole prompt's embeddings at once and keep whole-prompt prefill
+        if prefill_chunk is not None and (prefill_chunk < 1 or getattr(self.model, "prefill_embeds", None)):
+            prefill_chunk = None
+        self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
+                                   prefill_chunk=prefill_chunk)
         self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
                                   use_graphs=use_graphs and backend == "native", device=self.device)
         from .sampler import Sampler
@@ -182,6 +188,8 @@ class LLMEngine:
         self.last_step = {"kind": 1.0 if sched.is_decode else 0.0, "seconds": now - t0, "batch": len(sched.seqs)}
         done = []
         for s, t in zip(sched.seqs, toks):
+            if not sched.is_decode and s.num_cached < s.length:
+                continue                      # a prefill chunk that did not reach the prompt's end
             if s.t_first_token is None:
                 s.t_first_token = now
             s.output.append(int(t))

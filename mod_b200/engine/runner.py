@@ -198,16 +198,22 @@ class ModelRunner:
         ids, pos, slots, ctx, lidx = [], [], [], [], []
         bt = np.zeros((len(seqs), self.max_blocks), dtype=np.int32)
         t = 0
+        ends = []
         for i, (s, ql) in enumerate(zip(seqs, query_lens)):
-            start = s.length - ql
+            # the chunk covers positions [num_cached, num_cached + ql): the whole rest of the prompt,
+            # or one chunk of it under chunked prefill
+            start = s.num_cached
+            end = start + ql
+            assert 0 < end <= s.length, (start, ql, s.length)
             if start == 0:  # from scratch: fresh blocks, so cached block-table rows are stale
                 self._gen[s.req_id] = self._gen.get(s.req_id, 0) + 1
-            ids.append(np.asarray(s.all_tokens[start:], dtype=np.int64))
-            p = np.arange(start, s.length, dtype=np.int64)   # positions of the new tokens
+            ids.append(np.asarray(s.all_tokens[start:end], dtype=np.int64))
+            p = np.arange(start, end, dtype=np.int64)   # positions of the new tokens
             blk = np.asarray(s.blocks, dtype=np.int64)
             pos.append(p)
             slots.append(blk[p // bs] * bs + p % bs)
-            ctx.append(s.length)
+            ctx.append(end)
+            ends.append(end)
             t += ql
             lidx.append(t - 1)
             bt[i, :len(s.blocks)] = s.blocks
@@ -227,15 +233,15 @@ class ModelRunner:
                           state_slots=up([s.state_slot for s in seqs], torch.long), is_decode=False,
                           query_lens=list(query_lens), ctx_lens_host=ctx, inputs_embeds=inputs_embeds)
         if self.states is not None:
-            fresh = [s.state_slot for s, ql in zip(seqs, query_lens) if ql == s.length]
+            fresh = [s.state_slot for s in seqs if s.num_cached == 0]
             if fresh:
                 self.states.reset(torch.tensor(fresh, device=dev))
         h = self.model.forward(fb, self.kv, self.states)
         if return_logits:
-            for s in seqs:
-                s.num_cached = s.length
+            for s, e in zip(seqs, ends):
+                s.num_cached = e
             return self.model.logits(h).float()
         out = self._sample(h, seqs).to("cpu")
-        for s in seqs:
-            s.num_cached = s.length
+        for s, e in zip(seqs, ends):
+            s.num_cached = e
         return out.tolist()

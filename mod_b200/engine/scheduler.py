@@ -15,7 +15,7 @@ from __future__ import annotations
 
 from collections import deque
 from dataclasses import dataclass
-from typing import Deque, List
+from typing import Optional, Deque, List
 
 from .block_manager import BlockManager
 from .sequence import Sequence, SeqStatus
@@ -29,13 +29,18 @@ class ScheduledStep:
 
 
 class Scheduler:
-    def __init__(self, blocks: BlockManager, max_batch: int = 256, max_prefill_tokens: int = 16384):
+    def __init__(self, blocks: BlockManager, max_batch: int = 256, max_prefill_tokens: int = 16384,
+                 prefill_chunk: Optional[int] = None):
         self.blocks = blocks
         self.max_batch = max_batch
         self.max_prefill_tokens = max_prefill_tokens
         self.waiting: Deque[Sequence] = deque()
         self.running: List[Sequence] = []
         self.num_preempted = 0
+        # chunked prefill: a prompt is computed prefill_chunk tokens per step, and prefill chunks
+        # alternate with decode steps of the sequences already generating
+        self.prefill_chunk = prefill_chunk
+        self._last_prefill = False
 
     def add(self, seq: Sequence) -> None:
         seq.status = SeqStatus.WAITING
@@ -49,11 +54,11 @@ class Scheduler:
         budget = self.max_prefill_tokens
         while self.waiting and len(self.running) + len(picked) < self.max_batch:
             seq = self.waiting[0]
-            n = seq.length
+            n = seq.length if not self.prefill_chunk else min(seq.length, self.prefill_chunk)  # this step's tokens
             if picked and n > budget:
                 break
-            # reserve room for the prompt plus the first decode token
-            if not self.blocks.allocate(seq, n + 1):
+            # reserve room for the whole prompt plus the first decode token
+            if not self.blocks.allocate(seq, seq.length + 1):
                 if not picked and not self.running and self.blocks.num_free == self.blocks.num_blocks:
                     # can never fit: fail it instead of spinning
                     self.waiting.popleft()
@@ -66,13 +71,51 @@ class Scheduler:
             budget -= n
         return picked
 
+    @staticmethod
+    def _partial(s: Sequence) -> bool:
+        # one uncached prompt token left is decode-ready: decoding it equals prefilling it
+        return s.num_cached < s.length - 1
+
+    def _schedule_chunked(self) -> Optional[ScheduledStep]:
+        part = [s for s in self.running if self._partial(s)]
+        ready = [s for s in self.running if not self._partial(s)]
+        if part and not (self._last_prefill and ready):
+            budget, picked, qls = self.max_prefill_tokens, [], []
+            for s in part:
+                q = min(s.length - s.num_cached, self.prefill_chunk, budget)
+                if q <= 0:
+                    break
+                picked.append(s)
+                qls.append(q)
+                budget -= q
+            self._last_prefill = True
+            return ScheduledStep(picked, False, qls)
+        if not (self._last_prefill and ready):
+            new = self._admit()
+            if new:
+                for s in new:
+                    s.status = SeqStatus.RUNNING
+                self.running.extend(new)
+                self._last_prefill = True
+                return ScheduledStep(new, False, [min(s.length - s.num_cached, self.prefill_chunk) for s in new])
+        self._last_prefill = False
+        return None
+
     def schedule(self) -> ScheduledStep:
+        if self.prefill_chunk:
+            st = self._schedule_chunked()
+            if st is not None:
+                return st
+            return self._decode_step()
         new = self._admit()
         if new:
             for s in new:
                 s.status = SeqStatus.RUNNING
             self.running.extend(new)
             return ScheduledStep(new, False, [s.length - s.num_cached for s in new])
+        return self._decode_step()
+
+    def _decode_step(self) -> ScheduledStep:
         # decode: every running sequence needs a slot for one more token
         i = 0
         while i < len(self.running):
@@ -85,7 +128,8 @@ class Scheduler:
             victim.status = SeqStatus.WAITING
             self.waiting.appendleft(victim)
             self.num_preempted += 1
-        return ScheduledStep(list(self.running), True, [1] * len(self.running))
+        ready = [s for s in self.running if not self._partial(s)]
+        return ScheduledStep(ready, True, [1] * len(ready))
 
     def finish(self, seq: Sequence, status: SeqStatus = SeqStatus.FINISHED) -> None:
         seq.status = status

@@ -26,7 +26,8 @@ from .interfaces import PluginMetadata, PluginType, TextModelPluginInterface
 log = logging.getLogger("mod_b200.plugin")
 
 _RUNTIME_KEYS = {"device", "backend", "max_batch", "max_model_len", "max_prefill_tokens", "seed", "model_path",
-                 "use_graphs", "kv_mem_fraction", "max_new_tokens", "dtype", "prefix_caching"}
+                 "use_graphs", "kv_mem_fraction", "max_new_tokens", "dtype", "prefix_caching",
+                 "prefill_chunk"}
 
 
 class EnginePlugin(TextModelPluginInterface):
@@ -109,7 +110,8 @@ class EnginePlugin(TextModelPluginInterface):
         self.engine = LLMEngine(self._config, weights=weights, backend=rt["backend"], device=dev,
                                 max_batch=rt["max_batch"], max_model_len=rt["max_model_len"],
                                 use_graphs=rt.get("use_graphs", True),
-                                prefix_caching=bool(rt.get("prefix_caching", False)))
+                                prefix_caching=bool(rt.get("prefix_caching", False)),
+                                prefill_chunk=int(rt.get("prefill_chunk", 0)) or None)
         return self.engine
 
     def cleanup(self) -> bool:

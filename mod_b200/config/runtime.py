@@ -54,6 +54,7 @@ class RuntimeConfig:
     threads: int = 0                     # CPU backend OpenMP threads (0: default)
     offload: bool = False                # hybrid CPU/GPU weight streaming
     prefix_caching: bool = False         # share KV blocks of common prompt prefixes
+    prefill_chunk: int = 0               # >0: prefill prompts in chunks of this many tokens
     extra: Dict[str, Any] = field(default_factory=dict)
 
 

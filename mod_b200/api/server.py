@@ -12,7 +12,9 @@ the continuous batcher:
   per token;
 * ``GET /health`` -- engine state (running / waiting sequences, free KV
   blocks);
-* ``GET /v1/models`` -- the served model.
+* ``GET /v1/models`` -- the served model;
+* ``GET /metrics`` -- Prometheus text format: request and token counters,
+  request latency histogram, running / waiting sequences and free KV blocks.
 
 Requests go through :class:`~mod_b200.api.managers.AsyncEngine`, whose engine
 thread batches every pending request together.
@@ -52,6 +54,7 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
 
     app = FastAPI(title="mod_b200", version="0.1.0", lifespan=lifespan)
     app.state.front = front
+    m = _Metrics(engine)
 
     def _ids(req: CompletionRequest) -> List[int]:
         if isinstance(req.prompt, list):
@@ -78,6 +81,13 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
         return {"status": "ok", "running": len(engine.scheduler.running), "waiting": len(engine.scheduler.waiting),
                 "free_kv_blocks": engine.blocks.num_free}
 
+    @app.get("/metrics")
+    def metrics():
+        from fastapi.responses import Response
+
+        body, ctype = m.render()
+        return Response(content=body, media_type=ctype)
+
     @app.get("/v1/models")
     def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model"}]}
@@ -86,9 +96,13 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
     async def completions(req: CompletionRequest):
         ids, params = _ids(req), _params(req)
         created = int(time.time())
+        t0 = time.perf_counter()
+        m.requests.inc()
+        m.prompt_tokens.inc(len(ids))
         if req.stream:
             async def events():
                 async for tok in front.stream(ids, params):
+                    m.completion_tokens.inc()
                     yield "data: " + json.dumps({"object": "text_completion.chunk", "model": model_name,
                                                  "token": tok, "text": _text([tok])}) + "\n\n"
                 yield "data: [DONE]\n\n"
@@ -97,7 +111,10 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
         try:
             out = await front.generate(ids, params)
         except RuntimeError as e:
+            m.failures.inc()
             raise HTTPException(503, str(e))
+        m.completion_tokens.inc(len(out))
+        m.latency.observe(time.perf_counter() - t0)
         return {"object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": 0, "text": _text(out), "token_ids": out,
                              "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}],
@@ -105,6 +122,36 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
                           "total_tokens": len(ids) + len(out)}}
 
     return app
+
+
+class _Metrics:
+    """Prometheus metrics of one served engine (own registry, so several apps can coexist)."""
+
+    def __init__(self, engine):
+        from prometheus_client import CollectorRegistry, Counter, Gauge, Histogram
+
+        self.engine = engine
+        self.registry = r = CollectorRegistry()
+        self.requests = Counter("mb_requests", "completion requests", registry=r)
+        self.failures = Counter("mb_request_failures", "requests that failed", registry=r)
+        self.prompt_tokens = Counter("mb_prompt_tokens", "prompt tokens received", registry=r)
+        self.completion_tokens = Counter("mb_completion_tokens", "tokens generated", registry=r)
+        self.latency = Histogram("mb_request_seconds", "non-streaming request latency", registry=r,
+                                 buckets=(0.01, 0.05, 0.1, 0.25, 0.5, 1, 2, 5, 10, 30, 60))
+        self.running = Gauge("mb_running_sequences", "sequences in the running batch", registry=r)
+        self.waiting = Gauge("mb_waiting_sequences", "sequences waiting for admission", registry=r)
+        self.free_blocks = Gauge("mb_free_kv_blocks", "free paged-KV blocks", registry=r)
+        self.preempted = Gauge("mb_preemptions", "sequences preempted so far", registry=r)
+
+    def render(self):
+        from prometheus_client import CONTENT_TYPE_LATEST, generate_latest
+
+        e = self.engine
+        self.running.set(len(e.scheduler.running))
+        self.waiting.set(len(e.scheduler.waiting))
+        self.free_blocks.set(e.blocks.num_free)
+        self.preempted.set(e.scheduler.num_preempted)
+        return generate_latest(self.registry), CONTENT_TYPE_LATEST
 
 
 def serve(engine, tokenizer=None, model_name: str = "model", host: str = "127.0.0.1", port: int = 8000) -> None:

@@ -43,3 +43,6 @@ def test_completions_stream_health_and_errors():
         t = c.post("/v1/completions", json={"prompt": "hi", "max_tokens": 3})
         assert t.status_code == 200 and len(t.json()["choices"][0]["token_ids"]) == 3
         assert c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 0}).status_code == 400
+        mt = c.get("/metrics").text
+        assert "mb_requests_total 3.0" in mt and "mb_completion_tokens_total 15.0" in mt
+        assert "mb_free_kv_blocks" in mt and "mb_request_seconds_count 2.0" in mt

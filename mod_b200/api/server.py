@@ -10,6 +10,10 @@ the continuous batcher:
   "stream": bool}``; the reply carries the text (when a tokenizer is loaded),
   the token ids and usage counts; ``stream`` returns server-sent events, one
   per token;
+* ``POST /v1/chat/completions`` -- ``{"messages": [{"role", "content"}...],
+  "max_tokens", ..., "enable_thinking": bool}``: the messages go through the
+  ChatML template (thinking mode on or off) and the reply is one assistant
+  message with ``<think>`` blocks removed from ``content``;
 * ``GET /health`` -- engine state (running / waiting sequences, free KV
   blocks);
 * ``GET /v1/models`` -- the served model;
@@ -39,6 +43,17 @@ class CompletionRequest(BaseModel):
     seed: Optional[int] = None
     stop_token_ids: List[int] = []
     stream: bool = False
+
+
+class ChatRequest(BaseModel):
+    messages: List[dict]
+    max_tokens: int = 256
+    temperature: float = 0.0
+    top_p: float = 1.0
+    top_k: int = 0
+    seed: Optional[int] = None
+    stop_token_ids: List[int] = []
+    enable_thinking: bool = False
 
 
 def create_app(engine, tokenizer=None, model_name: str = "model"):
@@ -117,6 +132,37 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
         m.latency.observe(time.perf_counter() - t0)
         return {"object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": 0, "text": _text(out), "token_ids": out,
+                             "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                          "total_tokens": len(ids) + len(out)}}
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: ChatRequest):
+        from ..io.prompts import apply_chat_template, strip_thinking
+
+        if tokenizer is None:
+            raise HTTPException(400, "no tokenizer loaded: chat needs one")
+        if not req.messages:
+            raise HTTPException(400, "messages must not be empty")
+        text = apply_chat_template(tokenizer, req.messages, enable_thinking=req.enable_thinking)
+        ids = tokenizer.encode(text)
+        params = _params(CompletionRequest(prompt=ids, max_tokens=req.max_tokens, temperature=req.temperature,
+                                           top_p=req.top_p, top_k=req.top_k, seed=req.seed,
+                                           stop_token_ids=req.stop_token_ids))
+        m.requests.inc()
+        m.prompt_tokens.inc(len(ids))
+        t0 = time.perf_counter()
+        try:
+            out = await front.generate(ids, params)
+        except RuntimeError as e:
+            m.failures.inc()
+            raise HTTPException(503, str(e))
+        m.completion_tokens.inc(len(out))
+        m.latency.observe(time.perf_counter() - t0)
+        reply = tokenizer.decode(out)
+        return {"object": "chat.completion", "created": int(time.time()), "model": model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": strip_thinking(reply)},
+                             "token_ids": out,
                              "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                           "total_tokens": len(ids) + len(out)}}

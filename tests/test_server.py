@@ -46,3 +46,21 @@ def test_completions_stream_health_and_errors():
         mt = c.get("/metrics").text
         assert "mb_requests_total 3.0" in mt and "mb_completion_tokens_total 15.0" in mt
         assert "mb_free_kv_blocks" in mt and "mb_request_seconds_count 2.0" in mt
+
+
+def test_chat_completions_uses_the_chat_template():
+    from mod_b200.api.server import create_app
+    from mod_b200.io.prompts import apply_chat_template
+
+    tok = load_tokenizer(None)
+    msgs = [{"role": "user", "content": "Hi"}]
+    ids = apply_chat_template(tok, msgs, enable_thinking=False, tokenize=True)
+    ref = _engine().generate([ids], SamplingParams(max_new_tokens=4))[0]
+    app = create_app(_engine(), tok, "tiny-dense")
+    with TestClient(app) as c:
+        r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 4})
+        assert r.status_code == 200
+        body = r.json()
+        assert body["choices"][0]["token_ids"] == ref and body["choices"][0]["message"]["role"] == "assistant"
+        assert body["usage"]["prompt_tokens"] == len(ids)
+        assert c.post("/v1/chat/completions", json={"messages": []}).status_code == 400

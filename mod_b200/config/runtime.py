@@ -1,6 +1,7 @@
 """Runtime configuration, generation configuration, config-file loading.
 
-Load order: defaults -> file (JSON or YAML) -> environment (``MB_*``) -> explicit
+Load order: defaults -> file (JSON or YAML) -> environment (``MB_*``; the
+``PIO_*`` names of the same fields are read too, ``MB_*`` winning) -> explicit
 overrides (CLI), then validation.  Named profiles mirror the reference's
 presets (``pio/common/config/unified_config_manager.py:484-534``: performance,
 memory_efficient, balanced).  The reference's loader/merge/validator live in
@@ -145,6 +146,7 @@ def load_runtime(path: Optional[str] = None, profile: Optional[str] = None,
         data = load_file(path)
         d = deep_merge(d, data.get("runtime", data))
     if env:
+        d = deep_merge(d, from_env("PIO_"))
         d = deep_merge(d, from_env())
     if overrides:
         d = deep_merge(d, {k: v for k, v in overrides.items() if v is not None})

@@ -39,6 +39,11 @@ def test_runtime_config_layers(tmp_path, monkeypatch):
     monkeypatch.setenv("MB_MAX_MODEL_LEN", "999")
     cfg = load_runtime(str(p), profile="balanced", overrides={"tp": 2})
     assert (cfg.max_batch, cfg.comm, cfg.max_model_len, cfg.tp, cfg.kv_mem_fraction) == (7, "nccl", 999, 2, 0.8)
+    monkeypatch.setenv("PIO_MAX_BATCH", "5")          # the reference-style prefix is read too...
+    monkeypatch.setenv("PIO_SEED", "3")
+    monkeypatch.setenv("MB_SEED", "4")                # ...and MB_* wins where both are set
+    cfg = load_runtime(overrides={"tp": 1})
+    assert (cfg.max_batch, cfg.seed) == (5, 4)
     with pytest.raises(ConfigError):
         validate(RuntimeConfig(backend="nope"))
     with pytest.raises(ConfigError):

@@ -152,6 +152,79 @@ class StreamingEngine:
         self._thread.join(timeout=10)
 
 
+class ReplicaRouter:
+    """Data-parallel serving: requests spread over several engine replicas.
+
+    Each replica (an engine on its own device, or a CPU engine) gets its own
+    streaming thread, scheduler and KV cache; a new request goes to the
+    replica with the fewest queued + running sequences.  The interface is the
+    :class:`StreamingEngine` one, so :class:`AsyncEngine` and the HTTP server
+    can sit on top of a router unchanged.
+    """
+
+    def __init__(self, engines, max_queue: int = 1024):
+        if not engines:
+            raise ValueError("ReplicaRouter needs at least one engine")
+        self.replicas = [e if isinstance(e, StreamingEngine) else StreamingEngine(e, max_queue) for e in engines]
+        self._count = itertools.count()
+        self._lock = threading.Lock()
+        self._route: Dict[int, tuple] = {}       # router id -> (replica index, replica id)
+        self._streams = _RoutedStreams(self)
+
+    def _load(self, r: "StreamingEngine") -> int:
+        with r._lock:
+            return len(r._pq) + len(r.engine.scheduler.running) + len(r.engine.scheduler.waiting)
+
+    def submit_request(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
+                       images=None) -> int:
+        with self._lock:
+            i = min(range(len(self.replicas)), key=lambda j: (self._load(self.replicas[j]), j))
+            rid = next(self._count)
+            self._route[rid] = (i, self.replicas[i].submit_request(token_ids, params, priority, images=images))
+        return rid
+
+    def replica_of(self, rid: int) -> int:
+        return self._route[rid][0]
+
+    def generate_stream(self, rid: int, timeout: float = 300.0) -> Iterator[int]:
+        i, sub = self._route[rid]
+        return self.replicas[i].generate_stream(sub, timeout)
+
+    def cancel(self, rid: int) -> None:
+        i, sub = self._route[rid]
+        self.replicas[i].cancel(sub)
+
+    @property
+    def stats(self) -> Dict[str, int]:
+        out: Dict[str, int] = {}
+        for r in self.replicas:
+            for k, v in r.stats.items():
+                out[k] = out.get(k, 0) + v
+        return out
+
+    def shutdown(self) -> None:
+        for r in self.replicas:
+            r.shutdown()
+
+
+class _RoutedStreams:
+    """``router._streams[rid]`` / ``.pop(rid)``: the per-request token queue, as on a StreamingEngine."""
+
+    def __init__(self, router: ReplicaRouter):
+        self.router = router
+
+    def __getitem__(self, rid: int):
+        i, sub = self.router._route[rid]
+        return self.router.replicas[i]._streams[sub]
+
+    def pop(self, rid: int, default=None):
+        route = self.router._route.pop(rid, None)
+        if route is None:
+            return default
+        i, sub = route
+        return self.router.replicas[i]._streams.pop(sub, default)
+
+
 class AsyncEngine:
     """asyncio front-end over a :class:`StreamingEngine` (text or image + text requests).
 
@@ -165,7 +238,8 @@ class AsyncEngine:
     """
 
     def __init__(self, engine, max_queue: int = 1024):
-        self.streaming = engine if isinstance(engine, StreamingEngine) else StreamingEngine(engine, max_queue)
+        self.streaming = (engine if isinstance(engine, (StreamingEngine, ReplicaRouter))
+                          else StreamingEngine(engine, max_queue))
 
     async def stream(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
                      images=None):

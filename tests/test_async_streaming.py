@@ -97,3 +97,24 @@ def test_stop_token_ids_end_generation():
     stop = ref[3]
     got = _engine().generate([PROMPTS[0]], SamplingParams(max_new_tokens=8, stop_token_ids=(stop,)))[0]
     assert got == ref[:ref.index(stop) + 1]
+
+
+def test_replica_router_spreads_requests_and_matches():
+    from mod_b200.api.managers import AsyncEngine, ReplicaRouter
+
+    ref = _engine().generate(PROMPTS, SamplingParams(max_new_tokens=5))
+    router = ReplicaRouter([_engine(), _engine()])
+    ae = AsyncEngine(router)
+
+    async def main():
+        return await asyncio.gather(*(ae.generate(p, SamplingParams(max_new_tokens=5)) for p in PROMPTS))
+
+    try:
+        rids = [router.submit_request(p, SamplingParams(max_new_tokens=5)) for p in PROMPTS]
+        assert {router.replica_of(r) for r in rids} == {0, 1}      # both replicas got work
+        direct = [list(router.generate_stream(r, timeout=60)) for r in rids]
+        outs = asyncio.run(asyncio.wait_for(main(), 120))
+    finally:
+        ae.shutdown()
+    assert direct == ref and outs == ref
+    assert router.stats["completed"] == 2 * len(PROMPTS)

@@ -2,6 +2,7 @@
 // KV cache layouts match the GPU: K [blocks, Hkv, BS, D], V [blocks, Hkv, D, BS]
 // (V is stored transposed inside a block so the GPU P.V product reads it
 // K-major).
+#include <immintrin.h>
 #include <omp.h>
 #include <algorithm>
 #include <cmath>
@@ -12,6 +13,24 @@
 namespace mbcpu {
 
 static const float* cf(const at::Tensor& t) { return t.data_ptr<float>(); }
+
+// fp32 dot product with AVX2 FMAs (two 8-lane accumulators), scalar tail
+static inline float dot(const float* a, const float* b, int64_t n) {
+  __m256 s0 = _mm256_setzero_ps(), s1 = _mm256_setzero_ps();
+  int64_t i = 0;
+  for (; i + 16 <= n; i += 16) {
+    s0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), s0);
+    s1 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 8), _mm256_loadu_ps(b + i + 8), s1);
+  }
+  for (; i + 8 <= n; i += 8) s0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), s0);
+  s0 = _mm256_add_ps(s0, s1);
+  __m128 lo = _mm_add_ps(_mm256_castps256_ps128(s0), _mm256_extractf128_ps(s0, 1));
+  lo = _mm_hadd_ps(lo, lo);
+  lo = _mm_hadd_ps(lo, lo);
+  float r = _mm_cvtss_f32(lo);
+  for (; i < n; ++i) r += a[i] * b[i];
+  return r;
+}
 static float* mf(at::Tensor& t) { return t.data_ptr<float>(); }
 
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
@@ -114,23 +133,24 @@ void attn_paged(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor
       const float* qv = pq + (r * Hq + h) * D;
       std::vector<float> s(n);
       float mx = -INFINITY;
-      for (int64_t j = 0; j < n; ++j) {
+      for (int64_t j = 0; j < n; ++j) {  // K rows are contiguous: one vector dot product per key
         const int64_t blk = bt[b * MB + j / bs];
-        const float* kv = pk + ((blk * Hkv + hk) * bs + j % bs) * D;
-        float acc = 0.f;
-        for (int64_t d = 0; d < D; ++d) acc += qv[d] * kv[d];
-        s[j] = acc * (float)scale;
+        s[j] = dot(qv, pk + ((blk * Hkv + hk) * bs + j % bs) * D, D) * (float)scale;
         mx = std::max(mx, s[j]);
       }
       float sum = 0.f;
       for (int64_t j = 0; j < n; ++j) sum += (s[j] = std::exp(s[j] - mx));
+      const float inv = 1.f / sum;
+      for (int64_t j = 0; j < n; ++j) s[j] *= inv;
       float* o = po + (r * Hq + h) * D;
       std::fill(o, o + D, 0.f);
-      for (int64_t j = 0; j < n; ++j) {
-        const int64_t blk = bt[b * MB + j / bs];
-        const float* vv = pv + ((blk * Hkv + hk) * D) * bs + j % bs;
-        const float p = s[j] / sum;
-        for (int64_t d = 0; d < D; ++d) o[d] += p * vv[d * bs];
+      // V is stored [D, bs] inside a block: per block, each output element is one contiguous
+      // dot product over the block's tokens
+      for (int64_t j0 = 0; j0 < n; j0 += bs) {
+        const int64_t blk = bt[b * MB + j0 / bs];
+        const int64_t cnt = std::min<int64_t>(bs, n - j0);
+        const float* vb = pv + ((blk * Hkv + hk) * D) * bs;
+        for (int64_t d = 0; d < D; ++d) o[d] += dot(s.data() + j0, vb + d * bs, cnt);
       }
     }
 }

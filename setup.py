@@ -10,7 +10,7 @@ Only ``sm_100a`` code is generated (no PTX fallback, no other architectures).
 import glob
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 
 os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"  # keep torch from adding other -gencode targets
 
@@ -60,7 +60,10 @@ if glob.glob(os.path.join("csrc", "cpu", "*.cc")):
 setup(
     name="mod_b200",
     version="0.1.0",
-    packages=["mod_b200"],
+    packages=find_packages(include=["mod_b200", "mod_b200.*"]),
+    package_data={"mod_b200": ["config/baselines/*.yaml", "models/plugins/*/plugin_manifest.json"]},
+    entry_points={"console_scripts": ["mod_b200 = mod_b200.cli.main:main"]},
+    python_requires=">=3.10",
     ext_modules=exts,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

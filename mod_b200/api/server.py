@@ -43,6 +43,7 @@ class CompletionRequest(BaseModel):
     seed: Optional[int] = None
     stop_token_ids: List[int] = []
     stream: bool = False
+    n: int = 1                      # independent samples of one prompt (seed + i for sample i)
 
 
 class ChatRequest(BaseModel):
@@ -110,6 +111,8 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
         ids, params = _ids(req), _params(req)
+        if req.n < 1 or (req.n > 1 and req.stream):
+            raise HTTPException(400, "n must be >= 1 (and 1 when streaming)")
         created = int(time.time())
         t0 = time.perf_counter()
         m.requests.inc()
@@ -123,18 +126,24 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(events(), media_type="text/event-stream")
+        import asyncio
+        import dataclasses
+
+        base_seed = params.seed if params.seed is not None else 0
+        plist = [params] if req.n == 1 else [dataclasses.replace(params, seed=base_seed + i) for i in range(req.n)]
         try:
-            out = await front.generate(ids, params)
+            outs = await asyncio.gather(*(front.generate(ids, p) for p in plist))
         except RuntimeError as e:
             m.failures.inc()
             raise HTTPException(503, str(e))
-        m.completion_tokens.inc(len(out))
+        ntok = sum(len(o) for o in outs)
+        m.completion_tokens.inc(ntok)
         m.latency.observe(time.perf_counter() - t0)
         return {"object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "text": _text(out), "token_ids": out,
-                             "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}],
-                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
-                          "total_tokens": len(ids) + len(out)}}
+                "choices": [{"index": i, "text": _text(out), "token_ids": out,
+                             "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}
+                            for i, out in enumerate(outs)],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": ntok, "total_tokens": len(ids) + ntok}}
 
     @app.post("/v1/chat/completions")
     async def chat(req: ChatRequest):

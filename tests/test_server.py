@@ -64,3 +64,18 @@ def test_chat_completions_uses_the_chat_template():
         assert body["choices"][0]["token_ids"] == ref and body["choices"][0]["message"]["role"] == "assistant"
         assert body["usage"]["prompt_tokens"] == len(ids)
         assert c.post("/v1/chat/completions", json={"messages": []}).status_code == 400
+
+
+def test_n_samples_with_seeds():
+    from mod_b200.api.server import create_app
+
+    app = create_app(_engine(), None, "tiny-dense")
+    with TestClient(app) as c:
+        body = {"prompt": [5, 6, 7, 8], "max_tokens": 6, "temperature": 1.0, "seed": 11, "n": 3}
+        r = c.post("/v1/completions", json=body).json()
+        again = c.post("/v1/completions", json=body).json()
+        outs = [ch["token_ids"] for ch in r["choices"]]
+        assert len(outs) == 3 and r["usage"]["completion_tokens"] == 18
+        assert outs == [ch["token_ids"] for ch in again["choices"]]        # seeded: reproducible
+        assert len({tuple(o) for o in outs}) > 1                            # different seeds differ
+        assert c.post("/v1/completions", json={**body, "stream": True}).status_code == 400

@@ -7,6 +7,7 @@
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mod_b200 C++/OpenMP CPU backend and safetensors mmap reader";
   m.def("linear", &mbcpu::linear);
+  m.def("linear_w8", &mbcpu::linear_w8);
   m.def("rmsnorm", &mbcpu::rmsnorm);
   m.def("rope_qknorm", &mbcpu::rope_qknorm);
   m.def("attn_paged", &mbcpu::attn_paged);

@@ -7,6 +7,7 @@
 
 namespace mbcpu {
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y);
+void linear_w8(const at::Tensor& x, const at::Tensor& q, const at::Tensor& scale, at::Tensor& y);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
              double eps);
 void rope_qknorm(const at::Tensor& qkv, const c10::optional<at::Tensor>& q_w, const c10::optional<at::Tensor>& k_w,

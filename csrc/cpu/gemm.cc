@@ -1,5 +1,5 @@
 // GEMM  y[M, N] = x[M, K] * w[N, K]^T  (both operands K-contiguous), fp32
-// activations and accumulation; weights fp32 or bf16.
+// activations and accumulation; weights fp32, bf16 or int8 (+ per-row scale).
 //
 // Register-blocked dot-product kernel: a 4 x 4 tile of outputs keeps 16
 // accumulators along K (AVX-512 where the CPU has it, chosen at run time: 16
@@ -10,7 +10,8 @@
 // bf16 weights are widened to fp32 in registers (a bf16 value is the upper
 // half of the fp32 with the same value, so the widening is a 16-bit shift):
 // the result equals fp32 math on the bf16-rounded weights while the weight
-// stream, which bounds decode, is halved.
+// stream, which bounds decode, is halved.  int8 weights are widened the same
+// way (sign-extend, convert) and the per-row scale multiplies each output once.
 #include <immintrin.h>
 #include <omp.h>
 #include <algorithm>
@@ -28,6 +29,7 @@ static inline float hsum(__m256 v) {
 }
 
 static inline float to_f32(float v) { return v; }
+static inline float to_f32(int8_t v) { return (float)v; }
 static inline float to_f32(uint16_t v) {
   const uint32_t u = (uint32_t)v << 16;
   float f;
@@ -42,11 +44,21 @@ static inline __m256 load8(const uint16_t* p) {
   return _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_cvtepu16_epi32(h), 16));
 }
 
+static inline __m256 load8(const int8_t* p) {
+  const __m128i b = _mm_loadl_epi64(reinterpret_cast<const __m128i*>(p));
+  return _mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(b));
+}
+
 // 16 weights as fp32 (AVX-512)
 __attribute__((target("avx512f"))) static inline __m512 load16(const float* p) { return _mm512_loadu_ps(p); }
 __attribute__((target("avx512f"))) static inline __m512 load16(const uint16_t* p) {
   const __m256i h = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(p));
   return _mm512_castsi512_ps(_mm512_slli_epi32(_mm512_cvtepu16_epi32(h), 16));
+}
+
+__attribute__((target("avx512f"))) static inline __m512 load16(const int8_t* p) {
+  const __m128i b = _mm_loadu_si128(reinterpret_cast<const __m128i*>(p));
+  return _mm512_cvtepi32_ps(_mm512_cvtepi8_epi32(b));
 }
 
 // rows [m0, m0+mr) x cols [n0, n0+nr), mr, nr <= 4
@@ -167,6 +179,21 @@ static void gemm(const float* px, const WT* pw, float* py, int64_t M, int64_t K,
         for (int64_t m0 = bi * MB; m0 < m_end; m0 += 4)
           tile(px, pw, py, K, N, m0, (int)std::min<int64_t>(4, m_end - m0), n0, (int)std::min<int64_t>(4, n_end - n0));
     }
+}
+
+// int8 weight-only: y = (x . q^T) * scale[n], the per-channel scale applied once per output
+void linear_w8(const at::Tensor& x, const at::Tensor& q, const at::Tensor& scale, at::Tensor& y) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && y.scalar_type() == at::kFloat && scale.scalar_type() == at::kFloat);
+  TORCH_CHECK(q.scalar_type() == at::kChar, "linear_w8: weights must be int8");
+  TORCH_CHECK(x.is_contiguous() && q.is_contiguous() && y.is_contiguous() && scale.is_contiguous());
+  const int64_t M = x.size(0), K = x.size(1), N = q.size(0);
+  TORCH_CHECK(q.size(1) == K && y.size(0) == M && y.size(1) == N && scale.numel() == N);
+  float* py = y.data_ptr<float>();
+  gemm(x.data_ptr<float>(), reinterpret_cast<const int8_t*>(q.data_ptr()), py, M, K, N);
+  const float* sc = scale.data_ptr<float>();
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < M; ++i)
+    for (int64_t n = 0; n < N; ++n) py[i * N + n] *= sc[n];
 }
 
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y) {

@@ -24,8 +24,9 @@ def main(argv=None):
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--backend", default="cpu", choices=["cpu", "torch"])
-    ap.add_argument("--weight-dtype", default="fp32", choices=["fp32", "bf16"],
-                    help="bf16: weights stored in bf16 (fp32 math); config #1 itself is fp32")
+    ap.add_argument("--weight-dtype", default="fp32", choices=["fp32", "bf16", "int8"],
+                    help="bf16 / int8 (per-channel scales): projection weights stored narrower, fp32 math; "
+                         "config #1 itself is fp32")
     a = ap.parse_args(argv)
     from ..config import get_preset
     from ..engine import SamplingParams
@@ -37,8 +38,16 @@ def main(argv=None):
         torch.set_num_threads(a.threads)
     cfg = get_preset("qwen3-0.6b")
     t0 = time.perf_counter()
-    w = random_weights(cfg, device="cpu", dtype=torch.float32 if a.weight_dtype == "fp32" else torch.bfloat16,
+    w = random_weights(cfg, device="cpu", dtype=torch.bfloat16 if a.weight_dtype == "bf16" else torch.float32,
                        seed=0)
+    if a.weight_dtype == "int8":
+        from ..ops.quant import quantize_model
+
+        quantize_model(w)
+        # embedding / LM head stay out of int8 (as on the GPU path); store them bf16 here
+        tied = w.lm_head is w.embed
+        w.embed = w.embed.bfloat16()
+        w.lm_head = w.embed if tied else w.lm_head.bfloat16()
     init_s = time.perf_counter() - t0
     eng = LLMEngine(cfg, weights=w, backend=a.backend, device="cpu", max_batch=1,
                     max_model_len=a.prompt_len + a.new_tokens + 16)
@@ -56,7 +65,8 @@ def main(argv=None):
         eng.step()
         n += 1
     dec = time.perf_counter() - t1
-    label = "fp32" if a.weight_dtype == "fp32" else "bf16 weights, fp32 math"
+    label = {"fp32": "fp32", "bf16": "bf16 weights, fp32 math",
+             "int8": "int8 projections + bf16 embedding / LM head, fp32 math"}[a.weight_dtype]
     print(json.dumps({"config": f"qwen3-0.6b cpu {label} (16/8 GQA, head_dim 128, QK-norm)", "backend": a.backend,
                       "threads": a.threads or os.cpu_count(), "prompt_len": a.prompt_len, "ttft_s": round(ttft, 3),
                       "decode_tok_s": round(n / dec, 2), "decode_ms_per_token": round(dec / n * 1000, 2),

@@ -244,11 +244,14 @@ class CpuBackend(TorchBackend):
 
     def linear(self, x, w, bias=None, residual=None, out=None):
         x2 = x.reshape(-1, x.shape[-1]).float().contiguous()
-        # bf16 weights stay bf16 (widened in registers: half the weight bytes); others go to fp32
-        if not (isinstance(w, torch.Tensor) and w.dtype == torch.bfloat16 and w.is_contiguous()):
-            w = dense(w, torch.float32)
         y = torch.empty(x2.shape[0], w.shape[0], dtype=torch.float32)
-        self.C.linear(x2, w, y)
+        if isinstance(w, Int8Weight):   # int8 weight-only: widened in registers, per-channel scale
+            self.C.linear_w8(x2, w.q.contiguous(), w.scale.float().contiguous(), y)
+        else:
+            # bf16 weights stay bf16 (widened in registers: half the weight bytes); others go to fp32
+            if not (isinstance(w, torch.Tensor) and w.dtype == torch.bfloat16 and w.is_contiguous()):
+                w = dense(w, torch.float32)
+            self.C.linear(x2, w, y)
         if bias is not None:
             y += bias
         if residual is not None:

@@ -177,3 +177,38 @@ def test_cpu_engine_bf16_weights_match_widened_copy(name):
     a = LLMEngine(cfg, weights=wb, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
     b = LLMEngine(cfg, weights=wf, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
     assert a == b
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 300), (1, 40, 7), (6, 1000, 37), (128, 256, 96)])
+def test_linear_int8_weights(M, K, N):
+    x = _r(M, K, seed=32)
+    q = torch.randint(-127, 128, (N, K), generator=torch.Generator().manual_seed(33), dtype=torch.int8)
+    sc = torch.rand(N, generator=torch.Generator().manual_seed(34)) * 0.01
+    y = torch.empty(M, N)
+    C.linear_w8(x, q, sc, y)
+    ref = x @ (q.float() * sc[:, None]).t()
+    assert torch.allclose(y, ref, atol=1e-4, rtol=1e-5)
+
+
+def test_cpu_engine_int8_matches_dequantized_weights():
+    from mod_b200.config import get_preset
+    from mod_b200.engine.llm_engine import LLMEngine
+    from mod_b200.engine.sequence import SamplingParams
+    from mod_b200.models.weights import random_weights
+    from mod_b200.ops.quant import Int8Weight, quantize_model
+
+    cfg = get_preset("tiny-dense")
+    wq = random_weights(cfg, dtype=torch.float32, seed=0)
+    quantize_model(wq)
+    wd = random_weights(cfg, dtype=torch.float32, seed=0)
+    quantize_model(wd)
+    for L in wd.layers:                    # the same int8 values, dequantized to fp32 up front
+        for part in (L.attn, L.mlp):
+            for k, v in list(vars(part).items()):
+                if isinstance(v, Int8Weight):
+                    setattr(part, k, v.q.float() * v.scale[:, None])
+    prompts = [[1, 2, 3, 4, 5], [7, 8, 9]]
+    p = SamplingParams(max_new_tokens=6)
+    a = LLMEngine(cfg, weights=wq, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
+    b = LLMEngine(cfg, weights=wd, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
+    assert a == b

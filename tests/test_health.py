@@ -25,7 +25,8 @@ def _worker(rank, world, port, mode, q):
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    hb = Heartbeat(rank, world, interval=0.1, timeout=1.0).start()
+    # generous limit: under a loaded CI box a beat thread can stall for a while
+    hb = Heartbeat(rank, world, interval=0.1, timeout=3.0).start()
     x = torch.ones(4)
     dist.all_reduce(x)  # one healthy step for everyone
     hb.check()
@@ -51,7 +52,7 @@ def _worker(rank, world, port, mode, q):
         except RankFailure as e:
             q.put((rank, (e.ranks, e.reasons[victim], round(time.time() - t0, 2))))
             break
-        if time.time() - t0 > 10.0:
+        if time.time() - t0 > 20.0:
             q.put((rank, "not detected"))
             break
         time.sleep(0.05)
@@ -94,7 +95,7 @@ def test_survivors_detect_rank_loss(mode):
             assert reason == "left"
         else:
             assert "heartbeat" in reason
-            assert res[r][2] < 5.0
+            assert res[r][2] < 15.0
 
 
 def test_never_joined_rank_is_reported():

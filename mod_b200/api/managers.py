@@ -109,8 +109,6 @@ class StreamingEngine:
             with self._lock:
                 while not self._stop and not self._pq and not self._cancel and not self.engine.has_unfinished():
                     self._cv.wait(timeout=0.1)
-                if self._stop:
-                    return
                 if self._cancel:
                     for rid in self._cancel:
                         q = self._streams.get(rid)
@@ -126,6 +124,9 @@ class StreamingEngine:
                             q.put(None)
                         self.stats["cancelled"] = self.stats.get("cancelled", 0) + 1
                     self._cancel.clear()
+                # pending cancellations are applied even at shutdown, so their blocks are freed
+                if self._stop:
+                    return
                 while self._pq:
                     _, rid, ids, params, images = heapq.heappop(self._pq)
                     q = self._streams[rid]

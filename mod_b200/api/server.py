@@ -44,6 +44,7 @@ class CompletionRequest(BaseModel):
     stop_token_ids: List[int] = []
     stream: bool = False
     n: int = 1                      # independent samples of one prompt (seed + i for sample i)
+    stop: List[str] = []            # text stop strings (need a tokenizer); the reply ends before the first
 
 
 class ChatRequest(BaseModel):
@@ -92,6 +93,18 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
     def _text(ids: List[int]) -> Optional[str]:
         return tokenizer.decode(ids) if tokenizer is not None else None
 
+    async def _generate_stop(ids: List[int], params: SamplingParams, stop: List[str]):
+        """Generate until a stop string appears in the decoded text; the request is cancelled
+        there (its KV blocks freed) and the text cut before the stop string."""
+        out: List[int] = []
+        async for tok in front.stream(ids, params):
+            out.append(tok)
+            text = tokenizer.decode(out)
+            cut = min((text.find(x) for x in stop if x and x in text), default=-1)
+            if cut >= 0:
+                return out, text[:cut], "stop"
+        return out, tokenizer.decode(out), ("length" if len(out) >= params.max_new_tokens else "stop")
+
     @app.get("/health")
     def health():
         return {"status": "ok", "running": len(engine.scheduler.running), "waiting": len(engine.scheduler.waiting),
@@ -113,6 +126,8 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
         ids, params = _ids(req), _params(req)
         if req.n < 1 or (req.n > 1 and req.stream):
             raise HTTPException(400, "n must be >= 1 (and 1 when streaming)")
+        if req.stop and (tokenizer is None or req.stream):
+            raise HTTPException(400, "stop strings need a tokenizer and a non-streaming request")
         created = int(time.time())
         t0 = time.perf_counter()
         m.requests.inc()
@@ -132,17 +147,20 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
         base_seed = params.seed if params.seed is not None else 0
         plist = [params] if req.n == 1 else [dataclasses.replace(params, seed=base_seed + i) for i in range(req.n)]
         try:
-            outs = await asyncio.gather(*(front.generate(ids, p) for p in plist))
+            if req.stop:
+                res = await asyncio.gather(*(_generate_stop(ids, p, req.stop) for p in plist))
+            else:
+                outs = await asyncio.gather(*(front.generate(ids, p) for p in plist))
+                res = [(o, _text(o), "length" if len(o) >= req.max_tokens else "stop") for o in outs]
         except RuntimeError as e:
             m.failures.inc()
             raise HTTPException(503, str(e))
-        ntok = sum(len(o) for o in outs)
+        ntok = sum(len(o) for o, _, _ in res)
         m.completion_tokens.inc(ntok)
         m.latency.observe(time.perf_counter() - t0)
         return {"object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": i, "text": _text(out), "token_ids": out,
-                             "finish_reason": "length" if len(out) >= req.max_tokens else "stop"}
-                            for i, out in enumerate(outs)],
+                "choices": [{"index": i, "text": text, "token_ids": out, "finish_reason": why}
+                            for i, (out, text, why) in enumerate(res)],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": ntok, "total_tokens": len(ids) + ntok}}
 
     @app.post("/v1/chat/completions")

@@ -79,3 +79,23 @@ def test_n_samples_with_seeds():
         assert outs == [ch["token_ids"] for ch in again["choices"]]        # seeded: reproducible
         assert len({tuple(o) for o in outs}) > 1                            # different seeds differ
         assert c.post("/v1/completions", json={**body, "stream": True}).status_code == 400
+
+
+def test_stop_strings_cut_and_cancel():
+    from mod_b200.api.server import create_app
+
+    tok = load_tokenizer(None)
+    eng = _engine()
+    app = create_app(eng, tok, "tiny-dense")
+    with TestClient(app) as c:
+        full = c.post("/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 12}).json()["choices"][0]
+        text = full["text"]
+        stop = text[len(text) // 2:len(text) // 2 + 1] if len(text) > 2 else None
+        if not stop:
+            pytest.skip("the random model's text is too short to pick a stop string from")
+        r = c.post("/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 12, "stop": [stop]}).json()
+        ch = r["choices"][0]
+        assert ch["finish_reason"] == "stop" and stop not in ch["text"] and text.startswith(ch["text"])
+        assert len(ch["token_ids"]) <= len(full["token_ids"])
+        assert c.post("/v1/completions", json={"prompt": [1], "stop": ["x"], "stream": True}).status_code == 400
+    assert eng.blocks.num_free == eng.blocks.num_blocks          # the cancelled request released its blocks

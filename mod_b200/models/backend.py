@@ -225,6 +225,13 @@ class NativeBackend:
         return self.N.argmax(logits.contiguous())
 
 
+def _rows_f32(w, lo: int, hi: int) -> torch.Tensor:
+    """Rows [lo, hi) of a weight (fp32 / bf16 tensor or Int8Weight) as fp32."""
+    if isinstance(w, Int8Weight):
+        return w.q[lo:hi].float() * w.scale[lo:hi, None].float()
+    return w[lo:hi].float()
+
+
 class CpuBackend(TorchBackend):
     """C++/OpenMP CPU backend (``mod_b200._cpu``), fp32.  Plumbing and host
     reference path; the reference's equivalent is its C CPU library
@@ -294,9 +301,24 @@ class CpuBackend(TorchBackend):
         wts = torch.empty(T, top_k)
         self.C.moe_route(logits, top_k, renorm, ids, wts)
         out = torch.zeros_like(x) if residual is None else residual.clone()
-        # the C++ expert mixture reads fp32 weights (bf16 experts are widened per call)
-        self.C.moe_experts(x.contiguous(), ids, wts, dense(mo.w13, torch.float32), dense(mo.w2, torch.float32),
-                           mo.e_lo, mo.e_hi - mo.e_lo, out)
+        E_l = mo.e_hi - mo.e_lo
+        if isinstance(mo.w13, torch.Tensor) and mo.w13.dtype == torch.float32:
+            self.C.moe_experts(x.contiguous(), ids, wts, mo.w13, mo.w2, mo.e_lo, E_l, out)
+        else:
+            # narrow (bf16 / int8) experts: widen only the experts this call routes to, then run the
+            # same fp32 expert kernel on the compacted set (ids remapped; others skipped as -1)
+            local = ids.long() - mo.e_lo
+            active = torch.unique(local[(local >= 0) & (local < E_l)])
+            if active.numel():
+                remap = torch.full((E_l,), -1, dtype=torch.long)
+                remap[active] = torch.arange(active.numel())
+                cids = torch.where((local >= 0) & (local < E_l), remap[local.clamp(0, E_l - 1)],
+                                   torch.full_like(local, -1)).to(torch.int32)
+                r13, r2 = mo.w13.shape[0] // E_l, mo.w2.shape[0] // E_l
+                w13c = torch.cat([_rows_f32(mo.w13, int(e) * r13, (int(e) + 1) * r13) for e in active])
+                w2c = torch.cat([_rows_f32(mo.w2, int(e) * r2, (int(e) + 1) * r2) for e in active])
+                self.C.moe_experts(x.contiguous(), cids, wts, w13c.contiguous(), w2c.contiguous(), 0,
+                                   int(active.numel()), out)
         if mo.shared is not None:
             sh = self.swiglu_mlp(x, mo.shared.gate_up, mo.shared.down)
             out += torch.sigmoid(x.float() @ mo.shared_gate.float().t()) * sh

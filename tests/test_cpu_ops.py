@@ -212,3 +212,20 @@ def test_cpu_engine_int8_matches_dequantized_weights():
     a = LLMEngine(cfg, weights=wq, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
     b = LLMEngine(cfg, weights=wd, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
     assert a == b
+
+
+def test_cpu_moe_int8_experts_match_torch_backend():
+    """int8 experts: only the routed experts are widened per call; same tokens as the torch path."""
+    from mod_b200.config import get_preset
+    from mod_b200.engine.llm_engine import LLMEngine
+    from mod_b200.engine.sequence import SamplingParams
+    from mod_b200.models.weights import random_weights
+    from mod_b200.ops.quant import quantize_model
+
+    cfg = get_preset("tiny-moe")
+    w = random_weights(cfg, dtype=torch.float32, seed=0)
+    quantize_model(w)
+    prompts, p = [[1, 2, 3, 4, 5], [7, 8, 9]], SamplingParams(max_new_tokens=5)
+    a = LLMEngine(cfg, weights=w, backend="cpu", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
+    b = LLMEngine(cfg, weights=w, backend="torch", device="cpu", max_batch=2, max_model_len=64).generate(prompts, p)
+    assert a == b

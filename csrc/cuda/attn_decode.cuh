@@ -26,7 +26,9 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int b = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Hq = Hkv * G;
-  const int ctx = ctx_lens[b];
+  // The block table row holds max_blocks entries: a context longer than
+  // 16 * max_blocks is clamped to what the row can address (never read past it).
+  const int ctx = min(ctx_lens[b], max_blocks * BS);
   const int nblk = (ctx + BS - 1) / BS;
   const int bps = (nblk + splits - 1) / splits;
   const int blo = sp * bps, bhi = min(nblk, blo + bps);

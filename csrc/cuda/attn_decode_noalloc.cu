@@ -30,6 +30,7 @@
 #include <cstdio>
 #include <mutex>
 #include "attn_decode.cuh"
+#include "mb_noalloc.h"
 
 namespace {
 
@@ -93,12 +94,26 @@ __attribute__((visibility("default"))) size_t mb_attn_decode_noalloc_max_scratch
 // cudaStream_t (0 = legacy default stream).  Returns 0 on success, 1 for bad
 // arguments, 2 when B*Hq*splits*(D+1) exceeds the scratch array, 3 for a
 // head_dim / group size without a compiled kernel, 4 for a CUDA error.
+// Every ctx_lens[b] must be <= 16 * max_blocks; a longer one is clamped on the
+// device to the tokens its block-table row addresses.
 __attribute__((visibility("default"))) int mb_attn_decode_noalloc(
     const void* q, const void* k_cache, const void* v_cache, const int* block_tables, const int* ctx_lens, void* out,
     int B, int Hq, int Hkv, int D, int max_blocks, int splits, float scale, void* stream) {
   if (!q || !k_cache || !v_cache || !block_tables || !ctx_lens || !out || B <= 0 || Hq <= 0 || Hkv <= 0 ||
       Hq % Hkv != 0 || max_blocks <= 0 || splits <= 0)
     return fail(1, "mb_attn_decode_noalloc: invalid argument");
+  if (D != 64 && D != 128 && D != 256) return fail(3, "mb_attn_decode_noalloc: head_dim must be 64, 128 or 256");
+  {
+    // an error left by earlier, unrelated work on this thread is reported as such (and cleared),
+    // so that it is not mistaken for this call's launch failure below
+    const cudaError_t pending = cudaGetLastError();
+    if (pending != cudaSuccess) {
+      char m[200];
+      std::snprintf(m, sizeof(m), "mb_attn_decode_noalloc: CUDA error pending before the call: %s",
+                    cudaGetErrorString(pending));
+      return fail(4, m);
+    }
+  }
   const size_t need = (size_t)B * Hq * splits * (D + 1);
   if (need > kNoAllocScratchFloats) {
     char m[160];

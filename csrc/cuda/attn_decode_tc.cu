@@ -77,6 +77,7 @@ struct TileCursor {
   int item, t, nt;
   int B, Hkv, splits, chunk_blocks, items;
   const int* ctx_lens;
+  int max_blocks;
   int b, hk, sp, lo, hi, nblk;  // current item
   __device__ bool next(TileRef& r, __nv_bfloat16* out, float* part_o, float* part_lse) {
     while (t + 1 >= nt) {
@@ -85,7 +86,7 @@ struct TileCursor {
       sp = item % splits;
       hk = (item / splits) % Hkv;
       b = item / (splits * Hkv);
-      const int ctx = ctx_lens[b];
+      const int ctx = min(ctx_lens[b], max_blocks * 16);  // never past the block-table row
       nblk = (ctx + 15) / 16;
       const int blo = min(nblk, sp * chunk_blocks), bhi = min(nblk, blo + chunk_blocks);
       lo = blo * 16;
@@ -168,7 +169,8 @@ __global__ void __launch_bounds__(128, 1)
   pdl_trigger();
 
   // tile descriptors: cur (being computed) and nxt (being loaded)
-  TileCursor<G> cursor{(int)blockIdx.x - (int)gridDim.x, 0, 0, B, Hkv, splits, chunk_blocks, items, ctx_lens};
+  TileCursor<G> cursor{(int)blockIdx.x - (int)gridDim.x, 0, 0, B, Hkv, splits, chunk_blocks, items, ctx_lens,
+                       max_blocks};
   TileRef cur, nxt;
   bool has_cur = cursor.next(cur, out, part_o, part_lse);
   bool has_nxt = false;

@@ -31,12 +31,10 @@ enum EpiMode : int {
   kEpiScatterRows = 4,  // (+ bias) each output row stored at row_map[row] of its owner's buffer (P2P)
 };
 
-// Tensor-parallel operands of a GEMM: activations gathered from the peers'
-// shard buffers (all-gather fused into the operand loads) and/or a
-// reduce-scatter epilogue.  Peer memory is only ever read by plain
-// (non-multicast) TMA loads and written by ordinary stores.
+// Tensor-parallel operands of a GEMM: a wait on the flags of the shards that
+// the peers pushed into this rank's gathered buffer, and/or a reduce-scatter
+// epilogue.  Peer memory is only written, by ordinary stores.
 struct TpArgs {
-  const CUtensorMap* peer_maps;   // [N] maps over each rank's activation shard, box = 64 x sub rows
   const uint32_t* ag_flags;       // [N] local: ag_flags[p] >= *epoch once rank p's shard is ready
   uint32_t* epoch;                // local boundary counter
   int peer_rows;                  // rows per shard (tokens per rank)
@@ -66,7 +64,7 @@ struct GemmArgs {
   int ldc;
   int out_rows;          // tokens (rows of out) for the split-K workspace stride
   int* status;
-  TpArgs tp;             // tp.peer_maps == nullptr: not tensor parallel
+  TpArgs tp;             // zero-initialised: not tensor parallel
   const float* w_scale;  // int8-weight variant: per-row scale of A (row g*a_rows + r), applied in the epilogue
   const __nv_bfloat16* bias;  // kEpiScatterRows: per output feature
   // Persistent schedule (items > 0): the grid is sized to the resident CTAs and
@@ -130,23 +128,10 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_
   hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
 }
 
-// Loads `rows` activation rows starting at gathered row `row0`, k-block kx,
-// either from the local map or from the peers' shard buffers.
-__device__ __forceinline__ void load_act(const GemmArgs& a, const CUtensorMap* local, void* dst, uint64_t* bar, int kx,
-                                         int row0, int rows) {
-  if (!a.tp.peer_maps) {
-    tma_load_2d(dst, local, bar, kx, row0);
-    return;
-  }
-  for (int r = 0; r < rows; r += a.tp.sub) {
-    int p = (row0 + r) / a.tp.peer_rows;
-    int lr = (row0 + r) - p * a.tp.peer_rows;
-    if (p >= a.tp.nranks) {   // past the gathered rows: out-of-range coordinate -> TMA zero fill
-      p = a.tp.nranks - 1;
-      lr = a.tp.peer_rows;
-    }
-    tma_load_2d(reinterpret_cast<uint8_t*>(dst) + r * 128, &a.tp.peer_maps[p], bar, kx, lr);
-  }
+// Loads `rows` activation rows starting at row `row0`, k-block kx.
+__device__ __forceinline__ void load_act(const GemmArgs&, const CUtensorMap* local, void* dst, uint64_t* bar, int kx,
+                                         int row0, int) {
+  tma_load_2d(dst, local, bar, kx, row0);
 }
 
 // Stage layout: A tile(s) [128 x 64] bf16 SW128 | B tile [BN x 64] bf16 SW128 |

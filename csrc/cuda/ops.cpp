@@ -78,7 +78,6 @@ void tp_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, bool wai
              int64_t ag_flags, at::Tensor& state, int64_t rank, int64_t nranks, int64_t peer_rows,
              const at::Tensor& rs_peers, int64_t rs_off, int64_t rs_flag_off, const c10::optional<at::Tensor>& workspace);
 at::Tensor wrap_bf16(int64_t addr, int64_t rows, int64_t cols);
-at::Tensor tp_make_peer_maps(const std::vector<int64_t>& ag_addrs, int64_t rows, int64_t H, int64_t sub);
 void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_t rows, int64_t H, int64_t ag_off,
                int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off, at::Tensor& state,
                const c10::optional<at::Tensor>& x_add, at::Tensor& residual, const at::Tensor& w, double eps,
@@ -129,7 +128,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine", &mb::ep_combine);
   m.def("ep_recv_only", &mb::ep_recv_only);
   m.def("tp_gemm", &mb::tp_gemm);
-  m.def("tp_make_peer_maps", &mb::tp_make_peer_maps);
   m.def("wrap_bf16", &mb::wrap_bf16);
   m.def("tp_reduce", &mb::tp_reduce);
   m.def("tp_gather_rows", &mb::tp_gather_rows);

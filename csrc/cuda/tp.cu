@@ -27,17 +27,6 @@ namespace mb {
 CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows, int64_t cols, int64_t ld_bytes,
                          int box_cols, int box_rows, CUtensorMapSwizzle sw);
 
-// One 2-D map per rank over its ag shard, box 64 x sub rows, as a device byte tensor.
-at::Tensor tp_make_peer_maps(const std::vector<int64_t>& ag_addrs, int64_t rows, int64_t H, int64_t sub) {
-  std::vector<CUtensorMap> maps;
-  for (auto a : ag_addrs)
-    maps.push_back(make_tmap_2d(reinterpret_cast<void*>(a), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rows, H, H * 2, 64,
-                                (int)sub, CU_TENSOR_MAP_SWIZZLE_128B));
-  auto host = at::empty({(int64_t)(maps.size() * sizeof(CUtensorMap))}, at::kByte);
-  std::memcpy(host.data_ptr(), maps.data(), maps.size() * sizeof(CUtensorMap));
-  return host.to(at::Device(at::kCUDA, c10::cuda::current_device()));
-}
-
 __device__ __forceinline__ uint32_t ld_acq(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

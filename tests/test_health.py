@@ -30,6 +30,7 @@ def _worker(rank, world, port, mode, q):
     x = torch.ones(4)
     dist.all_reduce(x)  # one healthy step for everyone
     hb.check()
+    dist.barrier()  # every rank has passed its healthy check before the victim fails
     victim = world - 1
     if rank == victim:
         if mode == "raise":

@@ -7,18 +7,23 @@ Workload (BASELINE config #3): batch 128 (global), 512-token uniform-random
 prompts, greedy decode; random-init N(0, 0.02) bf16 weights from seed 0.
 Per run:
   1. prefill every prompt through the engine (records p50 TTFT);
-  2. W warm-up decode steps (the first one captures the CUDA graph);
-  3. ``value``: K decode steps timed on the device with CUDA events as back-to-back
-     replays of the captured decode-step graph (max over ranks);
-  4. ``e2e``: K decode steps through the public API ``LLMEngine.step()``: each
+  2. W warm-up decode steps through the engine (the first captures the CUDA graph);
+  3. N > 1: one untimed MoE layer of each rank's tokens checked against the
+     unsharded torch MoE computed locally ("check" in the JSON line);
+  4. ``value``: K decode steps timed on the device with CUDA events: each step
+     replays the captured decode graph and advances every sequence by one token
+     on the device (sampled token fed back, context + 1), so the context grows
+     over the K steps as in serving (max over ranks);
+  5. ``e2e``: K decode steps through the public API ``LLMEngine.step()``: each
      step copies its inputs host->device from pinned memory, runs, and reads
      the sampled tokens back device->host.
 N > 1 runs one process per GPU (torchrun) with expert parallelism: each rank
 serves 128/N sequences with a replicated attention stack (DP attention) and
 holds E/N experts; MoE layers exchange tokens with the fused NVLink
-dispatch/combine kernels (native) or NCCL all-to-all (baseline).
-Decode reads ~61 GB of weights per step on one GPU, far above the 126 MB L2,
-so no L2 flush is needed between steps.
+dispatch/combine kernels (native) or NCCL all-to-all + library grouped GEMMs
+(``--impl baseline``: PyTorch + NCCL + cuBLAS only, also CUDA-graph captured).
+Decode reads ~61 GB of weights per step on one GPU (~10 GB per rank at N=8),
+far above the 126 MB L2, so no L2 flush is needed between steps.
 """
 from __future__ import annotations
 
@@ -132,6 +137,38 @@ def reference_arm(args):
     print(json.dumps({"impl": "reference", "unavailable": why}))
 
 
+def moe_check(cfg, eng, dev, world, rank):
+    """One MoE layer of this rank's tokens through the engine's expert-parallel
+    path vs the unsharded torch MoE computed locally (all ranks take part).
+    Returns {"status": "ok"|"fail", "max_rel_err": e} (max over ranks)."""
+    import copy
+
+    import torch
+    import torch.distributed as dist
+
+    from mod_b200.models.backend import TorchBackend
+    from mod_b200.models.weights import random_weights
+
+    c1 = copy.deepcopy(cfg)
+    c1.num_hidden_layers = 1
+    full = random_weights(c1, device=dev, dtype=torch.bfloat16, seed=0)  # same layer-0 weights as the engine's
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    T = eng.runner.max_batch
+    x = (torch.randn(T, cfg.hidden_size, device=dev, generator=g) * 0.5).bfloat16()
+    ref = TorchBackend().moe(x, full.layers[0].moe, cfg.num_experts_per_tok, cfg.norm_topk_prob,
+                             cfg.moe_intermediate_size).float()
+    out = eng.model.moe_impl(x, eng.model.w.layers[0].moe).float()
+    torch.cuda.synchronize()
+    err = torch.tensor([((out - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()], device=dev,
+                       dtype=torch.float64)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    del full
+    torch.cuda.empty_cache()
+    e = err.item()
+    return {"status": "ok" if e < 3e-2 else "fail", "max_rel_err": round(e, 5),
+            "against": "unsharded torch MoE, layer 0, each rank's own tokens"}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -161,8 +198,13 @@ def main():
     K, W = args.steps, args.warmup
     backend = "native" if args.impl == "native" else "torch"
     max_len = args.prompt_len + W + 3 * K + 16
+    # the baseline runs its MoE through the library-only expert-parallel block at every N (at N=1 without
+    # collectives), which keeps its decode step free of host syncs and so CUDA-graph capturable
+    ep = True if (backend == "torch" and cfg.is_moe) else None
     eng = LLMEngine(cfg, backend=backend, device=dev, max_batch=per_rank, max_model_len=max_len,
-                    max_prefill_tokens=16384, seed=0, use_graphs=True)
+                    max_prefill_tokens=16384, seed=0, use_graphs=True, expert_parallel=ep)
+    if world > 1:
+        dist.barrier()
     g = torch.Generator().manual_seed(1000 + rank)
     prompts = [torch.randint(0, cfg.vocab_size, (args.prompt_len,), generator=g).tolist() for _ in range(per_rank)]
     params = SamplingParams(max_new_tokens=W + 3 * K + 8, ignore_eos=True)
@@ -178,14 +220,12 @@ def main():
     p50_ttft = ttfts[len(ttfts) // 2]
     for _ in range(W):
         eng.step()
+    check = moe_check(cfg, eng, dev, world, rank) if world > 1 else None
     runner = eng.runner
-    B = max(runner.graphs) if runner.graphs else None
-    if B is None:  # eager path (baseline): a timed step is one engine step
-        def one_step():
-            eng.step()
-    else:
-        def one_step():
-            runner.graphs[B].replay()
+    running = list(eng.scheduler.running)
+    for s in running:  # block tables must cover the K device-side steps
+        assert eng.blocks.allocate(s, s.length + K + 1), "KV pool too small for the timed steps"
+    one_step = runner.device_stepper(running)
 
     def maxr(x):
         if world == 1:
@@ -194,7 +234,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
-    # ---------------- device-timed decode steps (graph replays)
+    # ---------------- device-timed decode steps (graph replays, context advancing on the device)
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         if world > 1:
@@ -221,11 +261,15 @@ def main():
     if world > 1:
         dist.barrier()
     e2e_ms = maxr((time.perf_counter() - t1) * 1000) / K
-    ours, total = count_launches(one_step)
-    if args.profile and rank == 0:
+    ours, total = count_launches(one_step, prefix="mb::" if backend == "native" else "\x00")
+    if args.profile:  # every rank replays (the EP exchange waits for all of them); rank 0 prints
         from mod_b200.bench.profile import kernel_table
 
-        print(kernel_table(one_step, reps=3, top=40), file=sys.stderr, flush=True)
+        if world > 1:
+            dist.barrier()
+        table = kernel_table(one_step, reps=3, top=40)
+        if rank == 0:
+            print(table, file=sys.stderr, flush=True)
     from mod_b200.ops import check_status
 
     if backend == "native":
@@ -240,8 +284,7 @@ def main():
             "config": {"model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt_len,
                        "parallelism": f"ep{world}+dp_attn{world}" if world > 1 else "single",
                        "layers": cfg.num_hidden_layers, "decode_batch_per_gpu": per_rank,
-                       "timed": ("CUDA-graph replays of one decode step at fixed context" if B is not None
-                                 else "engine decode steps (eager)"),
+                       "timed": "CUDA-graph replays of the decode step, context advanced on the device each step",
                        "l2": "no flush: a step reads ~61 GB of weights (> 126 MB L2)"},
             "e2e": {"value": round(args.batch / (e2e_ms / 1000.0), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
@@ -249,6 +292,8 @@ def main():
             "gpu_launches": ours * K, "gpu_launches_per_step": ours, "all_kernels_per_step": total,
             "clocks": clk.summary(),
         }
+        if check is not None:
+            line["check"] = check
         if args.layers:
             line["invalid"] = "layer count overridden"
         print(json.dumps(line), flush=True)

@@ -501,6 +501,259 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
+// ------------------------------------------- fused route + dispatch (one launch)
+// Router GEMV, softmax top-k, the per-expert count exchange and the direct
+// placement of every (token, k) row in its owner's expert-ordered receive
+// region, in one kernel.  Phases, separated by grid barriers (the grid is at
+// most one CTA per SM, so every CTA is resident; waits are bounded):
+//   1. logits[t][e] = x[t] . Wr[e] in fp32, tiles of 8 experts x 16 tokens;
+//   2. a warp per token: softmax, top-k (ties to the lower expert id),
+//      optional renormalisation; ids / wts written, counts[e] += 1;
+//   3. the last CTA to arrive publishes this rank's counts to every rank and
+//      releases flag_n; every CTA waits for all ranks' counts, derives the
+//      expert bases (as ep_dispatch2 does) and a warp per pair stores the row
+//      into its owner's buffer.  The last CTA to finish releases flag_d at
+//      every owner, and zeroes counts / cursors / barrier counters for the
+//      next call.
+// Scratch (device, zero between calls): counts [E], cursor [E]; logits [T, E] f32.
+constexpr int kRdThreads = 1024;
+constexpr int kRdTileE = 8, kRdTileT = 16;
+
+__device__ __forceinline__ bool grid_arrive_wait(int* ctr, int target, int* status) {
+  __syncthreads();
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(ctr, 1);
+    ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0;; ++i) {
+      int v;
+      asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_status(status, kErrPeerTimeout);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(kRdThreads)
+    ep_route_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wr,
+                             int T, int K, int renorm, float* __restrict__ logits, int* __restrict__ ids,
+                             float* __restrict__ wts, int* __restrict__ counts, int* __restrict__ cursor,
+                             int* __restrict__ map, int* __restrict__ offs, int* __restrict__ bar) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = *a.epoch + 1;
+  const int E = a.El * a.N, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, H = a.H;
+  // ---------------- 1. router logits
+  {
+    const int tiles_e = (E + kRdTileE - 1) / kRdTileE, tiles_t = (T + kRdTileT - 1) / kRdTileT;
+    const int e_in = warp % kRdTileE, t_grp = warp / kRdTileE;  // 4 token groups of 4 tokens
+    for (int tile = blockIdx.x; tile < tiles_e * tiles_t; tile += G) {
+      const int e = (tile % tiles_e) * kRdTileE + e_in;
+      const int t0 = (tile / tiles_e) * kRdTileT + t_grp * 4;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (e < E) {
+        for (int c = lane * 8; c < H; c += 256) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(wr + (size_t)e * H + c);
+          const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (t0 + j < T) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(x + (size_t)(t0 + j) * H + c);
+              const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) acc[j] += __bfloat162float(wh[q]) * __bfloat162float(xh[q]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float v = warp_sum(acc[j]);
+        if (lane == 0 && e < E && t0 + j < T) logits[(size_t)(t0 + j) * E + e] = v;
+      }
+    }
+  }
+  if (!grid_arrive_wait(bar, G, a.status)) return;
+  // ---------------- 2. top-k per token (warp per token)
+  for (int t = blockIdx.x * (kRdThreads / 32) + warp; t < T; t += G * (kRdThreads / 32)) {
+    float v[EPL];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = e < E ? __ldcg(logits + (size_t)t * E + e) : -INFINITY;
+      mx = fmaxf(mx, v[i]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = e < E ? __expf(v[i] - mx) : -1.f;  // probabilities; -1 marks padding
+      sum += e < E ? v[i] : 0.f;
+    }
+    sum = warp_sum(sum);
+    float picked = 0.f, my_w = 0.f;
+    int my_id = -1;
+    for (int k = 0; k < K; ++k) {
+      float bv = -2.f;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (v[i] > bv) { bv = v[i]; bi = i * 32 + lane; }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == k) { my_w = bv / sum; my_id = bi; }
+      picked += bv / sum;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (i * 32 + lane == bi) v[i] = -2.f;
+    }
+    if (lane < K) {
+      if (my_id < 0 || my_id >= E) {  // non-finite logits: never index with an invalid id
+        set_status(a.status, kErrBounds);
+        my_id = 0;
+        my_w = 0.f;
+      }
+      ids[(size_t)t * K + lane] = my_id;
+      wts[(size_t)t * K + lane] = renorm ? my_w / picked : my_w;
+      atomicAdd(&counts[my_id], 1);
+    }
+  }
+  // ---------------- 3. count exchange, then placement
+  __shared__ int last_in;
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    last_in = atomicAdd(bar + 1, 1) == G - 1;
+  }
+  __syncthreads();
+  if (last_in) {  // every CTA's counts are in: publish them to every rank
+    __threadfence();
+    for (int d = 0; d < a.N; ++d) {
+      int* dst = at_off<int>(a.peers[d], a.L.cntm) + a.rank * kEpMaxExperts;
+      for (int e = tid; e < E; e += blockDim.x) dst[e] = __ldcg(counts + e);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      for (int d = 0; d < a.N; ++d) st_release_sys(at_off<uint32_t>(a.peers[d], a.L.flag_n) + a.rank, epoch);
+    }
+  }
+  __shared__ int ok_all;
+  __shared__ int sh[5 * kEpMaxExperts + 32];
+  int* base = sh;
+  int* pre = base + kEpMaxExperts;
+  int* sbase = pre + kEpMaxExperts;
+  int* col = sbase + kEpMaxExperts;
+  int* own = col + kEpMaxExperts;
+  int* scan_sh = own + kEpMaxExperts;
+  if (tid == 0) ok_all = 1;
+  __syncthreads();
+  const uint64_t self = a.peers[a.rank];
+  for (int src = tid; src < a.N; src += blockDim.x)  // own counts included: they arrive through the same path
+    if (!wait_flag(at_off<uint32_t>(self, a.L.flag_n) + src, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
+  __syncthreads();
+  __threadfence();
+  const int* cntm = at_off<int>(self, a.L.cntm);
+  int colsum = 0, mine = 0, lower = 0;
+  const int e = tid;
+  if (e < E && ok_all) {
+    for (int src = 0; src < a.N; ++src) {
+      const int c = __ldcg(cntm + src * kEpMaxExperts + e);
+      colsum += c;
+      if (src < a.rank) lower += c;
+      if (src == a.rank) mine = c;
+    }
+  }
+  const int gcol = block_excl_scan(e < E ? colsum : 0, scan_sh);
+  if (e < E) base[e] = gcol;
+  const int gmine = block_excl_scan(e < E ? mine : 0, scan_sh);
+  if (e < E) {
+    sbase[e] = gmine;
+    pre[e] = lower;
+    col[e] = colsum;
+    own[e] = mine;
+  }
+  __syncthreads();
+  int seg_col = 0, seg_mine = 0;
+  if (e < E) {
+    const int seg = (e / a.El) * a.El;
+    seg_col = base[seg];
+    seg_mine = sbase[seg];
+  }
+  __syncthreads();
+  if (e < E) {
+    base[e] = gcol - seg_col;
+    sbase[e] = gmine - seg_mine;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && tid <= a.El) {
+    const int g0 = a.rank * a.El;
+    offs[tid] = tid < a.El ? base[g0 + tid] : base[g0 + a.El - 1] + col[g0 + a.El - 1];
+  }
+  const int TK = T * K;
+  for (int pair = blockIdx.x * (kRdThreads / 32) + warp; pair < TK; pair += G * (kRdThreads / 32)) {
+    int ex = __ldcg(ids + pair);
+    if (ex < 0 || ex >= E) ex = 0;
+    const int dst = ex / a.El;
+    int idx = 0;
+    if (lane == 0) idx = atomicAdd(&cursor[ex], 1);
+    idx = __shfl_sync(0xffffffffu, idx, 0);
+    const int pos = base[ex] + pre[ex] + idx;
+    const int slot = sbase[ex] + idx;
+    if (!ok_all || idx < 0 || idx >= own[ex] || pos < 0 || pos >= a.N * a.C || slot < 0 || slot >= a.C) {
+      if (lane == 0) {
+        if (ok_all) set_status(a.status, kErrCapacity);
+        map[pair] = 0;
+      }
+      continue;
+    }
+    if (lane == 0) {
+      map[pair] = dst * a.C + slot;
+      at_off<int>(a.peers[dst], a.L.meta)[pos] = a.rank * a.C + slot;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(pair / K) * H);
+    uint4* dstp = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[dst], a.L.recv_x) + (size_t)pos * H);
+    copy_row<false>(dstp, src, H / 8, lane);
+  }
+  __syncthreads();
+  __shared__ int last;
+  if (tid == 0) {
+    __threadfence_system();
+    last = atomicAdd(&a.done[0], 1) == G - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  // every CTA is past its last use of counts / cursor / the barrier counters
+  for (int i = tid; i < E; i += blockDim.x) {
+    counts[i] = 0;
+    cursor[i] = 0;
+  }
+  if (tid == 0) {
+    bar[0] = 0;
+    bar[1] = 0;
+    __threadfence_system();
+    for (int d = 0; d < a.N; ++d) st_release_sys(at_off<uint32_t>(a.peers[d], a.L.flag_d) + a.rank, epoch);
+    a.done[0] = 0;
+  }
+}
+
 // Owner: expert outputs y (xs order, offs[El] rows) back to their sources' comb slots.
 __global__ void ep_combine_send2_kernel(EpArgs a, const int* __restrict__ offs, const __nv_bfloat16* __restrict__ y) {
   pdl_wait();
@@ -538,6 +791,92 @@ __global__ void ep_combine_send2_kernel(EpArgs a, const int* __restrict__ offs, 
     __threadfence_system();
     for (int src = 0; src < a.N; ++src) st_release_sys(at_off<uint32_t>(a.peers[src], a.L.flag_c) + a.rank, epoch);
     a.done[1] = 0;
+  }
+}
+
+// ------------------------------------------- combine fused with add + RMSNorm
+// Replaces ep_combine_reduce + the next layer's add + RMSNorm: a warp per
+// token waits (bounded) for every owner's flag_c, forms
+//   h = bf16(sum_k w[t,k] * comb[map[t,k]])      (fixed k order)
+//   residual[t] = bf16(residual[t] + h);  out[t] = rmsnorm(residual[t]) * nw
+// which is exactly what the two kernels computed.  The last CTA advances the
+// epoch.  H is a compile-time multiple of 256.
+template <int H>
+__global__ void ep_combine_norm_kernel(EpArgs a, const int* __restrict__ map, const float* __restrict__ wts, int T,
+                                       int K, __nv_bfloat16* __restrict__ residual,
+                                       const __nv_bfloat16* __restrict__ nw, __nv_bfloat16* __restrict__ out,
+                                       float eps) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int kChunks = H / 256;
+  const uint32_t epoch = *a.epoch + 1;
+  const uint64_t self = a.peers[a.rank];
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  for (int o = threadIdx.x; o < a.N; o += blockDim.x)
+    if (!wait_flag(at_off<uint32_t>(self, a.L.flag_c) + o, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
+  __syncthreads();
+  __threadfence();
+  const __nv_bfloat16* comb = at_off<__nv_bfloat16>(self, a.L.comb);
+  const int lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T; t += gridDim.x * (blockDim.x / 32)) {
+    float v[kChunks][8];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[c][q] = 0.f;
+    if (ok_all) {
+      for (int k = 0; k < K; ++k) {
+        const float wk = wts[t * K + k];
+        const __nv_bfloat16* row = comb + (size_t)map[t * K + k] * H;
+        uint4 raw[kChunks];
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) raw[c] = __ldcg(reinterpret_cast<const uint4*>(row + c * 256 + lane * 8));
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[c]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[c][q] += wk * __bfloat162float(h[q]);
+        }
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int col = c * 256 + lane * 8;
+      uint4 rr = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + col);
+      const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(&rr);
+      __align__(16) __nv_bfloat16 sum8[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float h = __bfloat162float(__float2bfloat16(v[c][q]));  // the combined row, rounded as stored
+        sum8[q] = __float2bfloat16(h + __bfloat162float(r[q]));
+        v[c][q] = __bfloat162float(sum8[q]);
+        ss += v[c][q] * v[c][q];
+      }
+      *reinterpret_cast<uint4*>(residual + (size_t)t * H + col) = *reinterpret_cast<uint4*>(sum8);
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / H + eps);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int col = c * 256 + lane * 8;
+      uint4 wr = *reinterpret_cast<const uint4*>(nw + col);
+      const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wr);
+      __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16(v[c][q] * inv * __bfloat162float(wh[q]));
+      *reinterpret_cast<uint4*>(out + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
+    }
+  }
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(&a.done[2], 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    *a.epoch = epoch;  // every kernel of this call has read the old value
+    a.done[2] = 0;
   }
 }
 
@@ -614,6 +953,46 @@ void ep_dispatch2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int6
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Fused route + dispatch: x [T, H] bf16, router weight wr [E, H] bf16 ->
+// ids / wts [T, K], map [T*K], this rank's xs offsets offs [El + 1], rows in the
+// owners' receive regions.  scratch: int32 [2E + 2] (counts, cursor, barrier
+// counters; zero before the first call, left zero by every call), logits f32 [>= T*E].
+void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                       const at::Tensor& x, const at::Tensor& wr, int64_t K, bool renorm, at::Tensor& ids,
+                       at::Tensor& wts, at::Tensor& map, at::Tensor& offs, at::Tensor& scratch, at::Tensor& logits) {
+  const int64_t N = peers.numel(), T = x.size(0), H = x.size(1);
+  const int64_t E = N * El;
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && wr.scalar_type() == at::kBFloat16 &&
+              wr.is_contiguous() && wr.size(0) == E && wr.size(1) == H);
+  TORCH_CHECK(H % 256 == 0, "ep_route_dispatch: hidden size must be a multiple of 256");
+  TORCH_CHECK(T * K <= C, "ep_route_dispatch: T*K (", T * K, ") exceeds capacity ", C);
+  TORCH_CHECK(E <= kEpMaxExperts && K <= 32 && K <= E);
+  TORCH_CHECK(ids.numel() >= T * K && wts.numel() >= T * K && map.numel() >= T * K && offs.numel() >= El + 1 &&
+              scratch.scalar_type() == at::kInt && scratch.numel() >= 2 * E + 2 &&
+              logits.scalar_type() == at::kFloat && logits.numel() >= T * E);
+  if (T == 0) return;
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index()));
+  const int64_t tiles = ((E + kRdTileE - 1) / kRdTileE) * ((T + kRdTileT - 1) / kRdTileT);
+  const int64_t pair_ctas = (T * K + kRdThreads / 32 - 1) / (kRdThreads / 32);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, std::max(tiles, pair_ctas)));
+  int* sc = scratch.data_ptr<int>();
+  const int epl = (int)((E + 31) / 32);
+#define MB_RD(P)                                                                                                   \
+  launch_k(ep_route_dispatch_kernel<P>, grid, kRdThreads, 0, st, a, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), \
+           reinterpret_cast<const __nv_bfloat16*>(wr.data_ptr()), (int)T, (int)K, (int)renorm, logits.data_ptr<float>(), \
+           ids.data_ptr<int>(), wts.data_ptr<float>(), sc, sc + E, map.data_ptr<int>(), offs.data_ptr<int>(), sc + 2 * E)
+  if (epl <= 4) MB_RD(4);
+  else if (epl <= 8) MB_RD(8);
+  else if (epl <= 16) MB_RD(16);
+  else MB_RD(32);
+#undef MB_RD
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Byte address of this rank's flag_d array (the gate/up GEMM waits on it).
 int64_t ep_flag_addr(const at::Tensor& peers, int64_t rank, int64_t C, int64_t H) {
   const EpLayout L = ep_layout(peers.numel(), C, H);
@@ -643,6 +1022,51 @@ void ep_combine2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64
       (residual && residual->defined()) ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
   launch_k(ep_combine_reduce_kernel, (int)std::max<int64_t>(1, T), 256, 0, st, a, (const int*)map.data_ptr<int>(),
            (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Combine, first half: the owner returns its expert outputs y to their
+// sources' comb slots (the weighted sum follows in ep_combine_norm).
+void ep_combine_send(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                     const at::Tensor& offs, const at::Tensor& y, int64_t H) {
+  const int64_t N = peers.numel();
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && y.size(1) == H);
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(y.device());
+  const int rows = (int)(N * C);
+  launch_k(ep_combine_send2_kernel, std::max(1, std::min(296, (rows + 7) / 8)), 256, 0,
+           at::cuda::getCurrentCUDAStream(), a, (const int*)offs.data_ptr<int>(),
+           reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Combine, second half, fused with the next add + RMSNorm:
+// residual [T, H] += sum_k wts * comb rows; out = rmsnorm(residual) * w.
+void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                     const at::Tensor& map, const at::Tensor& wts, at::Tensor& residual, const at::Tensor& w,
+                     at::Tensor& out, double eps) {
+  const int64_t N = peers.numel(), T = out.size(0), H = out.size(1), K = wts.size(1);
+  TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous() && residual.size(0) == T &&
+              residual.size(1) == H && out.is_contiguous() && w.numel() == H && w.is_contiguous());
+  EpArgs a = make_args(peers, rank, N, C, H, El, state);
+  c10::cuda::CUDAGuard guard(out.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int wpb = 8;
+  const int grid = (int)std::max<int64_t>(1, (T + wpb - 1) / wpb);
+  auto r = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  auto pw = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto po = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+#define MB_CN(HH)                                                                                               \
+  case HH:                                                                                                      \
+    launch_k(ep_combine_norm_kernel<HH>, grid, wpb * 32, 0, st, a, (const int*)map.data_ptr<int>(),            \
+             (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, pw, po, (float)eps);                      \
+    break;
+  switch (H) {
+    MB_CN(256) MB_CN(512) MB_CN(1024) MB_CN(2048) MB_CN(3072) MB_CN(4096)
+    default:
+      TORCH_CHECK(false, "ep_combine_norm: hidden size ", H, " not compiled");
+  }
+#undef MB_CN
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

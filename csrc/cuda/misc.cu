@@ -156,3 +156,42 @@ void verify_tokens(const at::Tensor& draft, const at::Tensor& target, at::Tensor
 }
 
 }  // namespace mb
+
+namespace mb {
+
+// Advances n live decode rows by one token on the device, so consecutive
+// replays of a captured decode step run at a growing context without host
+// work: ids[b] = sampled[b]; pos[b] += 1; ctx[b] += 1; slots[b] = the KV slot
+// of the new position in row b of the block table (-1 past the row's end).
+__global__ void decode_advance_kernel(const int64_t* __restrict__ sampled, int64_t* __restrict__ ids,
+                                      int* __restrict__ pos, int* __restrict__ ctx, int* __restrict__ slots,
+                                      const int* __restrict__ bt, int n, int max_blocks, int block_size) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n) return;
+  ids[b] = sampled[b];
+  const int p = pos[b] + 1;
+  pos[b] = p;
+  ctx[b] = ctx[b] + 1;
+  const int blk = p / block_size;
+  slots[b] = blk < max_blocks ? bt[(size_t)b * max_blocks + blk] * block_size + p % block_size : -1;
+}
+
+void decode_advance(const at::Tensor& sampled, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx, at::Tensor& slots,
+                    const at::Tensor& bt, int64_t n, int64_t block_size) {
+  TORCH_CHECK(sampled.scalar_type() == at::kLong && ids.scalar_type() == at::kLong);
+  TORCH_CHECK(pos.scalar_type() == at::kInt && ctx.scalar_type() == at::kInt && slots.scalar_type() == at::kInt &&
+              bt.scalar_type() == at::kInt && bt.dim() == 2 && bt.is_contiguous());
+  TORCH_CHECK(n <= sampled.numel() && n <= ids.numel() && n <= pos.numel() && n <= ctx.numel() &&
+              n <= slots.numel() && n <= bt.size(0));
+  if (n <= 0) return;
+  c10::cuda::CUDAGuard guard(ids.device());
+  launch_k(decode_advance_kernel, (unsigned)((n + 127) / 128), 128, 0, at::cuda::getCurrentCUDAStream(),
+           (const int64_t*)sampled.data_ptr<int64_t>(), ids.data_ptr<int64_t>(), pos.data_ptr<int>(),
+           ctx.data_ptr<int>(), slots.data_ptr<int>(), (const int*)bt.data_ptr<int>(), (int)n, (int)bt.size(1),
+           (int)block_size);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mb

@@ -88,6 +88,16 @@ std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
 int64_t ipc_open(const std::string& handle);
 void ipc_close(int64_t ptr);
 void ipc_free(int64_t ptr);
+void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                       const at::Tensor& x, const at::Tensor& wr, int64_t K, bool renorm, at::Tensor& ids,
+                       at::Tensor& wts, at::Tensor& map, at::Tensor& offs, at::Tensor& scratch, at::Tensor& logits);
+void ep_combine_send(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                     const at::Tensor& offs, const at::Tensor& y, int64_t H);
+void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
+                     const at::Tensor& map, const at::Tensor& wts, at::Tensor& residual, const at::Tensor& w,
+                     at::Tensor& out, double eps);
+void decode_advance(const at::Tensor& sampled, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx, at::Tensor& slots,
+                    const at::Tensor& bt, int64_t n, int64_t block_size);
 void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
 void swiglu(const at::Tensor& gu, at::Tensor& out);
 void argmax(const at::Tensor& logits, at::Tensor& out_idx, const c10::optional<at::Tensor>& out_val,
@@ -118,6 +128,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_buffer_bytes", &mb::ep_buffer_bytes);
   m.def("ep_dispatch", &mb::ep_dispatch);
   m.def("ep_dispatch2", &mb::ep_dispatch2);
+  m.def("ep_route_dispatch", &mb::ep_route_dispatch);
+  m.def("ep_combine_send", &mb::ep_combine_send);
+  m.def("ep_combine_norm", &mb::ep_combine_norm);
   m.def("vis_scatter_gemm", &mb::vis_scatter_gemm);
   m.def("vis_release", &mb::vis_release);
   m.def("vis_wait_merge", &mb::vis_wait_merge);
@@ -139,6 +152,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &mb::ipc_close);
   m.def("ipc_free", &mb::ipc_free);
   m.def("embed", &mb::embed);
+  m.def("decode_advance", &mb::decode_advance);
   m.def("swiglu", &mb::swiglu);
   m.def("argmax", &mb::argmax);
   m.def("verify_tokens", &mb::verify_tokens);

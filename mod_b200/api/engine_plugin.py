@@ -109,7 +109,7 @@ class EnginePlugin(TextModelPluginInterface):
             weights = random_weights(self._config, device=dev, dtype=dtype, seed=rt["seed"])
         self.engine = LLMEngine(self._config, weights=weights, backend=rt["backend"], device=dev,
                                 max_batch=rt["max_batch"], max_model_len=rt["max_model_len"],
-                                use_graphs=rt.get("use_graphs", True),
+                                use_graphs=rt.get("use_graphs"),
                                 prefix_caching=bool(rt.get("prefix_caching", False)),
                                 prefill_chunk=int(rt.get("prefill_chunk", 0)) or None)
         return self.engine

@@ -35,7 +35,7 @@ log = logging.getLogger("mod_b200.engine")
 class LLMEngine:
     def __init__(self, cfg: ModelConfig, weights: Optional[ModelWeights] = None, backend: str = "native",
                  device: Union[str, torch.device] = "cuda", max_batch: int = 128, max_model_len: int = 4096,
-                 num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: bool = True,
+                 num_blocks: Optional[int] = None, kv_mem_fraction: float = 0.85, use_graphs: Optional[bool] = None,
                  max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
                  expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
                  quantization: Optional[str] = None, prefix_caching: bool = False,
@@ -46,7 +46,9 @@ class LLMEngine:
         exchange tokens with the fused NVLink dispatch/combine (native backend)
         or NCCL all-to-all (torch backend).  ``quantization="int8"`` stores the
         projection matrices as int8 with per-channel scales (int8 weight-only
-        GEMMs); expert weights stay bf16 under expert parallelism."""
+        GEMMs); expert weights stay bf16 under expert parallelism.
+        ``use_graphs`` (default: on for the native backend, off for the torch
+        baseline): capture each padded decode batch size in a CUDA graph."""
         import torch.distributed as dist
 
         self.cfg = cfg
@@ -82,7 +84,7 @@ class LLMEngine:
 
             moe_impl = (FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
                                    prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
-                        if backend == "native" else NcclEPMoE(cfg, self.backend))
+                        if backend == "native" else NcclEPMoE(cfg, self.backend, max_tokens=max_batch))
         if weights is None and model is None:
             weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
         if quantization not in (None, "none", "int8"):
@@ -96,7 +98,9 @@ class LLMEngine:
         bs = 16
         if num_blocks is None:
             num_blocks = self._auto_blocks(kv_mem_fraction, max_batch, max_model_len, kv_heads)
-        self.kv = KVCache(cfg, num_blocks, self.device, dtype=torch.float32 if backend == "cpu" else self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
+        # one block more than the allocator hands out: the last block is scratch that padded rows of a captured
+        # decode step may write into (library-only path), so no live sequence's KV is touched
+        self.kv = KVCache(cfg, num_blocks + 1, self.device, dtype=torch.float32 if backend == "cpu" else self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
         has_delta = any(cfg.layer_type(i) == "linear_attention" for i in range(cfg.num_hidden_layers))
         self.states = StateCache(cfg, max_batch + 1, self.device) if has_delta else None
         # prefix caching shares KV blocks of common prompt prefixes; models with recurrent
@@ -111,7 +115,8 @@ class LLMEngine:
         self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
                                    prefill_chunk=prefill_chunk)
         self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
-                                  use_graphs=use_graphs and backend == "native", device=self.device)
+                                  use_graphs=(backend == "native") if use_graphs is None else (use_graphs and backend != "cpu"),
+                                  device=self.device)
         from .sampler import Sampler
 
         self.runner.sampler = Sampler()

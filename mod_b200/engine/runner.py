@@ -134,7 +134,9 @@ class ModelRunner:
         self.graphs[B] = g
         self.graph_out[B] = out
 
-    def decode(self, seqs: List[Sequence], return_logits: bool = False):
+    def _prepare_decode(self, seqs: List[Sequence]) -> int:
+        """Fills the pinned step buffers for ``seqs`` and copies them to the
+        device; returns the padded batch size."""
         n = len(seqs)
         B = _bucket(n, self.buckets) if self.use_graphs else n
         bs = self.blocks.block_size
@@ -168,6 +170,11 @@ class ModelRunner:
                     self.n_bt[i, :] = 0
                     rows[i] = (-1, 0, 0)
         self._copy_in(B)
+        return B
+
+    def decode(self, seqs: List[Sequence], return_logits: bool = False):
+        n = len(seqs)
+        B = self._prepare_decode(seqs)
         sampling = self.sampler is not None and any(s.params.temperature > 0 for s in seqs)
         if return_logits:
             h = self.model.forward(self._fb_decode(B), self.kv, self.states)
@@ -191,6 +198,44 @@ class ModelRunner:
         for s in seqs:
             s.num_cached = s.length
         return self.h_out[:n].tolist()
+
+    def device_stepper(self, seqs: List[Sequence]):
+        """Greedy decode steps that run entirely on the device, for timing.
+
+        Returns a callable; each call replays the captured decode step for
+        ``seqs`` and then advances every live row by one token on the device
+        (next input = sampled token, position and context + 1, KV slot from the
+        block table), so consecutive calls decode at a growing context with no
+        host work in between.  The caller must have grown every sequence's
+        block table to cover the positions the calls will reach.  The host-side
+        sequences are not updated: the next ``decode`` rewrites every row."""
+        assert self.use_graphs, "device steps replay the captured decode graph"
+        n = len(seqs)
+        B = self._prepare_decode(seqs)
+        if B not in self.graphs:
+            self.capture(B)
+            self._copy_in(B)
+        g, out, bs = self.graphs[B], self.graph_out[B], self.blocks.block_size
+        native = getattr(self.model.be, "name", "") == "native"
+        if native:
+            from ..ops import load_extension
+
+            C = load_extension()
+
+            def step():
+                g.replay()
+                C.decode_advance(out, self.d_ids, self.d_pos, self.d_ctx, self.d_slots, self.d_bt, n, bs)
+        else:  # library-only arm: the same update as torch ops
+            rows = torch.arange(n, device=self.device)
+
+            def step():
+                g.replay()
+                self.d_ids[:n].copy_(out[:n])
+                self.d_pos[:n] += 1
+                self.d_ctx[:n] += 1
+                p = self.d_pos[:n].long()
+                self.d_slots[:n] = (self.d_bt[rows, p // bs] * bs + p % bs).int()
+        return step
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, seqs: List[Sequence], query_lens: List[int], inputs_embeds=None, return_logits: bool = False):

@@ -104,6 +104,8 @@ class DecoderLM:
         cfg, be = self.cfg, self.be
         if L.moe is not None:
             if self.moe_impl is not None:
+                if getattr(self.moe_impl, "supports_defer", False):
+                    return self.moe_impl(x, L.moe, defer=True)
                 return self.moe_impl(x, L.moe)
             return be.moe(x, L.moe, cfg.num_experts_per_tok, cfg.norm_topk_prob, cfg.moe_intermediate_size)
         m = L.mlp
@@ -130,7 +132,7 @@ class DecoderLM:
                 residual = hidden.clone()
                 x = be.rmsnorm(hidden, L.in_norm, eps)
             else:
-                x = be.rmsnorm(hidden, L.in_norm, eps, residual=residual)
+                x = self._add_norm(hidden, L.in_norm, eps, residual)
             if L.kind == "full_attention":
                 hidden = self._attention(i, L, x, fb, kv)
             else:
@@ -139,8 +141,15 @@ class DecoderLM:
             hidden = self._mlp(L, x)
             if nv:
                 torch.cuda.nvtx.range_pop()
-        x = be.rmsnorm(hidden, w.final_norm, eps, residual=residual)
+        x = self._add_norm(hidden, w.final_norm, eps, residual)
         return x.index_select(0, fb.logits_idx)
+
+    def _add_norm(self, hidden, w, eps, residual):
+        """residual += hidden; returns rmsnorm(residual) * w.  An expert-parallel
+        MoE output still in flight finishes its combine inside this step."""
+        if hasattr(hidden, "add_norm"):
+            return hidden.add_norm(residual, w, eps)
+        return self.be.rmsnorm(hidden, w, eps, residual=residual)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         return self.be.linear(h, self.w.lm_head)

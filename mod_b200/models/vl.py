@@ -350,7 +350,7 @@ class VisionLanguageEnginePlugin(EnginePlugin):
         self.vl = VLModel(cfg, tw, vw, be, image_size=rt.get("image_size", self.image_size))
         self.engine = LLMEngine(cfg.text, model=self.vl, backend=rt["backend"], device=dev,
                                 max_batch=rt["max_batch"], max_model_len=max(rt["max_model_len"], 512),
-                                use_graphs=rt.get("use_graphs", True))
+                                use_graphs=rt.get("use_graphs"))
         return self.engine
 
     def infer(self, data):

@@ -73,6 +73,15 @@ def rope_qknorm(qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, 
     if slots is not None:
         bs = k_cache.shape[2]
         valid = slots >= 0
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            # fixed shapes inside a graph: padded rows (slot -1) write into the cache's last block,
+            # which the engine keeps out of the allocator as scratch
+            scratch = (k_cache.shape[0] - 1) * bs + torch.arange(T, device=slots.device) % bs
+            s = torch.where(valid, slots.long(), scratch)
+            blk, off = s // bs, s % bs
+            k_cache[blk, :, off, :] = k
+            v_cache[blk, :, :, off] = v
+            return q_out
         s = slots[valid].long()
         blk, off = s // bs, s % bs
         k_cache[blk, :, off, :] = k[valid]

@@ -41,11 +41,30 @@ def run(rank, world, impl, port, device_kind):
         moe = FusedEPMoE(cfg, be, max_tokens=16)
     scale = ref.float().abs().max().item()
     assert scale > 0, "reference MoE output is all zeros"
-    for rep in range(3):  # repeated calls exercise the epoch / buffer reuse
-        out = moe(x, shard.layers[0].moe)
-        err = (out.float() - ref.float()).abs().max().item()
-        tol = 1e-4 if dtype == torch.float32 else 3e-2  # relative to the output's magnitude
-        assert err < tol * scale, f"rank {rank} rep {rep}: max err {err} vs scale {scale}"
+    tol = 1e-4 if dtype == torch.float32 else 3e-2  # relative to the output's magnitude
+    modes = [None]
+    if impl == "fused":  # separate router / top-k / dispatch launches, then the fused route + dispatch kernel
+        modes = [False, True]
+    for fused_route in modes:
+        if fused_route is not None:
+            moe.fused_route = fused_route
+        for rep in range(3):  # repeated calls exercise the epoch / buffer reuse
+            out = moe(x, shard.layers[0].moe)
+            err = (out.float() - ref.float()).abs().max().item()
+            assert err < tol * scale, f"rank {rank} rep {rep} fused_route={fused_route}: max err {err} vs scale {scale}"
+    if impl == "fused":
+        # combine deferred into the next residual add + RMSNorm
+        from mod_b200.ops import reference as R
+
+        nw = (1.0 + 0.1 * torch.randn(cfg.hidden_size, device=dev)).to(dtype)
+        for rep in range(2):
+            res = (torch.randn(T, cfg.hidden_size, device=dev) * 0.5).to(dtype)
+            res_ref = res.clone()
+            want = R.rmsnorm(ref.to(dtype), nw, 1e-6, residual=res_ref)
+            got = moe(x, shard.layers[0].moe, defer=True).add_norm(res, nw, 1e-6)
+            assert torch.allclose(res.float(), res_ref.float(), rtol=2e-2, atol=2e-2 * res_ref.float().abs().max().item())
+            err = (got.float() - want.float()).abs().max().item()
+            assert err < 3e-2 * want.float().abs().max().item(), f"rank {rank} deferred combine: max err {err}"
     if device_kind != "cpu":
         from mod_b200.ops import check_status
         torch.cuda.synchronize()

@@ -22,7 +22,7 @@ def run(rank, world, backend, port, device_kind):
     dev = torch.device("cpu") if device_kind == "cpu" else torch.device("cuda", rank)
     dtype = torch.float32 if device_kind == "cpu" else torch.bfloat16
     cfg = get_preset("tiny-dense")
-    cfg.num_attention_heads, cfg.num_key_value_heads = 8, 4
+    cfg.num_attention_heads, cfg.num_key_value_heads = max(8, 2 * world), max(4, world)  # heads divide the ranks
     w = random_weights(cfg, device=dev, dtype=dtype, seed=0)
     g = torch.Generator().manual_seed(3)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (7, 19, 3)]

@@ -47,7 +47,7 @@ def test_ep_multi_gpu(cuda, impl):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs")
-    n = 2 if n < 4 else 4
+    n = min(n, 8)  # every visible GPU (up to 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_ep_worker.py"), impl]
@@ -101,7 +101,7 @@ def test_tp_multi_gpu(cuda, backend):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs")
-    n = 2 if n < 4 else 4
+    n = min(n, 8)  # every visible GPU (up to 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), backend]

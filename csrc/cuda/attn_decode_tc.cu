@@ -78,14 +78,30 @@ struct TileCursor {
   int B, Hkv, splits, chunk_blocks, items;
   const int* ctx_lens;
   int max_blocks;
+  int* work;            // [2] device: next item ticket, finished CTAs (zero between launches)
+  int* ticket;          // shared-memory slot that thread 0 publishes each ticket in
   int b, hk, sp, lo, hi, nblk;  // current item
+  // Items are handed out one at a time from a device counter (longest-first
+  // order: every sequence's first chunk, then every second chunk, ...), so a
+  // CTA that finishes early takes more work instead of the grid waiting on the
+  // CTAs that drew two long items.  All threads of the CTA call next() at the
+  // same points, so the barriers inside are reached by every thread.
+  // work == nullptr: static round-robin (item = blockIdx.x, + gridDim.x, ...).
+  __device__ int fetch() {
+    if (!work) return item < 0 ? (int)blockIdx.x : item + (int)gridDim.x;
+    __syncthreads();
+    if (threadIdx.x == 0) *ticket = atomicAdd(work, 1);
+    __syncthreads();
+    return *ticket;
+  }
   __device__ bool next(TileRef& r, __nv_bfloat16* out, float* part_o, float* part_lse) {
     while (t + 1 >= nt) {
-      item += gridDim.x;
+      item = fetch();
       if (item >= items) return false;
-      sp = item % splits;
-      hk = (item / splits) % Hkv;
-      b = item / (splits * Hkv);
+      const int bh = item % (B * Hkv);
+      sp = item / (B * Hkv);
+      hk = bh % Hkv;
+      b = bh / Hkv;
       const int ctx = min(ctx_lens[b], max_blocks * 16);  // never past the block-table row
       nblk = (ctx + 15) / 16;
       const int blo = min(nblk, sp * chunk_blocks), bhi = min(nblk, blo + chunk_blocks);
@@ -96,12 +112,12 @@ struct TileCursor {
       if (nt == 0) {  // empty chunk: write its output now and move on
         for (int i = threadIdx.x; i < G * 128; i += blockDim.x) {
           const int h = i / 128, d = i % 128;
-          const size_t bh = (size_t)b * Hkv * G + hk * G + h;
+          const size_t bh2 = (size_t)b * Hkv * G + hk * G + h;
           if (splits == 1) {
-            out[bh * 128 + d] = __float2bfloat16(0.f);
+            out[bh2 * 128 + d] = __float2bfloat16(0.f);
           } else {
-            part_o[(bh * splits + sp) * 128 + d] = 0.f;
-            if (d == 0) part_lse[bh * splits + sp] = -INFINITY;
+            part_o[(bh2 * splits + sp) * 128 + d] = 0.f;
+            if (d == 0) part_lse[bh2 * splits + sp] = -INFINITY;
           }
         }
       }
@@ -121,7 +137,7 @@ __global__ void __launch_bounds__(128, 1)
                           const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables,
                           const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
                           float* __restrict__ part_o, float* __restrict__ part_lse, int B, int Hkv, int max_blocks,
-                          int splits, int chunk_blocks, float scale_log2, int* status) {
+                          int splits, int chunk_blocks, float scale_log2, int* status, int* work) {
   constexpr int D = 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -134,6 +150,7 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(red_sum + 64); // K, V, S, O
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* ticket = abort_flag + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int Hq = Hkv * G;
@@ -169,8 +186,7 @@ __global__ void __launch_bounds__(128, 1)
   pdl_trigger();
 
   // tile descriptors: cur (being computed) and nxt (being loaded)
-  TileCursor<G> cursor{(int)blockIdx.x - (int)gridDim.x, 0, 0, B, Hkv, splits, chunk_blocks, items, ctx_lens,
-                       max_blocks};
+  TileCursor<G> cursor{-1, 0, 0, B, Hkv, splits, chunk_blocks, items, ctx_lens, max_blocks, work, ticket};
   TileRef cur, nxt;
   bool has_cur = cursor.next(cur, out, part_o, part_lse);
   bool has_nxt = false;
@@ -331,6 +347,11 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 32);
   }
+  // the last CTA to finish resets the work counter for the next launch (no CTA fetches any more)
+  if (work && tid == 0 && atomicAdd(work + 1, 1) == (int)gridDim.x - 1) {
+    work[0] = 0;
+    work[1] = 0;
+  }
 }
 
 }  // namespace
@@ -342,7 +363,7 @@ bool attn_decode_tc_supported(int64_t D, int64_t G) {
 // Same contract as attn_decode (attn_decode.cu); head_dim 128, group <= 16.
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
-                    const c10::optional<at::Tensor>& workspace, double scale) {
+                    const c10::optional<at::Tensor>& workspace, double scale, at::Tensor& work) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && out.is_contiguous());
   TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.size(2) == 16 && v_cache.size(3) == 16);
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt &&
@@ -352,6 +373,9 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
   TORCH_CHECK(Hq % Hkv == 0 && k_cache.size(3) == D && v_cache.size(2) == D);
   const int G = Hq / Hkv;
   TORCH_CHECK(attn_decode_tc_supported(D, G), "attn_decode_tc: needs head_dim 128 and group <= 16");
+  TORCH_CHECK(work.scalar_type() == at::kInt && work.is_cuda() && (work.numel() == 0 || work.numel() >= 2),
+              "attn_decode_tc: work must be empty (static schedule) or a zeroed int32 device tensor of 2 "
+              "elements (dynamic schedule; kept zero by the kernel)");
   if (B == 0) return;
   splits = std::max<int64_t>(1, splits);
   float* po = nullptr;
@@ -387,7 +411,8 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
     launch_k(kernel, grid, 128, kSmemBytes, st, tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
                                           block_tables.data_ptr<int>(), ctx_lens.data_ptr<int>(),
                                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), po, pl, B, Hkv, mbk,
-                                          (int)splits, chunk_blocks, sl2, status_ptr(q.device().index()));
+                                          (int)splits, chunk_blocks, sl2, status_ptr(q.device().index()),
+                                          work.numel() ? work.data_ptr<int>() : nullptr);
   };
   switch (G) {
     case 1: go(attn_decode_tc_kernel<1>, 1); break;

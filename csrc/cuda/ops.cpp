@@ -54,7 +54,7 @@ void vis_wait_merge(const at::Tensor& peers, int64_t rank, int64_t off, int64_t 
                     const at::Tensor& rows, at::Tensor& h);
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
-                    const c10::optional<at::Tensor>& workspace, double scale);
+                    const c10::optional<at::Tensor>& workspace, double scale, at::Tensor& work);
 bool attn_decode_tc_supported(int64_t D, int64_t G);
 void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                      const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,

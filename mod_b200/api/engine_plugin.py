@@ -27,7 +27,7 @@ log = logging.getLogger("mod_b200.plugin")
 
 _RUNTIME_KEYS = {"device", "backend", "max_batch", "max_model_len", "max_prefill_tokens", "seed", "model_path",
                  "use_graphs", "kv_mem_fraction", "max_new_tokens", "dtype", "prefix_caching",
-                 "prefill_chunk"}
+                 "prefill_chunk", "offload", "offload_layers"}
 
 
 class EnginePlugin(TextModelPluginInterface):
@@ -111,7 +111,9 @@ class EnginePlugin(TextModelPluginInterface):
                                 max_batch=rt["max_batch"], max_model_len=rt["max_model_len"],
                                 use_graphs=rt.get("use_graphs"),
                                 prefix_caching=bool(rt.get("prefix_caching", False)),
-                                prefill_chunk=int(rt.get("prefill_chunk", 0)) or None)
+                                prefill_chunk=int(rt.get("prefill_chunk", 0)) or None,
+                                offload_layers=(int(rt.get("offload_layers", 0)) or
+                                                ("auto" if rt.get("offload") else None)))
         return self.engine
 
     def cleanup(self) -> bool:

@@ -95,14 +95,21 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
 
     async def _generate_stop(ids: List[int], params: SamplingParams, stop: List[str]):
         """Generate until a stop string appears in the decoded text; the request is cancelled
-        there (its KV blocks freed) and the text cut before the stop string."""
+        there (the stream is closed at once, which frees its KV blocks), the text is cut before
+        the stop string and the token ids are trimmed to the tokens whose text ends before it."""
+        import contextlib
+
         out: List[int] = []
-        async for tok in front.stream(ids, params):
-            out.append(tok)
-            text = tokenizer.decode(out)
-            cut = min((text.find(x) for x in stop if x and x in text), default=-1)
-            if cut >= 0:
-                return out, text[:cut], "stop"
+        async with contextlib.aclosing(front.stream(ids, params)) as gen:
+            async for tok in gen:
+                out.append(tok)
+                text = tokenizer.decode(out)
+                cut = min((text.find(x) for x in stop if x and x in text), default=-1)
+                if cut >= 0:
+                    keep = len(out)
+                    while keep > 0 and len(tokenizer.decode(out[:keep])) > cut:
+                        keep -= 1
+                    return out[:keep], text[:cut], "stop"
         return out, tokenizer.decode(out), ("length" if len(out) >= params.max_new_tokens else "stop")
 
     @app.get("/health")

@@ -3,8 +3,10 @@
     python -m mod_b200.bench.kernels --case moe_gateup [--iters 20]
 
 Each case builds its inputs once (weights rotated across copies when they
-would fit in L2), times ``iters`` launches with CUDA events after warm-up,
-and prints one JSON line: microseconds per launch, algorithmic bytes and
+would fit in L2), captures ``iters`` launches in one CUDA graph after warm-up
+and times its replay with CUDA events (so host dispatch cost, which dominates
+a 5-15 us kernel launched from Python, is not in the number; ``--eager`` times
+plain launches instead), and prints one JSON line: microseconds per launch, algorithmic bytes and
 FLOPs, achieved bandwidth / throughput and the fraction of the measured
 peaks (``MEASURED_PEAKS.json`` when present, else 6.65 TB/s and
 1.59 PFLOP/s).  The same cases are what the committed ncu summaries profile.
@@ -34,12 +36,23 @@ def _rot(make, nbytes, limit=512e6):
     return [make() for _ in range(n)]
 
 
-def case(name: str):
+def case(name: str, T: int = 128):
     from ..ops import native as N
 
     dev = "cuda"
     bf = torch.bfloat16
-    T = 128
+    if name.startswith("cublas:"):  # the same GEMM shapes through torch.matmul (cuBLAS), for comparison
+        K, Nn = {"qkv": (2048, 5120), "o": (4096, 2048), "lm_head": (2048, 151936),
+                 "router": (2048, 128)}[name.split(":")[1]]
+        ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)
+        x = torch.randn(T, K, device=dev).to(bf)
+        y = torch.empty(T, Nn, device=dev, dtype=bf)
+        i = [0]
+
+        def run():
+            torch.matmul(x, ws[i[0] % len(ws)].t(), out=y)
+            i[0] += 1
+        return run, K * Nn * 2 + T * K * 2 + T * Nn * 2, 2 * T * K * Nn
     if name in ("qkv", "o", "lm_head", "router"):
         K, Nn = {"qkv": (2048, 5120), "o": (4096, 2048), "lm_head": (2048, 151936), "router": (2048, 128)}[name]
         ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)
@@ -69,7 +82,7 @@ def case(name: str):
         out = torch.empty(T * k, H, device=dev, dtype=bf)
         return (lambda: N.grouped_linear(xs, w, offs, E, False, 32, out=out)), w.numel() * 2, 2 * T * k * H * I
     if name in ("attn_decode", "attn_prefill"):
-        B, Hq, Hkv, D = 128, 32, 4, 128
+        B, Hq, Hkv, D = (T if name == "attn_decode" else 128), 32, 4, 128
         ctx = 600 if name == "attn_decode" else 512
         nbps = (ctx + 15) // 16
         nb = B * nbps + 8
@@ -78,10 +91,12 @@ def case(name: str):
         bt = torch.randperm(nb - 8, device=dev)[: B * nbps].view(B, nbps).int().contiguous()
         cl = torch.full((B,), ctx, device=dev, dtype=torch.int32)
         kv_bytes = B * ctx * Hkv * D * 2 * 2
-        if name == "attn_decode":
+        if name == "attn_decode":  # the engine's own launch policy (chunking, split-KV combine)
+            from ..models.backend import NativeBackend
+
+            be = NativeBackend()
             q = torch.randn(B, Hq, D, device=dev).to(bf)
-            ws = torch.empty(B * Hq * 4 * (D + 1), device=dev)
-            return (lambda: N.attn_decode_tc(q, kc, vc, bt, cl, splits=1, workspace=ws)), kv_bytes, 4 * B * Hq * ctx * D
+            return (lambda: be.attn_decode(q, kc, vc, bt, cl)), kv_bytes, 4 * B * Hq * ctx * D
         q = torch.randn(B * ctx, Hq, D, device=dev).to(bf)
         cu = torch.arange(B + 1, device=dev, dtype=torch.int32) * ctx
         flops = 4 * B * Hq * D * ctx * (ctx + 1) // 2
@@ -194,24 +209,41 @@ def main(argv=None):
     ap.add_argument("--case", default="all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--tokens", type=int, default=128, help="decode tokens (T) of the GEMM / attention cases")
+    ap.add_argument("--eager", action="store_true", help="time plain launches instead of a graph replay")
     a = ap.parse_args(argv)
     bw_peak, fl_peak, src = peaks()
     for name in (CASES if a.case == "all" else a.case.split(",")):
-        run, nbytes, flops = case(name)
+        run, nbytes, flops = case(name, a.tokens)
         for _ in range(a.warmup):
             run()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(True), torch.cuda.Event(True)
-        s.record()
-        for _ in range(a.iters):
-            run()
-        e.record()
+        if a.eager:
+            s.record()
+            for _ in range(a.iters):
+                run()
+            e.record()
+        else:
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(a.iters):
+                    run()
+            torch.cuda.synchronize()
+            g.replay()  # warm
+            torch.cuda.synchronize()
+            s.record()
+            g.replay()
+            e.record()
         torch.cuda.synchronize()
         us = s.elapsed_time(e) * 1000 / a.iters
-        rec = {"case": name, "us": round(us, 2), "bytes": nbytes, "flops": flops,
+        rec = {"case": name, "tokens": a.tokens, "us": round(us, 2), "bytes": nbytes, "flops": flops,
                "TBps": round(nbytes / us / 1e6, 3), "TFLOPs": round(flops / us / 1e6, 2),
                "frac_bw": round(nbytes / us / 1e6 / (bw_peak / 1e12), 3),
-               "frac_tc": round(flops / us / 1e6 / (fl_peak / 1e12), 3), "peaks": src}
+               "frac_tc": round(flops / us / 1e6 / (fl_peak / 1e12), 3), "peaks": src,
+               "timing": "eager launches" if a.eager else "CUDA-graph replay"}
         print(json.dumps(rec), flush=True)
         del run
         torch.cuda.empty_cache()

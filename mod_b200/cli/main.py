@@ -52,6 +52,9 @@ def _opts(args) -> dict:
         o["device"] = args.device
     if getattr(args, "backend", None):
         o["backend"] = args.backend
+    off = getattr(args, "offload_layers", None)
+    if off:  # hybrid CPU/GPU execution: "auto" (planner) or a layer count
+        o["offload_layers" if off != "auto" else "offload"] = int(off) if off != "auto" else True
     return o
 
 
@@ -247,6 +250,7 @@ def build_parser() -> argparse.ArgumentParser:
         p.add_argument("--backend", choices=["native", "torch", "cpu"])
         p.add_argument("--max-new-tokens", type=int, default=64)
         p.add_argument("--set", nargs="*", help="config overrides key=value")
+        p.add_argument("--offload-layers", help="stream the last N layers from pinned host memory ('auto': planner)")
         if name == "run":
             p.add_argument("--prompt", required=True)
             p.add_argument("--temperature", type=float, default=0.0)

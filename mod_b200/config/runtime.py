@@ -53,7 +53,8 @@ class RuntimeConfig:
     debug_bounds: bool = False
     seed: int = 0
     threads: int = 0                     # CPU backend OpenMP threads (0: default)
-    offload: bool = False                # hybrid CPU/GPU weight streaming
+    offload: bool = False                # hybrid CPU/GPU weight streaming (layer count from the planner)
+    offload_layers: int = 0              # >0: stream this many trailing layers from pinned host memory
     prefix_caching: bool = False         # share KV blocks of common prompt prefixes
     prefill_chunk: int = 0               # >0: prefill prompts in chunks of this many tokens
     extra: Dict[str, Any] = field(default_factory=dict)

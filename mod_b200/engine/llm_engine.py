@@ -39,7 +39,8 @@ class LLMEngine:
                  max_prefill_tokens: int = 16384, seed: int = 0, model=None, kv_heads: Optional[int] = None,
                  expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
                  quantization: Optional[str] = None, prefix_caching: bool = False,
-                 prefill_chunk: Optional[int] = None):
+                 prefill_chunk: Optional[int] = None, kv_swap: bool = True, kv_swap_bytes: int = 8 << 30,
+                 offload_layers: Union[int, str, None] = None):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
@@ -48,11 +49,23 @@ class LLMEngine:
         projection matrices as int8 with per-channel scales (int8 weight-only
         GEMMs); expert weights stay bf16 under expert parallelism.
         ``use_graphs`` (default: on for the native backend, off for the torch
-        baseline): capture each padded decode batch size in a CUDA graph."""
+        baseline): capture each padded decode batch size in a CUDA graph.
+        ``kv_swap``: a sequence preempted for KV space keeps its KV in pinned
+        host memory (up to ``kv_swap_bytes``) and resumes without recomputing.
+        ``offload_layers`` (hybrid CPU/GPU execution): the last N decoder layers
+        live in pinned host memory and are streamed to the device one layer
+        ahead of use (``runtime.offload.LayerStreamer``); ``"auto"`` takes N
+        from the placement planner for this device's memory.  Streaming runs
+        eagerly (no decode graphs)."""
         import torch.distributed as dist
 
         self.cfg = cfg
         self.device = torch.device(device)
+        from ..runtime.memory import UnifiedMemoryManager
+
+        # one owner of this rank's device memory: it records the free memory before any weight exists
+        # and sizes the KV pool from what the weights, buffers and workspace leave
+        self.memory = UnifiedMemoryManager(self.device)
         world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
         rank = dist.get_rank() if world > 1 else 0
         if expert_parallel is None:
@@ -95,9 +108,23 @@ class LLMEngine:
             quantize_model(weights, experts=not expert_parallel)
         self.quantization = quantization
         self.model = model if model is not None else DecoderLM(cfg, weights, self.backend, moe_impl=moe_impl)
+        self.streamer = None
+        if offload_layers == "auto":
+            from ..parallel.planner import plan
+
+            hbm = torch.cuda.get_device_properties(self.device).total_memory if self.device.type == "cuda" else 0
+            offload_layers = plan(cfg, 1, hbm_bytes=hbm).offload_layers if hbm else 0
+        if offload_layers and self.device.type == "cuda" and hasattr(self.model, "layer_source"):
+            from ..runtime.offload import enable_streaming
+
+            n = min(int(offload_layers), cfg.num_hidden_layers)
+            self.streamer = enable_streaming(self.model, cfg.num_hidden_layers - n)
+            use_graphs = False  # the streamer's copy schedule is decided per step on the host
         bs = 16
         if num_blocks is None:
             num_blocks = self._auto_blocks(kv_mem_fraction, max_batch, max_model_len, kv_heads)
+        else:
+            self.memory.define("kv", (num_blocks + 1) * KVCache.bytes_per_block(cfg, num_kv_heads=kv_heads or self.model.Hkv))
         # one block more than the allocator hands out: the last block is scratch that padded rows of a captured
         # decode step may write into (library-only path), so no live sequence's KV is touched
         self.kv = KVCache(cfg, num_blocks + 1, self.device, dtype=torch.float32 if backend == "cpu" else self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
@@ -114,6 +141,25 @@ class LLMEngine:
             prefill_chunk = None
         self.scheduler = Scheduler(self.blocks, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens,
                                    prefill_chunk=prefill_chunk)
+        # KV swap on preemption (attention-only models without prefix sharing): the preempted
+        # sequence's blocks go to pinned host memory and come back into fresh blocks later
+        self.swapper = None
+        if kv_swap and self.states is None and not self.prefix_caching and self.kv.k:
+            from ..runtime.memory import KVSwapper, PinnedPool
+
+            self.swapper = KVSwapper(self.kv, PinnedPool(kv_swap_bytes))
+            self.memory.define("host_swap", kv_swap_bytes)
+
+            def on_preempt(seq):
+                try:
+                    self.swapper.swap_out(seq.req_id, list(seq.blocks))
+                except Exception as e:  # pinned pool exhausted: fall back to recomputation
+                    log.warning("KV swap-out failed (%s); request %d will be recomputed", e, seq.req_id)
+                    return False
+                return True
+
+            self.scheduler.on_preempt = on_preempt
+            self.scheduler.on_resume = lambda seq: self.swapper.swap_in(seq.req_id, list(seq.blocks))
         self.runner = ModelRunner(self.model, self.kv, self.states, self.blocks, max_batch, max_model_len,
                                   use_graphs=(backend == "native") if use_graphs is None else (use_graphs and backend != "cpu"),
                                   device=self.device)
@@ -131,13 +177,19 @@ class LLMEngine:
         return cls(get_preset(name), **kw)
 
     def _auto_blocks(self, frac, max_batch, max_model_len, kv_heads) -> int:
+        """KV blocks for ``max_batch`` sequences of ``max_model_len`` tokens, capped by what the
+        memory manager has left after the weights and buffers already allocated on this device."""
         per_block = KVCache.bytes_per_block(self.cfg, num_kv_heads=kv_heads or self.model.Hkv)
         want = max_batch * ((max_model_len + 15) // 16) + max_batch
         if self.device.type != "cuda" or per_block == 0:
+            self.memory.define("kv", max(want, 16) * per_block)
             return max(want, 16)
-        free, _ = torch.cuda.mem_get_info(self.device)
-        cap = int(free * frac) // per_block
-        return max(16, min(want, cap))
+        free_now, _ = torch.cuda.mem_get_info(self.device)
+        used = max(0, self.memory.free_at_start - free_now)   # weights, exchange buffers, caches so far
+        cap = self.memory.plan_kv_blocks(per_block, used, workspace_bytes=1 << 30, fraction=frac) - 1
+        n = max(16, min(want, cap))
+        self.memory.define("kv", (n + 1) * per_block)
+        return n
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt: Seq[int], params: Optional[SamplingParams] = None, images=None,
@@ -225,4 +277,5 @@ class LLMEngine:
     def stats(self) -> Dict[str, float]:
         return {"free_blocks": self.blocks.num_free, "running": len(self.scheduler.running),
                 "waiting": len(self.scheduler.waiting), "preempted": self.scheduler.num_preempted,
+                "swapped_out": self.scheduler.num_swapped_out, "resumed": self.scheduler.num_resumed,
                 "h2d_bytes_last_step": self.runner.h2d_bytes, "d2h_bytes_last_step": self.runner.d2h_bytes}

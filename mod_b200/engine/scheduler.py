@@ -4,7 +4,11 @@ Each step is either a prefill step (new prompts, up to a token budget) or a
 decode step (one token for every running sequence).  Prefill is preferred
 while KV blocks and batch slots allow admission; when a decode step cannot
 get a block for every sequence, the most recently admitted sequence is
-preempted (blocks freed, sequence re-queued for recomputation).
+preempted: with a swap hook (the engine's ``KVSwapper``) its KV blocks are
+copied to pinned host memory, its device blocks freed, and it re-enters the
+running set later by copying them back into fresh blocks, with no
+recomputation; without one, its blocks are freed and it is re-queued for
+recomputation.
 
 The reference's ``BatchManager.step`` runs one request's full ``generate`` at
 a time, with no batching (``pio/common/managers/batch_manager.py:40-84``), and
@@ -41,6 +45,12 @@ class Scheduler:
         # alternate with decode steps of the sequences already generating
         self.prefill_chunk = prefill_chunk
         self._last_prefill = False
+        # KV swap hooks (set by the engine): on_preempt(seq) -> True when the sequence's KV was saved;
+        # on_resume(seq) copies it back into the sequence's (new) blocks
+        self.on_preempt = None
+        self.on_resume = None
+        self.num_swapped_out = 0
+        self.num_resumed = 0
 
     def add(self, seq: Sequence) -> None:
         seq.status = SeqStatus.WAITING
@@ -54,6 +64,8 @@ class Scheduler:
         budget = self.max_prefill_tokens
         while self.waiting and len(self.running) + len(picked) < self.max_batch:
             seq = self.waiting[0]
+            if seq.swapped:  # resumes by swap-in (``_resume_swapped``), never by a prefill
+                break
             n = seq.length if not self.prefill_chunk else min(seq.length, self.prefill_chunk)  # this step's tokens
             if picked and n > budget:
                 break
@@ -101,7 +113,24 @@ class Scheduler:
         self._last_prefill = False
         return None
 
+    def _resume_swapped(self) -> None:
+        """Swapped-out sequences at the head of the queue rejoin the running set when their
+        blocks (plus one decode slot) fit; their KV is copied back, no prefill needed."""
+        while self.waiting and self.waiting[0].swapped and len(self.running) < self.max_batch:
+            seq = self.waiting[0]
+            cached = seq.num_cached
+            if not self.blocks.allocate(seq, seq.length + 1):
+                break
+            self.waiting.popleft()
+            self.on_resume(seq)
+            seq.num_cached = cached
+            seq.swapped = False
+            seq.status = SeqStatus.RUNNING
+            self.running.append(seq)
+            self.num_resumed += 1
+
     def schedule(self) -> ScheduledStep:
+        self._resume_swapped()
         if self.prefill_chunk:
             st = self._schedule_chunked()
             if st is not None:
@@ -124,7 +153,13 @@ class Scheduler:
                 i += 1
                 continue
             victim = self.running.pop()          # newest admitted
+            cached = victim.num_cached
+            swapped = (self.on_preempt is not None and not self._partial(victim) and self.on_preempt(victim))
             self.blocks.release(victim)
+            if swapped:
+                victim.num_cached = cached
+                victim.swapped = True
+                self.num_swapped_out += 1
             victim.status = SeqStatus.WAITING
             self.waiting.appendleft(victim)
             self.num_preempted += 1

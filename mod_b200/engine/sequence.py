@@ -52,6 +52,7 @@ class Sequence:
     t_finish: Optional[float] = None
     images: Optional[object] = None   # pixel tensor for vision-language prompts
     callback: Optional[object] = None  # streaming: callback(seq, token)
+    swapped: bool = False             # preempted with its KV saved to host memory (resumes without recompute)
 
     @property
     def all_tokens(self) -> List[int]:

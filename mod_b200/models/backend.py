@@ -156,17 +156,30 @@ class NativeBackend:
     def attn_decode(self, q, k_cache, v_cache, block_tables, ctx_lens, splits=1):
         B, Hq, D = q.shape
         tc = self.N.attn_decode_tc_supported(D, Hq // k_cache.shape[1])
+        import os
+
+        impl = os.environ.get("MB_ATTN_IMPL", "tc")  # A/B timing: "cuda" forces the CUDA-core kernel
+        tc = tc and impl != "cuda"
+        dynamic = os.environ.get("MB_ATTN_DYNAMIC", "1") != "0"
+        chunk_env = os.environ.get("MB_ATTN_CHUNK")
         if tc:
-            # persistent tcgen05 kernel (2 CTAs per SM): split sequences into
-            # chunks only when (sequence, KV head) items cannot fill the GPU
+            # persistent tcgen05 kernel (3 CTAs per SM) with a dynamic work queue: sequences are cut
+            # into chunks of 2 KV tiles (16 blocks), or of 1 tile when that leaves fewer than two
+            # chunks per resident CTA, so the queue balances the CTAs; no split for short contexts
+            mb = block_tables.shape[1]
             items = B * k_cache.shape[1]
-            want = -(-2 * self._sms(q.device) // max(1, items))
-            splits = max(1, min(want, -(-block_tables.shape[1] // 8)))
+            chunk = 16 if items * -(-mb // 16) >= 2 * 3 * self._sms(q.device) else 8
+            if chunk_env is not None:  # blocks per chunk; 0 = whole sequences
+                chunk = int(chunk_env) or mb
+            splits = max(1, -(-mb // chunk))
+        elif chunk_env is not None:
+            splits = max(1, -(-block_tables.shape[1] // (int(chunk_env) or block_tables.shape[1])))
         ws = None
         if splits > 1:
             ws = torch.empty(B * Hq * splits * (D + 1), dtype=torch.float32, device=q.device)
         if tc:
-            return self.N.attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws)
+            return self.N.attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws,
+                                         dynamic=dynamic)
         return self.N.attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, splits=splits, workspace=ws)
 
     def attn_prefill(self, q, k, v):

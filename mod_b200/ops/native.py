@@ -80,14 +80,29 @@ def attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits: i
     return out
 
 
+_WORK = {}
+
+
+def _work_counter(device) -> torch.Tensor:
+    """Per-device int32[2] work queue of the decode-attention kernel; zero between
+    launches (the kernel's last CTA resets it), so one buffer serves every call."""
+    key = torch.device(device).index
+    if key not in _WORK:
+        _WORK[key] = torch.zeros(2, dtype=torch.int32, device=device)
+    return _WORK[key]
+
+
 def attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits: int = 1, workspace=None,
-                   scale: Optional[float] = None):
-    """tcgen05 flash-decode (head_dim 128, group <= 16); same contract as attn_decode."""
+                   scale: Optional[float] = None, dynamic: bool = True):
+    """tcgen05 flash-decode (head_dim 128, group <= 16); same contract as attn_decode.
+    Work items (sequence, KV head, chunk of ceil(max_blocks / splits) blocks) are
+    handed out dynamically, longest first."""
     if out is None:
         out = torch.empty_like(q)
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    _C().attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out, splits, workspace, scale)
+    work = _work_counter(q.device) if dynamic else torch.empty(0, dtype=torch.int32, device=q.device)
+    _C().attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out, splits, workspace, scale, work)
     return out
 
 

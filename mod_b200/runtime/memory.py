@@ -113,6 +113,8 @@ class KVSwapper:
     def swap_out(self, req_id: int, blocks: List[int]) -> None:
         bufs = []
         idx = torch.tensor(blocks, device=self.kv.k[0].device)
+        if self.stream:  # after every kernel that wrote these blocks
+            self.stream.wait_stream(torch.cuda.current_stream(self.kv.k[0].device))
         ctx = torch.cuda.stream(self.stream) if self.stream else _null()
         with ctx:
             for t in self.kv.k + self.kv.v:
@@ -126,9 +128,12 @@ class KVSwapper:
 
     def swap_in(self, req_id: int, blocks: List[int]) -> None:
         bufs = self.saved.pop(req_id)
-        idx = torch.tensor(blocks, device=self.kv.k[0].device)
+        idx = torch.tensor(blocks[:bufs[0].shape[0]], device=self.kv.k[0].device)  # the saved blocks' new homes
         for t, host in zip(self.kv.k + self.kv.v, bufs):
             t.index_copy_(0, idx, host.to(t.device, non_blocking=True))
+        if t.is_cuda:  # the host buffers go back to the pool only after the copies have read them
+            torch.cuda.current_stream(t.device).synchronize()
+        for host in bufs:
             self.pool.put(host.view(torch.uint8).view(-1))
 
     def has(self, req_id: int) -> bool:

@@ -50,3 +50,37 @@ def test_kv_swap_roundtrip_gpu(cuda):
         t.zero_()
     sw.swap_in(7, [10, 11])
     assert all(torch.equal(t[[10, 11]], b) for t, b in zip(kv.k + kv.v, before))
+
+
+def test_engine_offload_switch_generates_like_resident(cuda):
+    """The engine's ``offload_layers`` switch (runtime config / CLI --offload-layers) streams the
+    trailing layers from pinned host memory and generates the same tokens."""
+    cfg = get_preset("tiny-dense")
+    cfg.num_hidden_layers = 4
+    prompts = [[1, 2, 3, 4, 5], [9, 8, 7]]
+    w = random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0)
+    ref = LLMEngine(cfg, weights=w, backend="native", device=cuda, max_batch=2, max_model_len=64,
+                    use_graphs=False).generate(prompts, SamplingParams(max_new_tokens=5))
+    w2 = random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0)
+    eng = LLMEngine(cfg, weights=w2, backend="native", device=cuda, max_batch=2, max_model_len=64,
+                    offload_layers=2)
+    assert eng.streamer is not None and not w2.layers[3].attn.qkv.is_cuda and w2.layers[1].attn.qkv.is_cuda
+    assert eng.generate(prompts, SamplingParams(max_new_tokens=5)) == ref
+
+
+def test_preemption_swaps_kv_on_gpu(cuda):
+    """Native engine with decode graphs and a KV pool too small for every sequence: preempted
+    sequences resume from swapped KV, and the first generated tokens match an unpreempted run."""
+    cfg = get_preset("tiny-dense")
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (30, 17, 25, 9)]
+    params = SamplingParams(max_new_tokens=40, ignore_eos=True)
+    w = random_weights(cfg, device=cuda, dtype=torch.bfloat16, seed=0)
+    ref = LLMEngine(cfg, weights=w, backend="native", device=cuda, max_batch=4, max_model_len=96,
+                    num_blocks=64).generate(prompts, params)
+    eng = LLMEngine(cfg, weights=w, backend="native", device=cuda, max_batch=4, max_model_len=96, num_blocks=14)
+    out = eng.generate(prompts, params)
+    st = eng.stats()
+    assert st["preempted"] > 0 and st["resumed"] == st["swapped_out"] == st["preempted"]
+    agree = sum(a == b for x, y in zip(out, ref) for a, b in zip(x, y)) / sum(len(x) for x in ref)
+    assert all(x[:4] == y[:4] for x, y in zip(out, ref)) and agree >= 0.9, (out, ref)

@@ -96,6 +96,12 @@ void ep_combine_send(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
 void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                      const at::Tensor& map, const at::Tensor& wts, at::Tensor& residual, const at::Tensor& w,
                      at::Tensor& out, double eps);
+void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
+                    const c10::optional<at::Tensor>& residual, int64_t cs);
+void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& q_w,
+                      const c10::optional<at::Tensor>& k_w, const at::Tensor& positions, const at::Tensor& inv_freq,
+                      const c10::optional<at::Tensor>& slots, at::Tensor& q_out, at::Tensor& k_cache,
+                      at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs);
 void decode_advance(const at::Tensor& sampled, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx, at::Tensor& slots,
                     const at::Tensor& bt, int64_t n, int64_t block_size);
 void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
@@ -108,6 +114,8 @@ void verify_tokens(const at::Tensor& draft, const at::Tensor& target, at::Tensor
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mod_b200 sm_100a kernels";
   m.def("linear", &mb::linear);
+  m.def("linear_cluster", &mb::linear_cluster);
+  m.def("qkv_rope_cluster", &mb::qkv_rope_cluster);
   m.def("grouped_linear", &mb::grouped_linear);
   m.def("swiglu_linear", &mb::swiglu_linear);
   m.def("rmsnorm", &mb::rmsnorm);

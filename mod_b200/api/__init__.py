@@ -1,5 +1,5 @@
 """Plugin API: interfaces, plugin manager, backends, model factory."""
 from .interfaces import (HardwareBackendInterface, ModelPluginInterface, PluginMetadata, PluginType,  # noqa: F401
                          TextModelPluginInterface, VisionLanguagePluginInterface)
-from .manager import (ModelFactory, PluginManager, SecondaryPluginManager, SecondaryPluginType,  # noqa: F401
-                      create_model, get_plugin_manager)
+from .manager import (ModelFactory, PluginManager, SecondaryPlugin, SecondaryPluginManager,  # noqa: F401
+                      SecondaryPluginType, create_model, get_plugin_manager, get_secondary_plugin_manager)

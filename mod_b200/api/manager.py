@@ -152,9 +152,53 @@ class SecondaryPluginType(enum.Enum):
     SHARDING = "sharding"
 
 
+class SecondaryPlugin:
+    """A secondary (feature) plugin: a named factory whose ``initialize(**kw)``
+    builds the component, ``execute(*a, **kw)`` calls it, ``cleanup()`` drops it.
+    Same lifecycle as the reference's ``SecondaryPluginInterface``
+    (``pio/plugins/secondary_manager.py:20-66``)."""
+
+    def __init__(self, name: str, factory: Callable[..., Any], description: str = "",
+                 call: Optional[Callable[..., Any]] = None):
+        self.name, self.factory, self.description = name, factory, description
+        self._call = call
+        self.instance: Any = None
+
+    def initialize(self, **kw) -> bool:
+        try:
+            self.instance = self.factory(**kw)
+        except Exception as e:  # reported as a failed activation, like the reference
+            logging.getLogger("mod_b200.plugins").error("secondary plugin %s: %s", self.name, e)
+            self.instance = None
+            return False
+        return True
+
+    def execute(self, *a, **kw) -> Any:
+        if self._call is not None:
+            return self._call(self.instance, *a, **kw)
+        return self.instance(*a, **kw) if callable(self.instance) else self.instance
+
+    def cleanup(self) -> bool:
+        self.instance = None
+        return True
+
+
 class SecondaryPluginManager:
-    def __init__(self):
+    """Registry of secondary plugins by kind and name, with activation.
+
+    The default registrations (``register_defaults``) are the components this
+    engine actually uses: the unified memory manager, the two communication
+    backends (fused NVLink kernels / NCCL), adaptive admission, the pipeline
+    stage executor, the placement planner, the sm_100a kernel backend, int8
+    weight-only compression, memory budgets and layer streaming (the hybrid
+    CPU/GPU scheduler).  The reference's manager keeps one plugin per kind and
+    registers none (``pio/plugins/secondary_manager.py:69-165``)."""
+
+    def __init__(self, defaults: bool = False):
         self._reg: Dict[SecondaryPluginType, Dict[str, Any]] = {t: {} for t in SecondaryPluginType}
+        self.active: Dict[SecondaryPluginType, str] = {}
+        if defaults:
+            register_defaults(self)
 
     def register(self, kind: SecondaryPluginType, name: str, obj: Any) -> None:
         self._reg[kind][name] = obj
@@ -165,6 +209,122 @@ class SecondaryPluginManager:
     def list(self, kind: Optional[SecondaryPluginType] = None) -> Dict[str, List[str]]:
         kinds = [kind] if kind else list(SecondaryPluginType)
         return {k.value: sorted(self._reg[k]) for k in kinds}
+
+    # reference-style lifecycle: one active plugin per kind
+    def register_plugin(self, kind: SecondaryPluginType, plugin: SecondaryPlugin) -> None:
+        self.register(kind, plugin.name, plugin)
+
+    def get_plugin(self, kind: SecondaryPluginType, name: Optional[str] = None) -> Optional[SecondaryPlugin]:
+        name = name or self.active.get(kind)
+        if name is None and len(self._reg[kind]) == 1:
+            name = next(iter(self._reg[kind]))
+        return self._reg[kind].get(name) if name else None
+
+    def activate_plugin(self, kind: SecondaryPluginType, name: Optional[str] = None, **kw) -> bool:
+        p = self.get_plugin(kind, name)
+        if p is None or not p.initialize(**kw):
+            return False
+        self.active[kind] = p.name
+        return True
+
+    def deactivate_plugin(self, kind: SecondaryPluginType) -> bool:
+        name = self.active.pop(kind, None)
+        if name is None:
+            return False
+        return self._reg[kind][name].cleanup()
+
+    def execute_plugin(self, kind: SecondaryPluginType, *a, **kw) -> Any:
+        name = self.active.get(kind)
+        if name is None:
+            return None
+        return self._reg[kind][name].execute(*a, **kw)
+
+
+def register_defaults(m: SecondaryPluginManager) -> SecondaryPluginManager:
+    """Registers the engine's components as secondary plugins (imports are lazy)."""
+    T = SecondaryPluginType
+
+    def mem(device="cuda", **kw):
+        from ..runtime.memory import UnifiedMemoryManager
+
+        return UnifiedMemoryManager(device, **kw)
+
+    def fused_comm(parallelism="ep", **kw):
+        from ..parallel import ep, tp
+
+        return ep.FusedEPMoE if parallelism == "ep" else tp.FusedTP
+
+    def nccl_comm(parallelism="ep", **kw):
+        from ..parallel import ep, tp
+
+        return ep.NcclEPMoE if parallelism == "ep" else tp.NcclTP
+
+    def admission(**kw):
+        from .managers import AdaptiveAdmission
+
+        return AdaptiveAdmission(**kw)
+
+    def pipeline(**kw):
+        from ..parallel.pipeline import PipelineExecutor
+
+        return PipelineExecutor
+
+    def planner(**kw):
+        from ..parallel.planner import plan
+
+        return plan
+
+    def kernels(**kw):
+        from ..models.backend import make_backend
+
+        return make_backend("native")
+
+    def int8(**kw):
+        from ..ops.quant import quantize_model
+
+        return quantize_model
+
+    def budgets(device="cuda", **kw):
+        from ..runtime.memory import UnifiedMemoryManager
+
+        return UnifiedMemoryManager(device, **kw)
+
+    def streaming(**kw):
+        from ..runtime.offload import enable_streaming
+
+        return enable_streaming
+
+    m.register_plugin(T.MEMORY_MANAGER, SecondaryPlugin(
+        "unified", mem, "one owner of device memory per rank: KV pool sizing, region budgets, KV swap",
+        call=lambda inst, *a, **k: inst.report()))
+    m.register_plugin(T.DISTRIBUTED_EXECUTION, SecondaryPlugin(
+        "fused-nvlink", fused_comm, "in-kernel NVLink dispatch/combine (EP) and fused TP boundaries",
+        call=lambda inst, *a, **k: inst(*a, **k) if a or k else inst))
+    m.register_plugin(T.DISTRIBUTED_EXECUTION, SecondaryPlugin(
+        "nccl", nccl_comm, "NCCL all-to-all / all-reduce with library GEMMs (baseline)",
+        call=lambda inst, *a, **k: inst(*a, **k) if a or k else inst))
+    m.register_plugin(T.ADAPTIVE_BATCHING, SecondaryPlugin(
+        "adaptive-admission", admission, "admission control by measured step latency"))
+    m.register_plugin(T.PIPELINE, SecondaryPlugin("stage-executor", pipeline, "micro-batched pipeline stages"))
+    m.register_plugin(T.SHARDING, SecondaryPlugin("planner", planner, "TP/EP/PP/DP degrees and per-GPU bytes"))
+    m.register_plugin(T.KERNEL_FUSION, SecondaryPlugin("sm100-native", kernels, "hand-written sm_100a kernels"))
+    m.register_plugin(T.COMPRESSION, SecondaryPlugin("int8-weight-only", int8, "per-channel int8 projections"))
+    m.register_plugin(T.SECURITY, SecondaryPlugin(
+        "memory-budgets", budgets, "per-region byte budgets (OutOfBudget on overrun)",
+        call=lambda inst, region, nbytes: inst.charge(region, nbytes)))
+    m.register_plugin(T.MODEL_SURGERY, SecondaryPlugin(
+        "layer-streaming", streaming, "stream trailing layers from pinned host memory (hybrid CPU/GPU)"))
+    return m
+
+
+_SECONDARY: Optional[SecondaryPluginManager] = None
+
+
+def get_secondary_plugin_manager() -> SecondaryPluginManager:
+    global _SECONDARY
+    if _SECONDARY is None:
+        _SECONDARY = SecondaryPluginManager(defaults=True)
+    return _SECONDARY
 
 
 class ModelFactory:

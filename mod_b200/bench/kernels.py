@@ -53,6 +53,19 @@ def case(name: str, T: int = 128):
             torch.matmul(x, ws[i[0] % len(ws)].t(), out=y)
             i[0] += 1
         return run, K * Nn * 2 + T * K * 2 + T * Nn * 2, 2 * T * K * Nn
+    if name.startswith("cl:"):  # cluster split-K GEMM (DSMEM reduction): cl:qkv, cl:o, cl:router[:cs]
+        parts = name.split(":")
+        K, Nn = {"qkv": (2048, 5120), "o": (4096, 2048), "router": (2048, 128)}[parts[1]]
+        cs = int(parts[2]) if len(parts) > 2 else 0
+        ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)
+        x = torch.randn(T, K, device=dev).to(bf)
+        y = torch.empty(T, Nn, device=dev, dtype=bf)
+        i = [0]
+
+        def run():
+            N.linear_cluster(x, ws[i[0] % len(ws)], out=y, cs=cs)
+            i[0] += 1
+        return run, K * Nn * 2 + T * K * 2 + T * Nn * 2, 2 * T * K * Nn
     if name in ("qkv", "o", "lm_head", "router"):
         K, Nn = {"qkv": (2048, 5120), "o": (4096, 2048), "lm_head": (2048, 151936), "router": (2048, 128)}[name]
         ws = _rot(lambda: (torch.randn(Nn, K, device=dev) * 0.02).to(bf), K * Nn * 2)

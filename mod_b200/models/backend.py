@@ -87,6 +87,10 @@ class NativeBackend:
         load_extension()
         self.N = N
         self._one_group = {}
+        import os
+
+        # MB_CLUSTER_GEMM=0 keeps decode GEMMs on the split-K + reduction kernels (A/B timing)
+        self.cluster_gemm = os.environ.get("MB_CLUSTER_GEMM", "1") != "0"
 
     def _sms(self, device) -> int:
         if not hasattr(self, "_nsm"):
@@ -97,8 +101,21 @@ class NativeBackend:
         # built by a kernel (no host copy), so it is legal inside graph capture
         return torch.arange(2, dtype=torch.int32, device=device) * T
 
+    def _cluster_ok(self, x2, w) -> bool:
+        """Decode-sized bf16 GEMMs run on the cluster split-K kernel (DSMEM reduction, one launch)."""
+        if not self.cluster_gemm or isinstance(w, Int8Weight) or w.dtype != torch.bfloat16:
+            return False
+        T, K = x2.shape
+        return (1 <= T <= 128 and w.shape[0] % 128 == 0 and w.shape[0] <= 16384 and K % 64 == 0
+                and x2.stride(1) == 1 and w.is_contiguous())
+
     def linear(self, x, w, bias=None, residual=None, out=None):
-        T = x.reshape(-1, x.shape[-1]).shape[0]
+        x2 = x.reshape(-1, x.shape[-1])
+        if bias is None and self._cluster_ok(x2, w) and (out is None or out.is_contiguous()):
+            y = self.N.linear_cluster(x2, w, out=None if out is None else out.view(x2.shape[0], w.shape[0]),
+                                      residual=None if residual is None else residual.reshape(x2.shape[0], -1))
+            return y if out is None else out
+        T = x2.shape[0]
         ws = None
         n_out = w.shape[0]
         max_splits = 16 if n_out <= 1024 else (8 if n_out <= 128 * self._sms(x.device) else 0)
@@ -153,6 +170,14 @@ class NativeBackend:
         return self.N.rope_qknorm(qkv, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot,
                                   eps)
 
+    def qkv_rope(self, x, w, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps) -> bool:
+        """QKV projection with QK-norm, RoPE and the KV write in one cluster GEMM (decode sizes,
+        head_dim 128).  Returns False when the shape is not covered (caller runs the two-step form)."""
+        if D != 128 or w.shape[0] != (Hq + 2 * Hkv) * D or not self._cluster_ok(x, w):
+            return False
+        self.N.qkv_rope_cluster(x, w, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, rot, eps)
+        return True
+
     def attn_decode(self, q, k_cache, v_cache, block_tables, ctx_lens, splits=1):
         B, Hq, D = q.shape
         tc = self.N.attn_decode_tc_supported(D, Hq // k_cache.shape[1])
@@ -163,12 +188,15 @@ class NativeBackend:
         dynamic = os.environ.get("MB_ATTN_DYNAMIC", "1") != "0"
         chunk_env = os.environ.get("MB_ATTN_CHUNK")
         if tc:
-            # persistent tcgen05 kernel (3 CTAs per SM) with a dynamic work queue: sequences are cut
-            # into chunks of 2 KV tiles (16 blocks), or of 1 tile when that leaves fewer than two
-            # chunks per resident CTA, so the queue balances the CTAs; no split for short contexts
+            # persistent tcgen05 kernel (3 CTAs per SM) with a dynamic work queue (longest items first);
+            # sequences are cut into chunks of 16 blocks only when (sequence, KV head) items do not
+            # fill the resident CTAs.
+            # measured (Qwen3-30B-A3B shapes, ctx 600): 128 sequences x 4 KV heads run fastest unsplit
+            # (50.7 us vs 68-89 us with any split: the split-KV partials and combine cost more than the
+            # imbalance); 16 sequences run fastest in chunks of 16 blocks (17.3 vs 22.4 us unsplit)
             mb = block_tables.shape[1]
             items = B * k_cache.shape[1]
-            chunk = 16 if items * -(-mb // 16) >= 2 * 3 * self._sms(q.device) else 8
+            chunk = mb if items >= 3 * self._sms(q.device) else 16
             if chunk_env is not None:  # blocks per chunk; 0 = whole sequences
                 chunk = int(chunk_env) or mb
             splits = max(1, -(-mb // chunk))

@@ -49,11 +49,15 @@ class DecoderLM:
         cfg, be, aw = self.cfg, self.be, L.attn
         T = x.shape[0]
         Hq, Hkv, D = self.Hq, self.Hkv, cfg.head_dim
-        qkv = be.linear(x, aw.qkv, bias=aw.qkv_bias)
         kc, vc = kv.layer(i)
         q = torch.empty(T, Hq, D, dtype=x.dtype, device=x.device)
-        be.rope_qknorm(qkv, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc, vc, Hq, Hkv,
-                       D, cfg.rotary_dim, cfg.rms_norm_eps)
+        fused = (aw.qkv_bias is None and not cfg.attn_output_gate and hasattr(be, "qkv_rope")
+                 and be.qkv_rope(x, aw.qkv, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc,
+                                 vc, Hq, Hkv, D, cfg.rotary_dim, cfg.rms_norm_eps))
+        if not fused:
+            qkv = be.linear(x, aw.qkv, bias=aw.qkv_bias)
+            be.rope_qknorm(qkv, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc, vc, Hq,
+                           Hkv, D, cfg.rotary_dim, cfg.rms_norm_eps)
         if hasattr(be, "attn_paged"):
             o = be.attn_paged(q, kc, vc, fb)
         elif fb.is_decode:

@@ -35,6 +35,26 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     return out
 
 
+def linear_cluster(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                   residual: Optional[torch.Tensor] = None, cs: int = 0) -> torch.Tensor:
+    """``out = x @ w.T (+ residual)`` for decode-sized x (1..128 rows): split-K over a
+    thread-block cluster of ``cs`` CTAs (0: automatic) reduced through distributed
+    shared memory, one launch and no fp32 workspace."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    _C().linear_cluster(x, w, out, residual, cs)
+    return out
+
+
+def qkv_rope_cluster(x, w, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, rot_dim, eps,
+                     cs: int = 0):
+    """Packed QKV projection (head_dim 128) with QK-RMSNorm, RoPE and the paged KV
+    write in the cluster GEMM's epilogue; same result as ``linear`` + ``rope_qknorm``."""
+    _C().qkv_rope_cluster(x, w, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, rot_dim,
+                          eps, cs)
+    return q_out
+
+
 def swiglu_linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
                   workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """silu(x @ gate^T) * (x @ up^T), w = [gate; up]; decode shapes (T <= 256) with split-K."""

@@ -1,0 +1,60 @@
+"""Cluster split-K decode GEMM (DSMEM reduction) and its fused QKV + RoPE +
+QK-norm + KV-write epilogue, against plain fp32 torch references."""
+import pytest
+import torch
+
+from mod_b200.ops import reference as R
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("T,K,N", [(1, 2048, 128), (16, 2048, 5120), (37, 4096, 2048), (128, 2048, 5120),
+                                   (64, 768, 2048)])
+@pytest.mark.parametrize("cs", [0, 1, 2, 8])
+def test_linear_cluster_matches_fp32(cuda, T, K, N, cs):
+    from mod_b200.ops import native
+
+    if cs and (K // 64) // cs < 1:
+        pytest.skip("fewer K blocks than CTAs")
+    torch.manual_seed(T + K + N + cs)
+    x = torch.randn(T, K, device=cuda).bfloat16()
+    w = (torch.randn(N, K, device=cuda) * 0.02).bfloat16()
+    res = torch.randn(T, N, device=cuda).bfloat16()
+    for r in (None, res):
+        y = native.linear_cluster(x, w, residual=r, cs=cs)
+        ref = x.float() @ w.float().t() + (0 if r is None else r.float())
+        torch.cuda.synchronize()
+        torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * max(1.0, ref.abs().max().item()) / 8)
+
+
+@pytest.mark.parametrize("T,Hq,Hkv,rot", [(16, 32, 4, 128), (128, 32, 4, 128), (5, 8, 2, 64)])
+def test_qkv_rope_cluster_matches_unfused(cuda, T, Hq, Hkv, rot):
+    from mod_b200.ops import native
+
+    torch.manual_seed(T + Hq)
+    K, D, bs, nblk = 2048, 128, 16, 64
+    x = torch.randn(T, K, device=cuda).bfloat16()
+    w = (torch.randn((Hq + 2 * Hkv) * D, K, device=cuda) * 0.02).bfloat16()
+    qw = (1 + 0.1 * torch.randn(D, device=cuda)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(D, device=cuda)).bfloat16()
+    pos = torch.randint(0, 4000, (T,), device=cuda, dtype=torch.int32)
+    invf = R.inv_freq(rot, 1e6, device=cuda)
+    slots = torch.randperm(nblk * bs, device=cuda)[:T].int()
+    slots[0] = -1  # a padded row: no KV write
+    kc0 = torch.randn(nblk, Hkv, bs, D, device=cuda).bfloat16()
+    vc0 = torch.randn(nblk, Hkv, D, bs, device=cuda).bfloat16()
+    # reference: fp32 GEMM rounded to bf16 (the projection output), then the torch RoPE/QK-norm path
+    qkv = (x.float() @ w.float().t()).bfloat16()
+    q_ref = torch.empty(T, Hq, D, device=cuda, dtype=torch.bfloat16)
+    kc_ref, vc_ref = kc0.clone(), vc0.clone()
+    R.rope_qknorm(qkv, qw, kw, pos, invf, slots, q_ref, kc_ref, vc_ref, Hq, Hkv, D, rot, 1e-6)
+    q = torch.empty_like(q_ref)
+    kc, vc = kc0.clone(), vc0.clone()
+    native.qkv_rope_cluster(x, w, qw, kw, pos, invf, slots, q, kc, vc, Hq, Hkv, rot, 1e-6)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q.float(), q_ref.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(kc.float(), kc_ref.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(vc.float(), vc_ref.float(), rtol=3e-2, atol=3e-2)
+    from mod_b200.ops import check_status
+
+    check_status()

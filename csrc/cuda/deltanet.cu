@@ -23,6 +23,7 @@
 //
 // Replaces the reference's decayed linear-attention recurrence
 // (pio/plugins/cuda/c_src/tensor_ops_cuda.cu:420-452).
+#include <cstdlib>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -361,6 +362,22 @@ void deltanet_decode(const at::Tensor& mixed, const at::Tensor& z, const at::Ten
 }
 
 // Prefill of nseq sequences packed in mixed [T, C] (cu [nseq+1] int32 offsets, seq_of [T]).
+void launch_deltanet_chunk(const float* xc, const __nv_bfloat16* mixed, float* conv_state, const __nv_bfloat16* z,
+                           const __nv_bfloat16* ba, float* ssm, const int64_t* slots, const int* cu, const float* A_log,
+                           const float* dt_bias, const __nv_bfloat16* norm_w, __nv_bfloat16* out, int nseq, int Hk,
+                           int Hv, float eps, cudaStream_t st);
+
+// Prefill recurrence: the chunked tensor-core form (deltanet_chunk.cu) for dk = dv = 128 and conv
+// kernel 4, the token-serial scan otherwise (or with MB_DELTANET_CHUNK=0, kept for A/B timing).
+static bool use_chunked() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MB_DELTANET_CHUNK");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 void deltanet_prefill(const at::Tensor& mixed, const at::Tensor& z, const at::Tensor& ba, const at::Tensor& conv_w,
                       at::Tensor& conv_state, at::Tensor& ssm, const at::Tensor& slots, const at::Tensor& cu,
                       const at::Tensor& seq_of, const at::Tensor& A_log, const at::Tensor& dt_bias,
@@ -389,6 +406,14 @@ void deltanet_prefill(const at::Tensor& mixed, const at::Tensor& z, const at::Te
              (const int64_t*)slots.data_ptr<int64_t>(), (const int*)seq_of.data_ptr<int>(),                       \
              (const int*)cu.data_ptr<int>(), xc.data_ptr<float>(), C, (int)Hk);                                    \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                               \
+    if (DK_ == 128 && DV_ == 128 && KC_ == 4 && use_chunked()) {                                                  \
+      launch_deltanet_chunk((const float*)xc.data_ptr<float>(), bp(mixed), conv_state.data_ptr<float>(), bp(z),  \
+                            bp(ba), ssm.data_ptr<float>(), (const int64_t*)slots.data_ptr<int64_t>(),            \
+                            (const int*)cu.data_ptr<int>(), (const float*)A_log.data_ptr<float>(),               \
+                            (const float*)dt_bias.data_ptr<float>(), bp(norm_w),                                 \
+                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nseq, (int)Hk, (int)Hv, (float)eps, st); \
+      return;                                                                                                     \
+    }                                                                                                             \
     launch_k(deltanet_scan_kernel<DK_, DV_, KC_, 2>, dim3(nseq, (unsigned)Hv), 2 * DV_, 0, st,                          \
              (const float*)xc.data_ptr<float>(), bp(mixed), bp(z), bp(ba), conv_state.data_ptr<float>(),           \
              ssm.data_ptr<float>(), (const int64_t*)slots.data_ptr<int64_t>(), (const int*)cu.data_ptr<int>(),    \

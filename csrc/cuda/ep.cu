@@ -548,7 +548,8 @@ __global__ void __launch_bounds__(kRdThreads)
     ep_route_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wr,
                              int T, int K, int renorm, float* __restrict__ logits, int* __restrict__ ids,
                              float* __restrict__ wts, int* __restrict__ counts, int* __restrict__ cursor,
-                             int* __restrict__ map, int* __restrict__ offs, int* __restrict__ bar) {
+                             int* __restrict__ map, int* __restrict__ offs, int* __restrict__ bar,
+                             int* __restrict__ pos_map) {
   pdl_wait();
   pdl_trigger();
   const uint32_t epoch = *a.epoch + 1;
@@ -726,6 +727,7 @@ __global__ void __launch_bounds__(kRdThreads)
     }
     if (lane == 0) {
       map[pair] = dst * a.C + slot;
+      if (pos_map) pos_map[pair] = pos;  // single rank: the combine reads the expert rows in place
       at_off<int>(a.peers[dst], a.L.meta)[pos] = a.rank * a.C + slot;
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(pair / K) * H);
@@ -805,7 +807,7 @@ template <int H>
 __global__ void ep_combine_norm_kernel(EpArgs a, const int* __restrict__ map, const float* __restrict__ wts, int T,
                                        int K, __nv_bfloat16* __restrict__ residual,
                                        const __nv_bfloat16* __restrict__ nw, __nv_bfloat16* __restrict__ out,
-                                       float eps) {
+                                       float eps, const __nv_bfloat16* __restrict__ rows) {
   pdl_wait();
   pdl_trigger();
   constexpr int kChunks = H / 256;
@@ -814,11 +816,12 @@ __global__ void ep_combine_norm_kernel(EpArgs a, const int* __restrict__ map, co
   __shared__ int ok_all;
   if (threadIdx.x == 0) ok_all = 1;
   __syncthreads();
-  for (int o = threadIdx.x; o < a.N; o += blockDim.x)
+  // rows != nullptr (single rank): the expert outputs are read where the down GEMM wrote them
+  for (int o = threadIdx.x; o < a.N && !rows; o += blockDim.x)
     if (!wait_flag(at_off<uint32_t>(self, a.L.flag_c) + o, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
   __syncthreads();
   __threadfence();
-  const __nv_bfloat16* comb = at_off<__nv_bfloat16>(self, a.L.comb);
+  const __nv_bfloat16* comb = rows ? rows : at_off<__nv_bfloat16>(self, a.L.comb);
   const int lane = threadIdx.x & 31;
   for (int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T; t += gridDim.x * (blockDim.x / 32)) {
     float v[kChunks][8];
@@ -959,7 +962,8 @@ void ep_dispatch2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int6
 // counters; zero before the first call, left zero by every call), logits f32 [>= T*E].
 void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                        const at::Tensor& x, const at::Tensor& wr, int64_t K, bool renorm, at::Tensor& ids,
-                       at::Tensor& wts, at::Tensor& map, at::Tensor& offs, at::Tensor& scratch, at::Tensor& logits) {
+                       at::Tensor& wts, at::Tensor& map, at::Tensor& offs, at::Tensor& scratch, at::Tensor& logits,
+                       const c10::optional<at::Tensor>& pos_map) {
   const int64_t N = peers.numel(), T = x.size(0), H = x.size(1);
   const int64_t E = N * El;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && wr.scalar_type() == at::kBFloat16 &&
@@ -980,11 +984,17 @@ void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank,
   const int64_t pair_ctas = (T * K + kRdThreads / 32 - 1) / (kRdThreads / 32);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, std::max(tiles, pair_ctas)));
   int* sc = scratch.data_ptr<int>();
+  int* pm = nullptr;
+  if (pos_map && pos_map->defined()) {
+    TORCH_CHECK(pos_map->scalar_type() == at::kInt && pos_map->numel() >= T * K);
+    pm = pos_map->data_ptr<int>();
+  }
   const int epl = (int)((E + 31) / 32);
 #define MB_RD(P)                                                                                                   \
   launch_k(ep_route_dispatch_kernel<P>, grid, kRdThreads, 0, st, a, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), \
            reinterpret_cast<const __nv_bfloat16*>(wr.data_ptr()), (int)T, (int)K, (int)renorm, logits.data_ptr<float>(), \
-           ids.data_ptr<int>(), wts.data_ptr<float>(), sc, sc + E, map.data_ptr<int>(), offs.data_ptr<int>(), sc + 2 * E)
+           ids.data_ptr<int>(), wts.data_ptr<float>(), sc, sc + E, map.data_ptr<int>(), offs.data_ptr<int>(), sc + 2 * E, \
+           pm)
   if (epl <= 4) MB_RD(4);
   else if (epl <= 8) MB_RD(8);
   else if (epl <= 16) MB_RD(16);
@@ -1044,7 +1054,7 @@ void ep_combine_send(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
 // residual [T, H] += sum_k wts * comb rows; out = rmsnorm(residual) * w.
 void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                      const at::Tensor& map, const at::Tensor& wts, at::Tensor& residual, const at::Tensor& w,
-                     at::Tensor& out, double eps) {
+                     at::Tensor& out, double eps, const c10::optional<at::Tensor>& rows) {
   const int64_t N = peers.numel(), T = out.size(0), H = out.size(1), K = wts.size(1);
   TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous() && residual.size(0) == T &&
               residual.size(1) == H && out.is_contiguous() && w.numel() == H && w.is_contiguous());
@@ -1056,10 +1066,16 @@ void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
   auto r = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
   auto pw = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto po = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  const __nv_bfloat16* pr = nullptr;
+  if (rows && rows->defined()) {
+    TORCH_CHECK(N == 1 && rows->scalar_type() == at::kBFloat16 && rows->is_contiguous() && rows->size(1) == H,
+                "ep_combine_norm: local rows only on a single rank");
+    pr = reinterpret_cast<const __nv_bfloat16*>(rows->data_ptr());
+  }
 #define MB_CN(HH)                                                                                               \
   case HH:                                                                                                      \
     launch_k(ep_combine_norm_kernel<HH>, grid, wpb * 32, 0, st, a, (const int*)map.data_ptr<int>(),            \
-             (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, pw, po, (float)eps);                      \
+             (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, pw, po, (float)eps, pr);                  \
     break;
   switch (H) {
     MB_CN(256) MB_CN(512) MB_CN(1024) MB_CN(2048) MB_CN(3072) MB_CN(4096)

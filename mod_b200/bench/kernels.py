@@ -192,7 +192,7 @@ def case(name: str, T: int = 128):
             nbytes = B * Hv * d * d * 4 * 2 + B * C * (2 + 4 * 2 + 3 * 8) + B * Hv * d * 4
             return ((lambda: N.deltanet_decode(mix, z, ba, cw, conv, ssm, slots, A, dtb, nw, Hk, Hv, d, d, 1e-6,
                                                out=out)), nbytes, B * Hv * d * d * 6)
-        nseq, L = 4, 2048
+        nseq, L = 4, int(os.environ.get("MB_BENCH_DN_LEN", "2048"))  # tokens per sequence
         Tt = nseq * L
         mix = torch.randn(Tt, C, device=dev).to(bf)
         z = torch.randn(Tt, Hv * d, device=dev).to(bf)

@@ -12,6 +12,7 @@ completion.  The reference's per-plugin ``generate_text`` /
 from __future__ import annotations
 
 import logging
+import os
 import time
 from typing import Dict, List, Optional, Sequence as Seq, Union
 
@@ -98,6 +99,15 @@ class LLMEngine:
             moe_impl = (FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
                                    prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
                         if backend == "native" else NcclEPMoE(cfg, self.backend, max_tokens=max_batch))
+        elif (backend == "native" and cfg.is_moe and world == 1 and model is None and self.device.type == "cuda"
+              and quantization in (None, "none") and not cfg.shared_expert_intermediate_size
+              and os.environ.get("MB_MOE_FUSED", "1") != "0"):
+            # one GPU: the same fused route + placement kernel and the combine folded into the next
+            # add + RMSNorm (expert rows read in place), four launches per MoE layer instead of nine
+            from ..parallel.ep import FusedEPMoE
+
+            moe_impl = FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
+                                  prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
         if weights is None and model is None:
             weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
         if quantization not in (None, "none", "int8"):

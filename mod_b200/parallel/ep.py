@@ -130,11 +130,16 @@ class FusedEPMoE:
         ids = torch.empty(T, self.K, dtype=torch.int32, device=dev)
         wts = torch.empty(T, self.K, dtype=torch.float32, device=dev)
         emap = torch.empty(T * self.K, dtype=torch.int32, device=dev)
+        # single rank with a deferred combine: the weighted sum reads the expert rows where the down GEMM
+        # wrote them (row of each pair in the expert-ordered buffer), so no rows are sent back
+        local = defer and self.world == 1 and self.fused_route
+        pmap = torch.empty(T * self.K, dtype=torch.int32, device=dev) if local else None
         if self.fused_route:
             # one kernel: router GEMV, top-k, counts exchange, and every row stored at its
             # expert-ordered position in the owner's receive region
             self.C.ep_route_dispatch(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, x, mo.router, self.K,
-                                     cfg.norm_topk_prob, ids, wts, emap, ctx.offs, ctx.route_scratch, ctx.logits)
+                                     cfg.norm_topk_prob, ids, wts, emap, ctx.offs, ctx.route_scratch, ctx.logits,
+                                     pmap)
         else:
             logits = self.be.linear(x, mo.router)
             counts = torch.empty(E, dtype=torch.int32, device=dev)
@@ -153,6 +158,8 @@ class FusedEPMoE:
         # (returning rows from the down GEMM's epilogue measured slower: its per-element 2-byte
         # peer stores make 64-byte NVLink writes, where the copy kernel writes 512 bytes per warp)
         y = N.grouped_linear(h, mo.w2, ctx.offs, self.El, False, mr)
+        if local:
+            return PendingCombine(self, ctx, pmap, wts, T, rows=y)
         if defer:
             # rows go back now; the weighted sum happens inside the next add + RMSNorm
             self.C.ep_combine_send(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, ctx.offs, y, self.H)
@@ -195,14 +202,15 @@ class PendingCombine:
     not yet summed.  ``add_norm(residual, w, eps)`` does, in one kernel,
     residual += sum_k w_k * row_k and returns rmsnorm(residual) * w."""
 
-    def __init__(self, moe, ctx, emap, wts, T):
+    def __init__(self, moe, ctx, emap, wts, T, rows=None):
         self.moe, self.ctx, self.emap, self.wts, self.T = moe, ctx, emap, wts, T
+        self.rows = rows  # single rank: expert output rows read in place (emap indexes them)
 
     def add_norm(self, residual: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
         m, ctx = self.moe, self.ctx
         out = torch.empty_like(residual)
         m.C.ep_combine_norm(ctx.buf.peers, ctx.state, m.rank, ctx.cap, m.El, self.emap, self.wts, residual, w, out,
-                            eps)
+                            eps, self.rows)
         return out
 
 

@@ -331,6 +331,47 @@ def test_deltanet_prefill_then_decode(cuda, Hk, Hv, dk):
         torch.testing.assert_close(ssm, ssm_r, rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 4096])
+@pytest.mark.parametrize("chunked", [True, False])
+def test_deltanet_prefill_lengths_with_cached_state(cuda, L, chunked):
+    """Prefill of one sequence starting from a non-zero cached state, at lengths around the
+    64-token chunk, against the fp32 oracle; the chunked tensor-core scan and the token-serial
+    scan (MB_DELTANET_CHUNK=0, read once per process, so run in a child) both."""
+    import subprocess
+    import sys
+
+    code = f"""
+import torch, sys
+sys.path.insert(0, {repr(str(__import__('os').path.dirname(__import__('os').path.dirname(__file__))))})
+from tests.test_kernels_gpu import _dn_inputs
+from mod_b200.ops import native, check_status
+from mod_b200.models.deltanet import ref_prefill
+torch.manual_seed(9)
+cuda = torch.device('cuda:0')
+Hk, Hv, dk, L = 2, 4, 128, {L}
+C = 2 * Hk * dk + Hv * dk
+mix, z, ba, conv_w, A_log, dt_bias, norm_w = _dn_inputs(L, Hk, Hv, dk, dk, cuda)
+conv = torch.randn(3, C, 3, device=cuda) * 0.3
+ssm = torch.randn(3, Hv, dk, dk, device=cuda) * 0.05
+conv_r, ssm_r = conv.clone(), ssm.clone()
+slots = torch.tensor([1], device=cuda)
+cu = torch.tensor([0, L], dtype=torch.int32, device=cuda)
+seq_of = torch.zeros(L, dtype=torch.int32, device=cuda)
+out = native.deltanet_prefill(mix, z, ba, conv_w, conv, ssm, slots, cu, seq_of, A_log, dt_bias, norm_w,
+                              Hk, Hv, dk, dk, 1e-6)
+torch.cuda.synchronize(); check_status()
+ref = ref_prefill(mix, z, ba, conv_w, A_log, dt_bias, norm_w, conv_r, ssm_r, 1, Hk, Hv, dk, dk, 1e-6)
+err = ((out.float() - ref).abs().max() / ref.abs().max()).item()
+serr = ((ssm - ssm_r).abs().max() / ssm_r.abs().max()).item()
+assert torch.equal(conv, conv_r) or (conv - conv_r).abs().max().item() < 1e-5
+assert err < 3e-2 and serr < 3e-2, (err, serr)
+print('ok', err, serr)
+"""
+    env = dict(__import__("os").environ, MB_DELTANET_CHUNK="1" if chunked else "0")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]
+
+
 # ------------------------------------------------------------ int8 weight GEMM
 @pytest.mark.parametrize("T,K,N", [(1, 256, 128), (16, 2048, 2048), (100, 1024, 384), (256, 4096, 1024),
                                    (1000, 2048, 512), (4096, 1024, 256)])

@@ -1,6 +1,6 @@
 // Causal flash-attention prefill over the paged KV cache on tcgen05 tensor cores.
 //
-// q   [T, Hq*D] bf16 (packed rows of every sequence's new tokens; D = 128)
+// q   [T, Hq*D] bf16 (packed rows of every sequence's new tokens; D = 64, 128 or 256)
 // k/v cache as in decode: K [blocks, Hkv, 16, D], V [blocks, Hkv, D, 16]
 // out [T, Hq*D] bf16
 // Sequence b owns q rows [cu_q[b], cu_q[b+1]) whose absolute positions end
@@ -38,13 +38,20 @@ CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows,
 
 namespace {
 
-constexpr int D = 128;
-constexpr int kQBytes = 2 * 16384;   // two d-halves x [128 rows x 128 B]
-constexpr int kKBytes = 2 * 16384;
-constexpr int kVBytes = 8 * 4096;    // eight blocks x [128 d x 32 B]
-constexpr int kPBytes = 2 * 16384;   // two key-halves x [128 rows x 128 B]
-constexpr int kStages = 2;
-constexpr int kSmem = 1024 + kQBytes + kStages * (kKBytes + kVBytes) + kPBytes + 512;
+// Head dims 64 / 128 / 256: Q and K are D/64 swizzle-width chunks of [128 rows x 128 B]; a V
+// block is [D x 32 B].  D = 256 fits one K/V stage in shared memory, smaller D two.
+template <int D>
+struct PrefillCfg {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kQBytes = kChunks * 16384;
+  static constexpr int kKBytes = kChunks * 16384;
+  static constexpr int kVBlock = D * 32;
+  static constexpr int kVBytes = 8 * kVBlock;
+  static constexpr int kPBytes = 2 * 16384;    // two key-halves x [128 rows x 128 B]
+  static constexpr int kStages = D > 128 ? 1 : 2;
+  static constexpr int kSmem = 1024 + kQBytes + kStages * (kKBytes + kVBytes) + kPBytes + 512;
+  static constexpr int kTmemCols = D > 128 ? 512 : 256;   // S (128 columns) + O (D columns)
+};
 
 __device__ __forceinline__ uint64_t sdesc_k32(uint32_t addr) {
   uint64_t d = 0;
@@ -68,11 +75,15 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+template <int D>
 __global__ void __launch_bounds__(160, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const int* __restrict__ block_tables,
                            const int* __restrict__ cu_q, const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
-                           int Hq, int Hkv, int max_blocks, float scale_log2, int* status) {
+                           int Hq, int Hkv, int max_blocks, float scale_log2, int* status, int causal) {
+  using CF = PrefillCfg<D>;
+  constexpr int kQBytes = CF::kQBytes, kKBytes = CF::kKBytes, kVBytes = CF::kVBytes, kPBytes = CF::kPBytes;
+  constexpr int kStages = CF::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = sm;
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(160, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, CF::kTmemCols);
     tmem_relinquish();
   }
   if (tid == 128) {
@@ -136,7 +147,7 @@ __global__ void __launch_bounds__(160, 1)
   const int qrow0 = qt * 128;                        // first query row of this tile (within the sequence)
   if (qrow0 < ql) {
     const int pos0 = ctx - ql + qrow0;                 // absolute position of query row 0
-    const int last_pos = min(ctx - 1, pos0 + 127);
+    const int last_pos = causal ? min(ctx - 1, pos0 + 127) : ctx - 1;
     const int nkt = last_pos / 128 + 1;                // key tiles [0, nkt)
     const int nblk = (ctx + 15) / 16;
     const int* bt = block_tables + (size_t)b * max_blocks;
@@ -145,8 +156,8 @@ __global__ void __launch_bounds__(160, 1)
       // ------------------------------------------------ producer
       if (lane == 0) {
         mbar_arrive_expect_tx(barQ, kQBytes);
-        tma_load_2d(sQ, &tmQ, barQ, h * D, q0 + qrow0);
-        tma_load_2d(sQ + 16384, &tmQ, barQ, h * D + 64, q0 + qrow0);
+#pragma unroll
+        for (int c = 0; c < CF::kChunks; ++c) tma_load_2d(sQ + c * 16384, &tmQ, barQ, h * D + c * 64, q0 + qrow0);
       }
       for (int j = 0; j < nkt; ++j) {
         const int s = j % kStages;
@@ -156,25 +167,27 @@ __global__ void __launch_bounds__(160, 1)
         if (lane == 0) ok = mbar_wait(&emptyK[s], ph ^ 1, status);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        if (lane == 0) mbar_arrive_expect_tx(&fullK[s], nv * 4096);
+        if (lane == 0) mbar_arrive_expect_tx(&fullK[s], nv * D * 32);
         __syncwarp();
         int phys = 0;
         if (lane < nv) {
           phys = bt[j * 8 + lane];
           const int krow = (phys * Hkv + hk) * 16;
-          tma_load_2d(sK + s * kKBytes + lane * 2048, &tmK, &fullK[s], 0, krow);
-          tma_load_2d(sK + s * kKBytes + 16384 + lane * 2048, &tmK, &fullK[s], 64, krow);
+#pragma unroll
+          for (int c = 0; c < CF::kChunks; ++c)
+            tma_load_2d(sK + s * kKBytes + c * 16384 + lane * 2048, &tmK, &fullK[s], c * 64, krow);
         }
         if (lane == 0) ok = mbar_wait(&emptyV[s], ph ^ 1, status);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        if (lane == 0) mbar_arrive_expect_tx(&fullV[s], nv * 4096);
+        if (lane == 0) mbar_arrive_expect_tx(&fullV[s], nv * CF::kVBlock);
         __syncwarp();
-        if (lane < nv) tma_load_2d(sV + s * kVBytes + lane * 4096, &tmV, &fullV[s], 0, (phys * Hkv + hk) * D);
+        if (lane < nv) tma_load_2d(sV + s * kVBytes + lane * CF::kVBlock, &tmV, &fullV[s], 0, (phys * Hkv + hk) * D);
       }
     } else {
       // ------------------------------------------------ softmax / MMA warps
-      constexpr uint32_t idesc = make_idesc_bf16(128, 128);
+      constexpr uint32_t idesc = make_idesc_bf16(128, 128);      // S = Q K^T: 128 queries x 128 keys
+      constexpr uint32_t idesc_o = make_idesc_bf16(128, D);      // O += P V: 128 queries x D
       const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
       const int my_pos = pos0 + tid;                  // absolute position of this thread's query row
       float m = -INFINITY, l = 0.f;
@@ -186,7 +199,7 @@ __global__ void __launch_bounds__(160, 1)
         tc_fence_after();
         if (tid == 0 && ok) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
             tc_mma_bf16(tS, make_sdesc_k128(smem_u32(sQ) + off), make_sdesc_k128(smem_u32(sK + s * kKBytes) + off),
                         idesc, kk > 0);
@@ -206,7 +219,7 @@ __global__ void __launch_bounds__(160, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
           const int kpos = j * 128 + c;
-          sc[c] = (kpos <= my_pos && kpos < ctx) ? sc[c] * scale_log2 : -INFINITY;
+          sc[c] = ((!causal || kpos <= my_pos) && kpos < ctx) ? sc[c] * scale_log2 : -INFINITY;
           mt = fmaxf(mt, sc[c]);
         }
         const float mn = fmaxf(m, mt);
@@ -231,7 +244,7 @@ __global__ void __launch_bounds__(160, 1)
         // ---- rescale this warp's O rows when any running max moved
         if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 128; c += 16) {
+          for (int c = 0; c < D; c += 16) {
             float o[16];
             tmem_ld16(tO + lane_off + c, o);
 #pragma unroll
@@ -252,8 +265,8 @@ __global__ void __launch_bounds__(160, 1)
 #pragma unroll
           for (int kb = 0; kb < 8; ++kb) {
             const uint32_t poff = (kb >> 2) * 16384 + (kb & 3) * 32;
-            tc_mma_bf16(tO, make_sdesc_k128(smem_u32(sP) + poff), sdesc_k32(smem_u32(sV + s * kVBytes) + kb * 4096),
-                        idesc, (j > 0 || kb > 0));
+            tc_mma_bf16(tO, make_sdesc_k128(smem_u32(sP) + poff),
+                        sdesc_k32(smem_u32(sV + s * kVBytes) + kb * CF::kVBlock), idesc_o, (j > 0 || kb > 0));
           }
           tc_commit(barO);
           tc_commit(&emptyV[s]);
@@ -266,7 +279,7 @@ __global__ void __launch_bounds__(160, 1)
       __nv_bfloat16* dst = out + ((size_t)(q0 + qrow0 + tid) * Hq + h) * D;
       const bool store = ok && qrow0 + tid < ql;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 16) {
+      for (int c = 0; c < D; c += 16) {
         float o[16];
         tmem_ld16(tO + lane_off + c, o);
         if (store) {
@@ -283,25 +296,22 @@ __global__ void __launch_bounds__(160, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, CF::kTmemCols);
   }
 }
 
 }  // namespace
 
-// q [T, Hq*D] (contiguous rows), cu_q [B+1], ctx_lens [B], block_tables [B, max_blocks]
-void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
-                     const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,
-                     at::Tensor& out, int64_t max_q_len, double scale) {
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && out.is_contiguous() && q.dim() == 2);
-  TORCH_CHECK(k_cache.size(3) == D && v_cache.size(2) == D && k_cache.size(2) == 16 && v_cache.size(3) == 16);
-  TORCH_CHECK(block_tables.scalar_type() == at::kInt && cu_q.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt);
+template <int D>
+static void launch_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                           const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,
+                           at::Tensor& out, int64_t max_q_len, double scale, bool causal) {
+  using CF = PrefillCfg<D>;
   const int T = (int)q.size(0), Hkv = (int)k_cache.size(1), NB = (int)k_cache.size(0);
   const int Hq = (int)(q.size(1) / D);
   TORCH_CHECK(Hq * D == q.size(1) && Hq % Hkv == 0 && out.sizes() == q.sizes());
   const int B = (int)ctx_lens.numel();
   if (T == 0 || B == 0) return;
-  c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto tq = make_tmap_2d(q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, T, (int64_t)Hq * D, (int64_t)Hq * D * 2, 64,
                          128, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -309,16 +319,34 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                          16, CU_TENSOR_MAP_SWIZZLE_128B);
   auto tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (int64_t)NB * Hkv * D, 16, 32, 16, D,
                          CU_TENSOR_MAP_SWIZZLE_32B);
+  auto kern = attn_prefill_tc_kernel<D>;
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem));
     attr = true;
   }
   const int qtiles = (int)((max_q_len + 127) / 128);
-  launch_k(attn_prefill_tc_kernel, dim3(qtiles, Hq, B), 160, kSmem, st, tq, tk, tv, block_tables.data_ptr<int>(),
+  launch_k(kern, dim3(qtiles, Hq, B), 160, CF::kSmem, st, tq, tk, tv, block_tables.data_ptr<int>(),
            cu_q.data_ptr<int>(), ctx_lens.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), Hq, Hkv,
-           (int)block_tables.size(1), (float)(scale * 1.4426950408889634), status_ptr(q.device().index()));
+           (int)block_tables.size(1), (float)(scale * 1.4426950408889634), status_ptr(q.device().index()),
+           (int)causal);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// q [T, Hq*D] (contiguous rows), cu_q [B+1], ctx_lens [B], block_tables [B, max_blocks]; D in {64, 128, 256}.
+// causal = false: every query row of sequence b sees all ctx_lens[b] keys (bidirectional, e.g. a ViT).
+void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                     const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,
+                     at::Tensor& out, int64_t max_q_len, double scale, bool causal) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && out.is_contiguous() && q.dim() == 2);
+  const int64_t D = k_cache.size(3);
+  TORCH_CHECK(v_cache.size(2) == D && k_cache.size(2) == 16 && v_cache.size(3) == 16);
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && cu_q.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt);
+  c10::cuda::CUDAGuard guard(q.device());
+  if (D == 128) launch_prefill<128>(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, out, max_q_len, scale, causal);
+  else if (D == 256) launch_prefill<256>(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, out, max_q_len, scale, causal);
+  else if (D == 64) launch_prefill<64>(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, out, max_q_len, scale, causal);
+  else TORCH_CHECK(false, "attn_prefill_tc: head_dim must be 64, 128 or 256");
 }
 
 }  // namespace mb

@@ -58,7 +58,7 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
 bool attn_decode_tc_supported(int64_t D, int64_t G);
 void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                      const at::Tensor& block_tables, const at::Tensor& cu_q, const at::Tensor& ctx_lens,
-                     at::Tensor& out, int64_t max_q_len, double scale);
+                     at::Tensor& out, int64_t max_q_len, double scale, bool causal);
 void moe_route(const at::Tensor& logits, int64_t K, bool renorm, at::Tensor& ids, at::Tensor& wts,
                at::Tensor& counts, at::Tensor& offs, at::Tensor& cursor);
 void moe_permute(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& offs, at::Tensor& cursor,
@@ -103,6 +103,8 @@ void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optio
                       const c10::optional<at::Tensor>& k_w, const at::Tensor& positions, const at::Tensor& inv_freq,
                       const c10::optional<at::Tensor>& slots, at::Tensor& q_out, at::Tensor& k_cache,
                       at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs);
+void vit_rope_kv(const at::Tensor& qkv, const at::Tensor& pos, int64_t N, int64_t heads, int64_t D, double theta,
+                 at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache);
 void decode_advance(const at::Tensor& sampled, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx, at::Tensor& slots,
                     const at::Tensor& bt, int64_t n, int64_t block_size);
 void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, int64_t vocab_start);
@@ -127,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_w8", &mb::linear_w8);
   m.def("sample_tokens", &mb::sample_tokens);
   m.def("patchify", &mb::patchify);
+  m.def("vit_rope_kv", &mb::vit_rope_kv);
   m.def("bias_act", &mb::bias_act);
   m.def("deltanet_prefill", &mb::deltanet_prefill);
   m.def("attn_decode_tc_supported", &mb::attn_decode_tc_supported);

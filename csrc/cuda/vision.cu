@@ -152,4 +152,63 @@ void bias_act(at::Tensor& y, const c10::optional<at::Tensor>& bias, bool gelu) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ViT attention operands: 2-D rotary embedding of q and k (rotate-half; angle index i < D/4
+// follows the patch row, D/4 <= i < D/2 the column; theta^(-i'/(D/4)) with i' = i mod D/4),
+// q -> q_out [B*N, heads*D]; k and v of image b go to block b*nblk + t/16 of a paged cache
+// (K [blocks, heads, 16, D], V [blocks, heads, D, 16]) so the bidirectional flash kernel can
+// read every image as one sequence.  One CTA per patch row.
+__global__ void vit_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const int* __restrict__ pos, int N,
+                                  int heads, int D, int nblk, float theta, __nv_bfloat16* __restrict__ q_out,
+                                  __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x, b = row / N, t = row % N;
+  const int half = D / 2, quarter = D / 4;
+  const float pr = (float)pos[t * 2], pc = (float)pos[t * 2 + 1];
+  const __nv_bfloat16* src = qkv + (size_t)row * 3 * heads * D;
+  const size_t blk = (size_t)b * nblk + t / 16, off = t % 16;
+  for (int i = threadIdx.x; i < heads * half; i += blockDim.x) {
+    const int h = i / half, d = i % half;
+    const int ii = d % quarter;
+    const float inv = powf(theta, -(float)ii / (float)quarter);
+    float sn, cs;
+    sincosf((d < quarter ? pr : pc) * inv, &sn, &cs);
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {  // q, k
+      const __nv_bfloat16* x = src + (size_t)which * heads * D + h * D;
+      const float x1 = __bfloat162float(x[d]), x2 = __bfloat162float(x[d + half]);
+      const __nv_bfloat16 o1 = __float2bfloat16(x1 * cs - x2 * sn), o2 = __float2bfloat16(x2 * cs + x1 * sn);
+      if (which == 0) {
+        q_out[(size_t)row * heads * D + h * D + d] = o1;
+        q_out[(size_t)row * heads * D + h * D + d + half] = o2;
+      } else {
+        __nv_bfloat16* kd = k_cache + ((blk * heads + h) * 16 + off) * D;
+        kd[d] = o1;
+        kd[d + half] = o2;
+      }
+    }
+  }
+  for (int i = threadIdx.x; i < heads * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    v_cache[((blk * heads + h) * D + d) * 16 + off] = src[(size_t)2 * heads * D + i];
+  }
+}
+
+void vit_rope_kv(const at::Tensor& qkv, const at::Tensor& pos, int64_t N, int64_t heads, int64_t D, double theta,
+                 at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache) {
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.is_contiguous() && qkv.size(1) == 3 * heads * D);
+  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous() && pos.numel() == 2 * N && D % 4 == 0);
+  const int64_t rows = qkv.size(0), nblk = (N + 15) / 16;
+  TORCH_CHECK(rows % N == 0 && q_out.is_contiguous() && q_out.numel() == rows * heads * D);
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.size(0) >= rows / N * nblk &&
+              k_cache.size(1) == heads && k_cache.size(2) == 16 && k_cache.size(3) == D && v_cache.size(2) == D);
+  if (rows == 0) return;
+  c10::cuda::CUDAGuard guard(qkv.device());
+  launch_k(vit_rope_kv_kernel, (unsigned)rows, 256, 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), (const int*)pos.data_ptr<int>(), (int)N,
+           (int)heads, (int)D, (int)nblk, (float)theta, reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
+           reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace mb

@@ -215,8 +215,8 @@ class NativeBackend:
 
     def attn_prefill_paged(self, q, k_cache, v_cache, fb):
         """All sequences of a prefill step in one tcgen05 flash-attention launch
-        (head_dim 128); None when the shape is not covered."""
-        if q.shape[-1] != 128:
+        (head_dim 64, 128 or 256); None when the shape is not covered."""
+        if q.shape[-1] not in (64, 128, 256):
             return None
         ql = fb.query_lens
         cu = [0]

@@ -132,16 +132,35 @@ def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, b
     eps = vc.layer_norm_eps
     pos = grid_positions(size, vc.patch_size, vc.spatial_merge_size, patches.device)
     x = be.linear(patches.reshape(B * N, -1).to(vw.patch.dtype).contiguous(), vw.patch, bias=vw.patch_bias)
+    native = getattr(be, "name", "") == "native" and D in (64, 128, 256) and patches.is_cuda
+    if native:
+        # every image is one sequence of a paged cache (block table = its own blocks), so one
+        # bidirectional tcgen05 flash launch covers the whole batch
+        nblk = (N + 15) // 16
+        dev = patches.device
+        bt = torch.arange(B * nblk, dtype=torch.int32, device=dev).view(B, nblk)
+        cu = torch.arange(B + 1, dtype=torch.int32, device=dev) * N
+        ctx = torch.full((B,), N, dtype=torch.int32, device=dev)
+        pos_i = pos.int().contiguous()
+        alloc = torch.empty if N % 16 == 0 else torch.zeros  # no stale NaNs behind the last patch
+        kc = alloc(B * nblk, heads, 16, D, dtype=torch.bfloat16, device=dev)
+        vc = alloc(B * nblk, heads, D, 16, dtype=torch.bfloat16, device=dev)
+        q = torch.empty(B * N, heads * D, dtype=torch.bfloat16, device=dev)
     for blk in vw.blocks:
         h = be.rmsnorm(x, blk.norm1, eps)
-        qkv = be.linear(h, blk.qkv, bias=blk.qkv_bias).view(B, N, 3, heads, D)
-        outs = []
-        for b in range(B):
-            q = rope_2d(qkv[b, :, 0], pos)
-            k = rope_2d(qkv[b, :, 1], pos)
-            v = qkv[b, :, 2]
-            outs.append(R.attn_prefill(q, k, v, causal=False))
-        o = torch.stack(outs).reshape(B * N, H)
+        qkv = be.linear(h, blk.qkv, bias=blk.qkv_bias)
+        if native:
+            be.N.vit_rope_kv(qkv.contiguous(), pos_i, N, heads, D, 10000.0, q, kc, vc)
+            o = be.N.attn_prefill_tc(q.view(B * N, heads, D), kc, vc, bt, cu, ctx, N, causal=False)
+            o = o.reshape(B * N, H)
+        else:
+            qkv = qkv.view(B, N, 3, heads, D)
+            outs = []
+            for b in range(B):
+                qb = rope_2d(qkv[b, :, 0], pos)
+                kb = rope_2d(qkv[b, :, 1], pos)
+                outs.append(R.attn_prefill(qb, kb, qkv[b, :, 2], causal=False))
+            o = torch.stack(outs).reshape(B * N, H)
         x = be.linear(o, blk.proj, bias=blk.proj_bias, residual=x)
         h = be.rmsnorm(x, blk.norm2, eps)
         h = _linear_gelu(be, h, blk.fc1, blk.fc1_bias)

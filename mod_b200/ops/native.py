@@ -127,15 +127,16 @@ def attn_decode_tc(q, k_cache, v_cache, block_tables, ctx_lens, out=None, splits
 
 
 def attn_prefill_tc(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, max_q_len: int, out=None,
-                    scale: Optional[float] = None):
-    """Causal tcgen05 flash prefill over the paged cache.  q [T, Hq, D] (D = 128)."""
+                    scale: Optional[float] = None, causal: bool = True):
+    """tcgen05 flash prefill over the paged cache.  q [T, Hq, D] (D = 64, 128 or 256); causal=False
+    lets every query of a sequence see all its keys (bidirectional)."""
     T, Hq, D = q.shape
     if out is None:
         out = torch.empty_like(q)
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     _C().attn_prefill_tc(q.view(T, Hq * D), k_cache, v_cache, block_tables, cu_q, ctx_lens, out.view(T, Hq * D),
-                         max_q_len, scale)
+                         max_q_len, scale, causal)
     return out
 
 
@@ -258,3 +259,9 @@ def grouped_linear_wait(xs, w, offs, groups: int, swiglu: bool, max_rows_per_gro
         out = torch.empty(xs.shape[0], n_out, dtype=xs.dtype, device=xs.device)
     _C().grouped_linear_wait(xs, w, offs, out, groups, swiglu, max_rows_per_group, flags, state, nranks, epoch_add)
     return out
+
+
+def vit_rope_kv(qkv, pos, N: int, heads: int, D: int, theta: float, q_out, k_cache, v_cache):
+    """ViT 2-D RoPE of q and k, q -> q_out, k / v of each image into its own blocks of a paged cache."""
+    _C().vit_rope_kv(qkv, pos, N, heads, D, theta, q_out, k_cache, v_cache)
+    return q_out

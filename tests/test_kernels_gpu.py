@@ -194,15 +194,17 @@ def test_attn_decode_tc(cuda, B, Hq, Hkv, splits, lens):
             _close(o[b], ref[b])
 
 
+@pytest.mark.parametrize("D,causal", [(128, True), (256, True), (64, True), (64, False), (256, False)])
 @pytest.mark.parametrize("Hq,Hkv,lens", [(32, 4, [(512, 512), (300, 300), (1, 1)]), (16, 8, [(130, 130), (70, 200)]),
                                          (8, 8, [(129, 1000), (256, 256)])])
-def test_attn_prefill_tc(cuda, Hq, Hkv, lens):
-    """(query_len, context_len) per sequence; context > query means a cached prefix."""
+def test_attn_prefill_tc(cuda, Hq, Hkv, lens, D, causal):
+    """(query_len, context_len) per sequence; context > query means a cached prefix.  Head dims
+    64 (ViT), 128, 256 (Qwen3-Next gated attention); causal=False is bidirectional attention."""
     native, check = _N()
     from mod_b200.ops import reference as R
 
     torch.manual_seed(6)
-    D, nb = 128, 256
+    nb = 256
     kc, vc = _rand(nb, Hkv, 16, D), _rand(nb, Hkv, D, 16)
     B = len(lens)
     maxb = 64
@@ -214,13 +216,15 @@ def test_attn_prefill_tc(cuda, Hq, Hkv, lens):
     q = _rand(T, Hq, D)
     out = native.attn_prefill_tc(q, kc, vc, bt.cuda(), torch.tensor(cu, dtype=torch.int32, device=cuda),
                                  torch.tensor([c for _, c in lens], dtype=torch.int32, device=cuda),
-                                 max(ql for ql, _ in lens))
+                                 max(ql for ql, _ in lens), causal=causal)
     check()
     for b, (ql, ctx) in enumerate(lens):
         k = R.gather_kv(kc, bt[b].cuda(), ctx).float()
         v = R.gather_v(vc, bt[b].cuda(), ctx).float()
         qb = q[cu[b]:cu[b + 1]].float()
         mask = torch.arange(ctx, device=cuda)[None, :] <= (ctx - ql + torch.arange(ql, device=cuda))[:, None]
+        if not causal:
+            mask = torch.ones_like(mask)
         ref = torch.nn.functional.scaled_dot_product_attention(qb.transpose(0, 1)[None], k.transpose(0, 1)[None],
                                                                v.transpose(0, 1)[None], attn_mask=mask[None, None],
                                                                enable_gqa=True)[0].transpose(0, 1)

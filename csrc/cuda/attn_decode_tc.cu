@@ -40,15 +40,23 @@ CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows,
 
 namespace {
 
-constexpr int kTileTok = 128;
 constexpr int kBS = 16;
-constexpr int kKBytes = 2 * 16384;     // two d-halves x [128 rows x 128 B]
-constexpr int kVBytes = 8 * 4096;      // eight blocks x [128 d rows x 32 B]
-constexpr int kQBytes = 2 * 2048;      // two d-halves x [16 rows x 128 B]
-constexpr int kPBytes = 8 * 512;       // eight blocks x [16 rows x 32 B]
-// One Q buffer: the next item's Q is written only after the last S MMA that reads
-// the current one has completed.  75,776 B per CTA lets three CTAs share an SM.
-constexpr int kSmemBytes = 1024 + kKBytes + kVBytes + kQBytes + kPBytes + 1024;
+// Head dim D = 128 or 256: K / Q are D/64 swizzle-width chunks; a V block is [D rows x 32 B];
+// O^T (M = D) is D/128 MMAs of M = 128, each with its own 16 TMEM columns.
+template <int D>
+struct DecCfg {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kKBytes = kChunks * 16384;   // chunks x [128 rows x 128 B]
+  static constexpr int kVBlock = D * 32;
+  static constexpr int kVBytes = 8 * kVBlock;        // eight blocks x [D rows x 32 B]
+  static constexpr int kQBytes = kChunks * 2048;     // chunks x [16 rows x 128 B]
+  static constexpr int kPBytes = 8 * 512;            // eight blocks x [16 rows x 32 B]
+  static constexpr int kHalves = D / 128;
+  static constexpr int kTmemCols = D > 128 ? 64 : 32;
+  // One Q buffer: the next item's Q is written only after the last S MMA that reads the
+  // current one has completed.  D = 128: 75,776 B per CTA, three CTAs per SM.
+  static constexpr int kSmemBytes = 1024 + kKBytes + kVBytes + kQBytes + kPBytes + 1024;
+};
 
 // SW32 K-major descriptor: 8-row core groups of 32-byte rows (SBO = 256 B).
 __device__ __forceinline__ uint64_t make_sdesc_k32(uint32_t smem_addr) {
@@ -72,7 +80,7 @@ struct TileRef {
 // Walks this CTA's (item, tile) sequence: items blockIdx.x, +gridDim.x, ...
 // Items whose chunk is empty get their (zero / -inf) output written here and
 // are skipped.  Every thread runs the same walk.
-template <int G>
+template <int G, int D>
 struct TileCursor {
   int item, t, nt;
   int B, Hkv, splits, chunk_blocks, items;
@@ -110,13 +118,13 @@ struct TileCursor {
       nt = hi > lo ? (hi - lo + 127) / 128 : 0;
       t = -1;
       if (nt == 0) {  // empty chunk: write its output now and move on
-        for (int i = threadIdx.x; i < G * 128; i += blockDim.x) {
-          const int h = i / 128, d = i % 128;
+        for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+          const int h = i / D, d = i % D;
           const size_t bh2 = (size_t)b * Hkv * G + hk * G + h;
           if (splits == 1) {
-            out[bh2 * 128 + d] = __float2bfloat16(0.f);
+            out[bh2 * D + d] = __float2bfloat16(0.f);
           } else {
-            part_o[(bh2 * splits + sp) * 128 + d] = 0.f;
+            part_o[(bh2 * splits + sp) * D + d] = 0.f;
             if (d == 0) part_lse[bh2 * splits + sp] = -INFINITY;
           }
         }
@@ -131,14 +139,15 @@ struct TileCursor {
   }
 };
 
-template <int G>
+template <int G, int D>
 __global__ void __launch_bounds__(128, 1)
     attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                           const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables,
                           const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
                           float* __restrict__ part_o, float* __restrict__ part_lse, int B, int Hkv, int max_blocks,
                           int splits, int chunk_blocks, float scale_log2, int* status, int* work) {
-  constexpr int D = 128;
+  using CF = DecCfg<D>;
+  constexpr int kKBytes = CF::kKBytes, kVBytes = CF::kVBytes, kQBytes = CF::kQBytes, kPBytes = CF::kPBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = sm;
@@ -162,7 +171,7 @@ __global__ void __launch_bounds__(128, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 32);
+    tmem_alloc(tmem_slot, CF::kTmemCols);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -186,7 +195,7 @@ __global__ void __launch_bounds__(128, 1)
   pdl_trigger();
 
   // tile descriptors: cur (being computed) and nxt (being loaded)
-  TileCursor<G> cursor{-1, 0, 0, B, Hkv, splits, chunk_blocks, items, ctx_lens, max_blocks, work, ticket};
+  TileCursor<G, D> cursor{-1, 0, 0, B, Hkv, splits, chunk_blocks, items, ctx_lens, max_blocks, work, ticket};
   TileRef cur, nxt;
   bool has_cur = cursor.next(cur, out, part_o, part_lse);
   bool has_nxt = false;
@@ -196,20 +205,21 @@ __global__ void __launch_bounds__(128, 1)
   auto issue_k = [&](const TileRef& r) {  // warp 0
     const int* bt = block_tables + (size_t)r.b * max_blocks;
     const int nv = max(0, min(8, r.nblk - r.t0 / 16));
-    if (lane == 0) mbar_arrive_expect_tx(&bars[0], nv * 4096);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[0], nv * D * 32);
     __syncwarp();
     if (lane < nv) {
       const int krow = (bt[r.t0 / 16 + lane] * Hkv + r.hk) * kBS;
-      tma_load_2d(sK + lane * 2048, &tmK, &bars[0], 0, krow);
-      tma_load_2d(sK + 16384 + lane * 2048, &tmK, &bars[0], 64, krow);
+#pragma unroll
+      for (int c = 0; c < CF::kChunks; ++c) tma_load_2d(sK + c * 16384 + lane * 2048, &tmK, &bars[0], c * 64, krow);
     }
   };
   auto issue_v = [&](const TileRef& r) {  // warp 0
     const int* bt = block_tables + (size_t)r.b * max_blocks;
     const int nv = max(0, min(8, r.nblk - r.t0 / 16));
-    if (lane == 0) mbar_arrive_expect_tx(&bars[1], nv * 4096);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[1], nv * CF::kVBlock);
     __syncwarp();
-    if (lane < nv) tma_load_2d(sV + lane * 4096, &tmV, &bars[1], 0, (bt[r.t0 / 16 + lane] * Hkv + r.hk) * D);
+    if (lane < nv)
+      tma_load_2d(sV + lane * CF::kVBlock, &tmV, &bars[1], 0, (bt[r.t0 / 16 + lane] * Hkv + r.hk) * D);
   };
   auto load_q = [&](const TileRef& r) {  // all threads
     uint8_t* dst = sQ;
@@ -230,12 +240,13 @@ __global__ void __launch_bounds__(128, 1)
     fence_async_smem();
     __syncthreads();
   }
-  float m[G], l[G], acc[G];
+  float m[G], l[G], acc[CF::kHalves][G];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     m[h] = -INFINITY;
     l[h] = 0.f;
-    acc[h] = 0.f;
+#pragma unroll
+    for (int hf = 0; hf < CF::kHalves; ++hf) acc[hf][h] = 0.f;
   }
   uint32_t it = 0;
   while (has_cur) {
@@ -246,7 +257,7 @@ __global__ void __launch_bounds__(128, 1)
     if (tid == 32 && ok) {
       const uint32_t qb = smem_u32(sQ);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
+      for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
         const uint32_t qoff = (kk >> 2) * 2048 + (kk & 3) * 32;
         tc_mma_bf16(tS, make_sdesc_k128(smem_u32(sK) + off), make_sdesc_k128(qb + qoff), idesc, kk > 0);
@@ -299,37 +310,46 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     if (tid == 32 && ok) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        tc_mma_bf16(tO, make_sdesc_k32(smem_u32(sV) + j * 4096), make_sdesc_k32(smem_u32(sP) + j * 512), idesc,
-                    j > 0);
+      for (int hf = 0; hf < CF::kHalves; ++hf)  // head-dim rows 128*hf.. of every V block
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          tc_mma_bf16(tO + hf * 16, make_sdesc_k32(smem_u32(sV) + j * CF::kVBlock + hf * 4096),
+                      make_sdesc_k32(smem_u32(sP) + j * 512), idesc, j > 0);
       tc_commit(&bars[3]);
     }
     ok = ok && mbar_wait(&bars[3], par, status);
     tc_fence_after();
     if (warp == 0 && has_nxt && ok) issue_v(nxt);
-    float o[16];
-    tmem_ld16(tO + lane_off, o);
+#pragma unroll
+    for (int hf = 0; hf < CF::kHalves; ++hf) {
+      float o[16];
+      tmem_ld16(tO + hf * 16 + lane_off, o);
+#pragma unroll
+      for (int h = 0; h < G; ++h) acc[hf][h] = acc[hf][h] * corr[h] + o[h];
+    }
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const float lt = red_sum[h] + red_sum[16 + h] + red_sum[32 + h] + red_sum[48 + h];
       l[h] = l[h] * corr[h] + lt;
-      acc[h] = acc[h] * corr[h] + o[h];
     }
-    if (cur.last) {  // thread tid owns head-dim element d = tid
-      const int d = tid;
+    if (cur.last) {  // thread tid owns head-dim elements d = tid + 128 * hf
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float v = l[h] > 0.f ? acc[h] / l[h] : 0.f;
         const size_t bh = (size_t)cur.b * Hq + cur.hk * G + h;
-        if (splits == 1) {
-          out[bh * D + d] = __float2bfloat16(v);
-        } else {
-          part_o[(bh * splits + cur.sp) * D + d] = v;
-          if (d == 0) part_lse[bh * splits + cur.sp] = l[h] > 0.f ? m[h] + log2f(l[h]) : -INFINITY;
+#pragma unroll
+        for (int hf = 0; hf < CF::kHalves; ++hf) {
+          const int d = tid + 128 * hf;
+          const float v = l[h] > 0.f ? acc[hf][h] / l[h] : 0.f;
+          if (splits == 1) {
+            out[bh * D + d] = __float2bfloat16(v);
+          } else {
+            part_o[(bh * splits + cur.sp) * D + d] = v;
+            if (d == 0) part_lse[bh * splits + cur.sp] = l[h] > 0.f ? m[h] + log2f(l[h]) : -INFINITY;
+          }
+          acc[hf][h] = 0.f;
         }
         m[h] = -INFINITY;
         l[h] = 0.f;
-        acc[h] = 0.f;
       }
     }
     tc_fence_before();
@@ -345,7 +365,7 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, CF::kTmemCols);
   }
   // the last CTA to finish resets the work counter for the next launch (no CTA fetches any more)
   if (work && tid == 0 && atomicAdd(work + 1, 1) == (int)gridDim.x - 1) {
@@ -357,10 +377,11 @@ __global__ void __launch_bounds__(128, 1)
 }  // namespace
 
 bool attn_decode_tc_supported(int64_t D, int64_t G) {
-  return D == 128 && (G == 1 || G == 2 || G == 4 || G == 8 || G == 16);
+  return (D == 128 && (G == 1 || G == 2 || G == 4 || G == 8 || G == 16)) ||
+         (D == 256 && (G == 1 || G == 2 || G == 4 || G == 8));
 }
 
-// Same contract as attn_decode (attn_decode.cu); head_dim 128, group <= 16.
+// Same contract as attn_decode (attn_decode.cu); head_dim 128 (group <= 16) or 256 (group <= 8).
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                     const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
                     const c10::optional<at::Tensor>& workspace, double scale, at::Tensor& work) {
@@ -372,7 +393,7 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
   const int Hkv = (int)k_cache.size(1), NB = (int)k_cache.size(0);
   TORCH_CHECK(Hq % Hkv == 0 && k_cache.size(3) == D && v_cache.size(2) == D);
   const int G = Hq / Hkv;
-  TORCH_CHECK(attn_decode_tc_supported(D, G), "attn_decode_tc: needs head_dim 128 and group <= 16");
+  TORCH_CHECK(attn_decode_tc_supported(D, G), "attn_decode_tc: needs head_dim 128 (group <= 16) or 256 (group <= 8)");
   TORCH_CHECK(work.scalar_type() == at::kInt && work.is_cuda() && (work.numel() == 0 || work.numel() >= 2),
               "attn_decode_tc: work must be empty (static schedule) or a zeroed int32 device tensor of 2 "
               "elements (dynamic schedule; kept zero by the kernel)");
@@ -394,38 +415,51 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
   auto tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (int64_t)NB * Hkv * D, 16, 32, 16, D,
                          CU_TENSOR_MAP_SWIZZLE_32B);
   const float sl2 = (float)(scale * 1.4426950408889634);
-  // persistent grid: every resident CTA (three per SM at this shared-memory size)
+  // persistent grid: every resident CTA (three per SM at D = 128, one at D = 256)
   static int sms = 0;
   if (!sms) C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.device().index()));
-  const int per_sm = std::max(1, std::min(3, (int)(228 * 1024 / (kSmemBytes + 1024))));
   const int mbk = (int)block_tables.size(1);
   const int chunk_blocks = (mbk + (int)splits - 1) / (int)splits;
   const int items = B * Hkv * (int)splits;
-  const int grid = std::min(items, per_sm * sms);
-  static bool attr[17] = {false};
-  auto go = [&](auto kernel, int g) {
-    if (!attr[g]) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-      attr[g] = true;
+  static bool attr[2][17] = {{false}};
+  auto go = [&](auto kernel, int g, int smem) {
+    const int di = D == 256;
+    if (!attr[di][g]) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr[di][g] = true;
     }
-    launch_k(kernel, grid, 128, kSmemBytes, st, tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
-                                          block_tables.data_ptr<int>(), ctx_lens.data_ptr<int>(),
-                                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), po, pl, B, Hkv, mbk,
-                                          (int)splits, chunk_blocks, sl2, status_ptr(q.device().index()),
-                                          work.numel() ? work.data_ptr<int>() : nullptr);
+    const int per_sm = std::max(1, std::min(3, (int)(228 * 1024 / (smem + 1024))));
+    const int grid = std::min(items, per_sm * sms);
+    launch_k(kernel, grid, 128, smem, st, tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
+             block_tables.data_ptr<int>(), ctx_lens.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+             po, pl, B, Hkv, mbk, (int)splits, chunk_blocks, sl2, status_ptr(q.device().index()),
+             work.numel() ? work.data_ptr<int>() : nullptr);
   };
-  switch (G) {
-    case 1: go(attn_decode_tc_kernel<1>, 1); break;
-    case 2: go(attn_decode_tc_kernel<2>, 2); break;
-    case 4: go(attn_decode_tc_kernel<4>, 4); break;
-    case 8: go(attn_decode_tc_kernel<8>, 8); break;
-    case 16: go(attn_decode_tc_kernel<16>, 16); break;
-    default: TORCH_CHECK(false, "attn_decode_tc: group size must be 1, 2, 4, 8 or 16");
+  constexpr int s128 = DecCfg<128>::kSmemBytes, s256 = DecCfg<256>::kSmemBytes;
+  if (D == 128) {
+    switch (G) {
+      case 1: go(attn_decode_tc_kernel<1, 128>, 1, s128); break;
+      case 2: go(attn_decode_tc_kernel<2, 128>, 2, s128); break;
+      case 4: go(attn_decode_tc_kernel<4, 128>, 4, s128); break;
+      case 8: go(attn_decode_tc_kernel<8, 128>, 8, s128); break;
+      default: go(attn_decode_tc_kernel<16, 128>, 16, s128); break;
+    }
+  } else {
+    switch (G) {
+      case 1: go(attn_decode_tc_kernel<1, 256>, 1, s256); break;
+      case 2: go(attn_decode_tc_kernel<2, 256>, 2, s256); break;
+      case 4: go(attn_decode_tc_kernel<4, 256>, 4, s256); break;
+      default: go(attn_decode_tc_kernel<8, 256>, 8, s256); break;
+    }
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (splits > 1) {
-    launch_k(attn_combine_kernel<128>, B * Hq, 128, 0, st, po, pl, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                    (int)splits);
+    if (D == 128)
+      launch_k(attn_combine_kernel<128>, B * Hq, 128, 0, st, po, pl, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+               (int)splits);
+    else
+      launch_k(attn_combine_kernel<256>, B * Hq, 128, 0, st, po, pl, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+               (int)splits);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

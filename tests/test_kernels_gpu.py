@@ -172,19 +172,23 @@ def test_attn_decode(cuda, B, Hq, Hkv, D, splits):
 @pytest.mark.parametrize("B,Hq,Hkv,splits,lens", [(4, 32, 4, 1, (1, 17, 100, 255)), (3, 32, 4, 4, (300, 129, 16)),
                                                   (2, 16, 8, 1, (128, 513)), (5, 8, 8, 3, (1, 2, 3, 700, 64)),
                                                   (2, 64, 4, 2, (77, 1000)), (2, 16, 2, 1, (0, 40))])
-def test_attn_decode_tc(cuda, B, Hq, Hkv, splits, lens):
+@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("dynamic", [True, False])
+def test_attn_decode_tc(cuda, B, Hq, Hkv, splits, lens, D, dynamic):
     native, check = _N()
     from mod_b200.ops import reference as R
 
+    if D == 256 and Hq // Hkv > 8:
+        pytest.skip("head_dim 256 covers groups up to 8")
     torch.manual_seed(5)
-    D, nb = 128, 160
+    nb = 160
     kc, vc = _rand(nb, Hkv, 16, D), _rand(nb, Hkv, D, 16)
     lens_t = torch.tensor(lens, dtype=torch.int32)
     maxb = 64
     bt = torch.stack([torch.randperm(nb)[:maxb] for _ in range(B)]).int()
     q = _rand(B, Hq, D)
     ws = torch.empty(B * Hq * splits * (D + 1), device=cuda, dtype=torch.float32)
-    o = native.attn_decode_tc(q, kc, vc, bt.cuda(), lens_t.cuda(), splits=splits, workspace=ws)
+    o = native.attn_decode_tc(q, kc, vc, bt.cuda(), lens_t.cuda(), splits=splits, workspace=ws, dynamic=dynamic)
     check()
     ref = R.attn_decode(q.float(), kc.float(), vc.float(), bt.cuda(), lens_t.clamp(min=1))
     for b in range(B):

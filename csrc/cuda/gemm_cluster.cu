@@ -37,12 +37,15 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"  // i8x4_to_bf16x4
 #include "launch.cuh"
 #include "status.h"
 
 namespace mb {
 
 CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows);
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows, int64_t cols, int64_t ld_bytes,
+                         int box_cols, int box_rows, CUtensorMapSwizzle sw);
 
 namespace {
 
@@ -67,6 +70,7 @@ struct ClusterArgs {
   int Hq, Hkv, rot_dim, block_size;
   float eps;
   int* status;
+  const float* w_scale;   // int8 weights: per-row (output feature) scale, applied after the reduction
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -89,28 +93,34 @@ __device__ __forceinline__ float ld_dsmem(uint32_t addr) {
   return v;
 }
 
-template <int BN, int STAGES>
+// Stage: A tile [128 x 64] bf16 SW128 | B tile [BN x 64] bf16 SW128 | (int8 weights) the raw
+// int8 A tile [128 x 64] that the epilogue warps expand into the A slot.
+template <int BN, int STAGES, bool W8>
 struct CSmem {
   static constexpr int kABytes = 128 * 64 * 2;
   static constexpr int kBBytes = BN * 64 * 2;
-  static constexpr int kStage = kABytes + kBBytes;
+  static constexpr int kRawBytes = W8 ? 128 * 64 : 0;
+  static constexpr int kRawOff = kABytes + kBBytes;
+  static constexpr int kStage = kABytes + kBBytes + kRawBytes;
+  static constexpr int kTx = (W8 ? kRawBytes : kABytes) + kBBytes;   // bytes the TMA delivers per stage
   static constexpr int kPartial = BN * 128 * 4;   // fp32 tile parked for the cluster reduction
   static constexpr int kRing = STAGES * kStage > kPartial ? STAGES * kStage : kPartial;
   static constexpr int kBytes = 1024 + kRing + 2048;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool W8>
 __global__ void __launch_bounds__(192, 1)
     gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         ClusterArgs args) {
-  using L = CSmem<BN, STAGES>;
+  using L = CSmem<BN, STAGES, W8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tail = smem + L::kRing;
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint64_t* cfull = empty + STAGES;   // int8: the stage's A tile has been expanded (4 warp arrivals)
+  uint64_t* tfull = cfull + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
   float* red = reinterpret_cast<float*>(tmem_slot + 4);     // [4 warps] cross-warp sums
   float* rot = red + 8;                                      // [128] one head vector for RoPE
@@ -127,6 +137,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&cfull[s], 4);
     }
     mbar_init(tfull, 1);
     fence_mbar_init();
@@ -151,8 +162,8 @@ __global__ void __launch_bounds__(192, 1)
       // weight tiles of the first stages go out before the dependency wait (weights are immutable)
       const int pre = min(STAGES, kbs);
       for (int s = 0; s < pre; ++s) {
-        mbar_arrive_expect_tx(&full[s], L::kStage);
-        tma_load_2d(smem + s * L::kStage, &tmA, &full[s], (kb_lo + s) * 64, m_tile * 128);
+        mbar_arrive_expect_tx(&full[s], L::kTx);
+        tma_load_2d(smem + s * L::kStage + (W8 ? L::kRawOff : 0), &tmA, &full[s], (kb_lo + s) * 64, m_tile * 128);
       }
       pdl_wait();
       pdl_trigger();
@@ -161,8 +172,8 @@ __global__ void __launch_bounds__(192, 1)
         uint8_t* st = smem + s * L::kStage;
         if (it >= pre) {
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, args.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], L::kStage);
-          tma_load_2d(st, &tmA, &full[s], (kb_lo + it) * 64, m_tile * 128);
+          mbar_arrive_expect_tx(&full[s], L::kTx);
+          tma_load_2d(st + (W8 ? L::kRawOff : 0), &tmA, &full[s], (kb_lo + it) * 64, m_tile * 128);
         }
         tma_load_2d(st + L::kABytes, &tmB, &full[s], (kb_lo + it) * 64, 0);
       }
@@ -179,6 +190,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int it = 0; it < kbs && ok; ++it) {
         const int s = it % STAGES;
         if (!mbar_wait(&full[s], (it / STAGES) & 1, args.status)) { ok = false; break; }
+        if (W8 && !mbar_wait(&cfull[s], (it / STAGES) & 1, args.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * L::kStage);
         const uint32_t b_addr = a_addr + L::kABytes;
@@ -193,6 +205,30 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     pdl_wait();
     pdl_trigger();
+    if (W8) {
+      // ------------------------------------------------ int8 -> bf16 expansion (epilogue warps)
+      // thread c expands 16-byte chunks idx = c + 128 m of the [128 x 64] tile: row r = idx / 8,
+      // chunk k = idx % 8 -> SW128 position r*128 + (k ^ (r % 8))*16
+      const int c = threadIdx.x - 64;
+      for (int it = 0; it < kbs; ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1, args.status)) break;
+        uint8_t* st = smem + s * L::kStage;
+        const uint8_t* raw = st + L::kRawOff;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int idx = c + 128 * m, r = idx >> 3, k = idx & 7;
+          const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 64 + k * 8);
+          uint4 o;
+          i8x4_to_bf16x4(w.x, o.x, o.y);
+          i8x4_to_bf16x4(w.y, o.z, o.w);
+          *reinterpret_cast<uint4*>(st + r * 128 + ((k ^ (r & 7)) << 4)) = o;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cfull[s]);
+      }
+    }
   }
 
   // ------------------------------------------------ park the partial tile in shared memory
@@ -229,6 +265,7 @@ __global__ void __launch_bounds__(192, 1)
       float acc = 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc += part[c];
+      if (W8) acc *= args.w_scale[m_tile * 128 + f];
       if (args.mode == kCStore) {
         const size_t o = (size_t)j * args.ldc + (size_t)m_tile * 128 + f;
         if (args.residual) acc += __bfloat162float(args.residual[o]);
@@ -283,11 +320,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool W8>
 void launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const ClusterArgs& a, int m_tiles, int cs,
                     cudaStream_t st) {
-  using L = CSmem<BN, STAGES>;
-  auto k = gemm_cluster_kernel<BN, STAGES>;
+  using L = CSmem<BN, STAGES, W8>;
+  auto k = gemm_cluster_kernel<BN, STAGES, W8>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
@@ -324,10 +361,14 @@ int pick_cs(int m_tiles, int kb_total, int sms) {
   return cs;
 }
 
+// w: bf16 [N, K], or int8 [N, K] with a.w_scale set (per-row scales).
 void run(const at::Tensor& x, const at::Tensor& w, ClusterArgs a, int64_t cs_req) {
   const int64_t T = x.size(0), K = x.size(1), N = w.size(0);
+  const bool w8 = w.scalar_type() == at::kChar;
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
-  auto ta = make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), 128);
+  auto ta = w8 ? make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, w.stride(0), 64, 128,
+                              CU_TENSOR_MAP_SWIZZLE_NONE)
+               : make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), 128);
   auto tb = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
   const int m_tiles = (int)(N / 128);
   const int kb_total = (int)((K + 63) / 64);
@@ -339,18 +380,28 @@ void run(const at::Tensor& x, const at::Tensor& w, ClusterArgs a, int64_t cs_req
   a.T = (int)T;
   a.status = status_ptr(x.device().index());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  // stage counts keep a CTA near 100 KB of shared memory, so two share an SM
-  switch (bn) {
-    case 16: launch_cluster<16, 5>(ta, tb, a, m_tiles, cs, st); break;
-    case 32: launch_cluster<32, 5>(ta, tb, a, m_tiles, cs, st); break;
-    case 64: launch_cluster<64, 4>(ta, tb, a, m_tiles, cs, st); break;
-    default: launch_cluster<128, 3>(ta, tb, a, m_tiles, cs, st); break;
+  // stage counts keep a CTA near 100-120 KB of shared memory
+  if (w8) {
+    switch (bn) {
+      case 16: launch_cluster<16, 4, true>(ta, tb, a, m_tiles, cs, st); break;
+      case 32: launch_cluster<32, 4, true>(ta, tb, a, m_tiles, cs, st); break;
+      case 64: launch_cluster<64, 3, true>(ta, tb, a, m_tiles, cs, st); break;
+      default: launch_cluster<128, 3, true>(ta, tb, a, m_tiles, cs, st); break;
+    }
+  } else {
+    switch (bn) {
+      case 16: launch_cluster<16, 5, false>(ta, tb, a, m_tiles, cs, st); break;
+      case 32: launch_cluster<32, 5, false>(ta, tb, a, m_tiles, cs, st); break;
+      case 64: launch_cluster<64, 4, false>(ta, tb, a, m_tiles, cs, st); break;
+      default: launch_cluster<128, 3, false>(ta, tb, a, m_tiles, cs, st); break;
+    }
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void check_operands(const at::Tensor& x, const at::Tensor& w) {
-  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 &&
+              (w.scalar_type() == at::kBFloat16 || w.scalar_type() == at::kChar));
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && w.size(1) == x.size(1));
   TORCH_CHECK(x.size(0) >= 1 && x.size(0) <= 128, "gemm_cluster: 1..128 tokens");
   TORCH_CHECK(w.size(0) % 128 == 0 && x.size(1) % 64 == 0, "gemm_cluster: N % 128 == 0 and K % 64 == 0");
@@ -362,6 +413,7 @@ void check_operands(const at::Tensor& x, const at::Tensor& w) {
 void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
                     const c10::optional<at::Tensor>& residual, int64_t cs) {
   check_operands(x, w);
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16, "linear_cluster: bf16 weights (int8: linear_cluster_w8)");
   TORCH_CHECK(y.is_contiguous() && y.scalar_type() == at::kBFloat16 && y.size(0) == x.size(0) &&
               y.size(1) == w.size(0));
   c10::cuda::CUDAGuard guard(x.device());
@@ -376,6 +428,26 @@ void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
   run(x, w, a, cs);
 }
 
+// int8 weight-only: y = (x @ wq^T) * scale[n] (+ residual); wq int8 [N, K], scale fp32 [N].
+void linear_cluster_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
+                       const c10::optional<at::Tensor>& residual, int64_t cs) {
+  check_operands(x, wq);
+  TORCH_CHECK(wq.scalar_type() == at::kChar && scale.scalar_type() == at::kFloat && scale.numel() == wq.size(0));
+  TORCH_CHECK(y.is_contiguous() && y.scalar_type() == at::kBFloat16 && y.size(0) == x.size(0) &&
+              y.size(1) == wq.size(0));
+  c10::cuda::CUDAGuard guard(x.device());
+  ClusterArgs a{};
+  a.mode = kCStore;
+  a.out = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.ldc = (int)y.size(1);
+  a.w_scale = scale.data_ptr<float>();
+  if (residual && residual->defined()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == y.sizes());
+    a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  run(x, wq, a, cs);
+}
+
 // Packed QKV projection (head_dim 128) with per-head QK-RMSNorm, RoPE and the
 // paged KV write fused into the cluster reduction: same outputs as
 // linear + rope_qknorm.
@@ -384,6 +456,7 @@ void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optio
                       const c10::optional<at::Tensor>& slots, at::Tensor& q_out, at::Tensor& k_cache,
                       at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs) {
   check_operands(x, w);
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16, "qkv_rope_cluster: bf16 weights");
   const int64_t T = x.size(0);
   TORCH_CHECK(w.size(0) == (Hq + 2 * Hkv) * 128, "qkv_rope_cluster: w must be [(Hq + 2 Hkv) * 128, K]");
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() == T && inv_freq.scalar_type() == at::kFloat);

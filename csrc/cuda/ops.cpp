@@ -99,6 +99,8 @@ void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
                      at::Tensor& out, double eps, const c10::optional<at::Tensor>& rows);
 void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
                     const c10::optional<at::Tensor>& residual, int64_t cs);
+void linear_cluster_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
+                       const c10::optional<at::Tensor>& residual, int64_t cs);
 void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& q_w,
                       const c10::optional<at::Tensor>& k_w, const at::Tensor& positions, const at::Tensor& inv_freq,
                       const c10::optional<at::Tensor>& slots, at::Tensor& q_out, at::Tensor& k_cache,
@@ -119,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear", &mb::linear);
   m.def("linear_cluster", &mb::linear_cluster);
   m.def("qkv_rope_cluster", &mb::qkv_rope_cluster);
+  m.def("linear_cluster_w8", &mb::linear_cluster_w8);
   m.def("grouped_linear", &mb::grouped_linear);
   m.def("swiglu_linear", &mb::swiglu_linear);
   m.def("rmsnorm", &mb::rmsnorm);

@@ -53,6 +53,20 @@ def case(name: str, T: int = 128):
             torch.matmul(x, ws[i[0] % len(ws)].t(), out=y)
             i[0] += 1
         return run, K * Nn * 2 + T * K * 2 + T * Nn * 2, 2 * T * K * Nn
+    if name.startswith("clw8:"):  # int8-weight cluster GEMM: clw8:qkv, clw8:o
+        from ..ops.quant import quantize_int8
+
+        K, Nn = {"qkv": (2048, 5120), "o": (4096, 2048)}[name.split(":")[1]]
+        ws = _rot(lambda: quantize_int8(torch.randn(Nn, K, device=dev) * 0.02), K * Nn)
+        x = torch.randn(T, K, device=dev).to(bf)
+        y = torch.empty(T, Nn, device=dev, dtype=bf)
+        i = [0]
+
+        def run():
+            w = ws[i[0] % len(ws)]
+            N.linear_cluster_w8(x, w.q, w.scale, out=y)
+            i[0] += 1
+        return run, K * Nn + Nn * 4 + T * K * 2 + T * Nn * 2, 2 * T * K * Nn
     if name.startswith("cl:"):  # cluster split-K GEMM (DSMEM reduction): cl:qkv, cl:o, cl:router[:cs]
         parts = name.split(":")
         K, Nn = {"qkv": (2048, 5120), "o": (4096, 2048), "router": (2048, 128)}[parts[1]]

@@ -102,18 +102,26 @@ class NativeBackend:
         return torch.arange(2, dtype=torch.int32, device=device) * T
 
     def _cluster_ok(self, x2, w) -> bool:
-        """Decode-sized bf16 GEMMs run on the cluster split-K kernel (DSMEM reduction, one launch)."""
-        if not self.cluster_gemm or isinstance(w, Int8Weight) or w.dtype != torch.bfloat16:
+        """Decode-sized GEMMs (bf16 or int8 weights) run on the cluster split-K kernel (DSMEM
+        reduction, one launch)."""
+        if not self.cluster_gemm or x2.dtype != torch.bfloat16:
+            return False
+        wt = w.q if isinstance(w, Int8Weight) else w
+        if wt.dtype not in (torch.bfloat16, torch.int8):
             return False
         T, K = x2.shape
-        return (1 <= T <= 128 and w.shape[0] % 128 == 0 and w.shape[0] <= 16384 and K % 64 == 0
-                and x2.stride(1) == 1 and w.is_contiguous())
+        return (1 <= T <= 128 and wt.shape[0] % 128 == 0 and wt.shape[0] <= 16384 and K % 64 == 0
+                and x2.stride(1) == 1 and wt.is_contiguous())
 
     def linear(self, x, w, bias=None, residual=None, out=None):
         x2 = x.reshape(-1, x.shape[-1])
         if bias is None and self._cluster_ok(x2, w) and (out is None or out.is_contiguous()):
-            y = self.N.linear_cluster(x2, w, out=None if out is None else out.view(x2.shape[0], w.shape[0]),
-                                      residual=None if residual is None else residual.reshape(x2.shape[0], -1))
+            o = None if out is None else out.view(x2.shape[0], w.shape[0])
+            r = None if residual is None else residual.reshape(x2.shape[0], -1)
+            if isinstance(w, Int8Weight):
+                y = self.N.linear_cluster_w8(x2, w.q, w.scale, out=o, residual=r)
+            else:
+                y = self.N.linear_cluster(x2, w, out=o, residual=r)
             return y if out is None else out
         T = x2.shape[0]
         ws = None

@@ -46,6 +46,16 @@ def linear_cluster(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]
     return out
 
 
+def linear_cluster_w8(x: torch.Tensor, wq: torch.Tensor, scale: torch.Tensor, out: Optional[torch.Tensor] = None,
+                      residual: Optional[torch.Tensor] = None, cs: int = 0) -> torch.Tensor:
+    """int8 weight-only ``out = (x @ wq.T) * scale (+ residual)`` for decode-sized x: the cluster
+    split-K GEMM with each int8 weight tile expanded to bf16 in shared memory."""
+    if out is None:
+        out = torch.empty(x.shape[0], wq.shape[0], dtype=x.dtype, device=x.device)
+    _C().linear_cluster_w8(x, wq, scale, out, residual, cs)
+    return out
+
+
 def qkv_rope_cluster(x, w, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, rot_dim, eps,
                      cs: int = 0):
     """Packed QKV projection (head_dim 128) with QK-RMSNorm, RoPE and the paged KV

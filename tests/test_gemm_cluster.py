@@ -58,3 +58,18 @@ def test_qkv_rope_cluster_matches_unfused(cuda, T, Hq, Hkv, rot):
     from mod_b200.ops import check_status
 
     check_status()
+
+
+@pytest.mark.parametrize("T,K,N", [(1, 2048, 128), (16, 2048, 5120), (100, 1024, 384), (128, 2048, 2048)])
+def test_linear_cluster_w8_matches_fp32(cuda, T, K, N):
+    from mod_b200.ops import native
+    from mod_b200.ops.quant import quantize_int8
+
+    torch.manual_seed(T + N)
+    x = torch.randn(T, K, device=cuda).bfloat16()
+    qw = quantize_int8(torch.randn(N, K, device=cuda) * 0.05)
+    res = torch.randn(T, N, device=cuda).bfloat16()
+    y = native.linear_cluster_w8(x, qw.q, qw.scale, residual=res)
+    ref = x.float() @ (qw.q.float() * qw.scale[:, None]).t() + res.float()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * max(1.0, ref.abs().max().item()) / 8)

@@ -24,6 +24,7 @@
 // Replaces the reference's decayed linear-attention recurrence
 // (pio/plugins/cuda/c_src/tensor_ops_cuda.cu:420-452).
 #include <cstdlib>
+#include <type_traits>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -43,13 +44,13 @@ __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162f
 
 // Prefill conv + SiLU + q/k L2 norm, CTA per token.  mixed [T, C] raw; seq_of [T] / cu [nseq+1]
 // place the token in its sequence, and positions before the sequence start read the slot's
-// history (advanced later by the scan kernel).  Output xc [T, C] f32, q heads also scaled by
-// DK^-1/2.
-template <int DK, int KC>
+// history (advanced later by the scan kernel).  Output xc [T, C] (fp32 for the token-serial scan,
+// bf16 for the chunked scan, whose products take bf16 operands), q heads also scaled by DK^-1/2.
+template <int DK, int KC, typename OutT>
 __global__ void __launch_bounds__(256)
     deltanet_conv_kernel(const __nv_bfloat16* __restrict__ mixed, const __nv_bfloat16* __restrict__ conv_w,
                          float* __restrict__ conv_state, const int64_t* __restrict__ slots,
-                         const int* __restrict__ seq_of, const int* __restrict__ cu, float* __restrict__ xc, int C,
+                         const int* __restrict__ seq_of, const int* __restrict__ cu, OutT* __restrict__ xc, int C,
                          int Hk) {
   pdl_wait();
   pdl_trigger();
@@ -81,8 +82,11 @@ __global__ void __launch_bounds__(256)
     for (int i = l; i < DK; i += 32) row[hh * DK + i] *= sc;
   }
   __syncthreads();
-  float* dst = xc + (int64_t)t * C;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) dst[c] = row[c];
+  OutT* dst = xc + (int64_t)t * C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    if constexpr (std::is_same<OutT, float>::value) dst[c] = row[c];
+    else dst[c] = __float2bfloat16(row[c]);
+  }
 }
 
 // Decode conv: one thread per (token, channel), all channels in parallel.  Every token is its
@@ -362,7 +366,7 @@ void deltanet_decode(const at::Tensor& mixed, const at::Tensor& z, const at::Ten
 }
 
 // Prefill of nseq sequences packed in mixed [T, C] (cu [nseq+1] int32 offsets, seq_of [T]).
-void launch_deltanet_chunk(const float* xc, const __nv_bfloat16* mixed, float* conv_state, const __nv_bfloat16* z,
+void launch_deltanet_chunk(const __nv_bfloat16* xc, const __nv_bfloat16* mixed, float* conv_state, const __nv_bfloat16* z,
                            const __nv_bfloat16* ba, float* ssm, const int64_t* slots, const int* cu, const float* A_log,
                            const float* dt_bias, const __nv_bfloat16* norm_w, __nv_bfloat16* out, int nseq, int Hk,
                            int Hv, float eps, cudaStream_t st);
@@ -399,22 +403,32 @@ void deltanet_prefill(const at::Tensor& mixed, const at::Tensor& z, const at::Te
   const size_t smem = (size_t)C * sizeof(float);
 #define MB_DP(DK_, DV_, KC_)                                                                                      \
   if (dk == DK_ && dv == DV_ && KC == KC_) {                                                                      \
-    auto ck = deltanet_conv_kernel<DK_, KC_>;                                                              \
+    const bool chunked = DK_ == 128 && DV_ == 128 && KC_ == 4 && use_chunked();                                   \
+    if (chunked) {                                                                                                \
+      /* bf16 conv output (written into the fp32 buffer's first half) for the chunked scan */                     \
+      auto ck = deltanet_conv_kernel<DK_, KC_, __nv_bfloat16>;                                                    \
+      if (smem > 48 * 1024)                                                                                       \
+        C10_CUDA_CHECK(cudaFuncSetAttribute(ck, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));         \
+      auto xb = reinterpret_cast<__nv_bfloat16*>(xc.data_ptr<float>());                                           \
+      launch_k(ck, dim3(T), 256, smem, st, bp(mixed), bp(conv_w), conv_state.data_ptr<float>(),                   \
+               (const int64_t*)slots.data_ptr<int64_t>(), (const int*)seq_of.data_ptr<int>(),                     \
+               (const int*)cu.data_ptr<int>(), xb, C, (int)Hk);                                                   \
+      C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                             \
+      launch_deltanet_chunk(xb, bp(mixed), conv_state.data_ptr<float>(), bp(z), bp(ba), ssm.data_ptr<float>(),    \
+                            (const int64_t*)slots.data_ptr<int64_t>(), (const int*)cu.data_ptr<int>(),            \
+                            (const float*)A_log.data_ptr<float>(), (const float*)dt_bias.data_ptr<float>(),       \
+                            bp(norm_w), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nseq, (int)Hk, (int)Hv, \
+                            (float)eps, st);                                                                      \
+      return;                                                                                                     \
+    }                                                                                                             \
+    auto ck = deltanet_conv_kernel<DK_, KC_, float>;                                                              \
     if (smem > 48 * 1024)                                                                                         \
       C10_CUDA_CHECK(cudaFuncSetAttribute(ck, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));           \
     launch_k(ck, dim3(T), 256, smem, st, bp(mixed), bp(conv_w), conv_state.data_ptr<float>(),                     \
              (const int64_t*)slots.data_ptr<int64_t>(), (const int*)seq_of.data_ptr<int>(),                       \
              (const int*)cu.data_ptr<int>(), xc.data_ptr<float>(), C, (int)Hk);                                    \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                               \
-    if (DK_ == 128 && DV_ == 128 && KC_ == 4 && use_chunked()) {                                                  \
-      launch_deltanet_chunk((const float*)xc.data_ptr<float>(), bp(mixed), conv_state.data_ptr<float>(), bp(z),  \
-                            bp(ba), ssm.data_ptr<float>(), (const int64_t*)slots.data_ptr<int64_t>(),            \
-                            (const int*)cu.data_ptr<int>(), (const float*)A_log.data_ptr<float>(),               \
-                            (const float*)dt_bias.data_ptr<float>(), bp(norm_w),                                 \
-                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nseq, (int)Hk, (int)Hv, (float)eps, st); \
-      return;                                                                                                     \
-    }                                                                                                             \
-    launch_k(deltanet_scan_kernel<DK_, DV_, KC_, 2>, dim3(nseq, (unsigned)Hv), 2 * DV_, 0, st,                          \
+    launch_k(deltanet_scan_kernel<DK_, DV_, KC_, 2>, dim3(nseq, (unsigned)Hv), 2 * DV_, 0, st,                   \
              (const float*)xc.data_ptr<float>(), bp(mixed), bp(z), bp(ba), conv_state.data_ptr<float>(),           \
              ssm.data_ptr<float>(), (const int64_t*)slots.data_ptr<int64_t>(), (const int*)cu.data_ptr<int>(),    \
              (const float*)A_log.data_ptr<float>(), (const float*)dt_bias.data_ptr<float>(), bp(norm_w),          \

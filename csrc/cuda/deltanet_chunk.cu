@@ -26,7 +26,9 @@
 // block recurrence T_ij = -T_ii sum_k M_ik T_kj.
 //
 // Inputs are the outputs of deltanet_conv_kernel (conv + SiLU + q/k L2 norm,
-// q scaled by dk^-1/2, fp32 [T, C]) plus the gate logits ba and z.
+// q scaled by dk^-1/2, bf16 [T, C]) plus the gate logits ba and z.  The next
+// chunk's q / k / v rows are copied into a staging buffer with cp.async while
+// the current chunk computes, so the chunk step never waits on global loads.
 // Reference: pio/models/qwen3_coder_next/model.py:245-277 (a decayed linear
 // attention in the reference, not the delta rule).
 #include <torch/extension.h>
@@ -58,7 +60,16 @@ struct ChunkSmem {
   float Tf[kC * (kC + 1)];        // T in fp32, and the block products
   float g[kC], gc[kC], beta[kC];
   float ss[2][kC];                // per-token sums of squares of O (two column halves)
+  __nv_bfloat16 stg[3][kC * kLdD];  // next chunk's q, k, v rows, filled by cp.async during this chunk
 };
+
+// 16-byte asynchronous global -> shared copy; src_bytes = 0 fills the 16 bytes with zeros.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -68,6 +79,9 @@ __device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t lds32(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+// Two fp32 -> bf16 conversions in one packed instruction (the scalar form is a separate
+// conversion per value, and the kernel is bound by that pipe otherwise).
+__device__ __forceinline__ __nv_bfloat162 pk(float a, float b) { return __floats2bfloat162_rn(a, b); }
 // A fragment (16x16) of a row-major [rows][ld] operand at (r0, k0).
 __device__ __forceinline__ void lda(uint32_t* a, const __nv_bfloat16* A, int ld, int r0, int k0, int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -96,7 +110,7 @@ __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + __expf(-x)); }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    deltanet_chunk_kernel(const float* __restrict__ xc, const __nv_bfloat16* __restrict__ mixed,
+    deltanet_chunk_kernel(const __nv_bfloat16* __restrict__ xc, const __nv_bfloat16* __restrict__ mixed,
                           float* __restrict__ conv_state, const __nv_bfloat16* __restrict__ z,
                           const __nv_bfloat16* __restrict__ ba, float* __restrict__ ssm,
                           const int64_t* __restrict__ slots, const int* __restrict__ cu,
@@ -132,15 +146,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       const int r = warp * 16 + g4, c = n * 8 + 2 * t4;
-      sm.ST[c * kLdD + r] = __float2bfloat16(S[n][0]);
-      sm.ST[(c + 1) * kLdD + r] = __float2bfloat16(S[n][1]);
-      sm.ST[c * kLdD + r + 8] = __float2bfloat16(S[n][2]);
-      sm.ST[(c + 1) * kLdD + r + 8] = __float2bfloat16(S[n][3]);
+      const __nv_bfloat162 a = pk(S[n][0], S[n][1]), b = pk(S[n][2], S[n][3]);
+      sm.ST[c * kLdD + r] = a.x;
+      sm.ST[(c + 1) * kLdD + r] = a.y;
+      sm.ST[c * kLdD + r + 8] = b.x;
+      sm.ST[(c + 1) * kLdD + r + 8] = b.y;
     }
   };
   store_ST();
 
   const int nchunks = (L + kC - 1) / kC;
+  // staging: chunk ch's q, k, v rows (16 x 16-byte pieces per 128-wide row); rows past the
+  // sequence are zero-filled
+  auto issue_stage = [&](int ch) {
+    const int tb = start + ch * kC, nval = min(kC, L - ch * kC);
+    for (int i = tid; i < 3 * kC * 16; i += kThreads) {
+      const int a = i / (kC * 16), r = (i / 16) % kC, seg = i % 16;
+      const int col = a == 0 ? hk * kD : a == 1 ? Hk * kD + hk * kD : 2 * Hk * kD + h * kD;
+      const bool in = r < nval;
+      const __nv_bfloat16* src = xc + (in ? (int64_t)(tb + r) * Ctot + col + seg * 8 : 0);
+      cp_async16(sm.stg[a] + r * kLdD + seg * 8, src, in ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  if (nchunks > 0) issue_stage(0);
   for (int ch = 0; ch < nchunks; ++ch) {
     const int t0 = start + ch * kC;
     const int valid = min(kC, L - ch * kC);
@@ -161,34 +190,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i <= tid; ++i) acc += sm.g[i];
       sm.gc[tid] = acc;
     }
-    // ---------------- operands: q, k rows (bf16), (beta v)^T
-    for (int i = tid; i < kC * (kD / 4); i += kThreads) {
-      const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-      float4 qv = make_float4(0.f, 0.f, 0.f, 0.f), kv = qv, vv = qv;
-      if (r < valid) {
-        const float* row = xc + (int64_t)(t0 + r) * Ctot;
-        qv = *reinterpret_cast<const float4*>(row + hk * kD + c4);
-        kv = *reinterpret_cast<const float4*>(row + Hk * kD + hk * kD + c4);
-        vv = *reinterpret_cast<const float4*>(row + 2 * Hk * kD + h * kD + c4);
+    // ---------------- operands from the staging buffer: q, k rows (bf16), (beta v)^T
+    cp_async_wait_all();
+    __syncthreads();  // staged rows visible to every thread; gates of this chunk written
+    // 8 channels per step: q, k rows copied; (beta v)^T and (beta exp(g) k)^T transposed
+    for (int i = tid; i < kC * 16; i += kThreads) {
+      const int r = i / 16, c0 = (i % 16) * 8;
+      const uint4 q8 = *reinterpret_cast<const uint4*>(sm.stg[0] + r * kLdD + c0);
+      const uint4 k8 = *reinterpret_cast<const uint4*>(sm.stg[1] + r * kLdD + c0);
+      const uint4 v8 = *reinterpret_cast<const uint4*>(sm.stg[2] + r * kLdD + c0);
+      *reinterpret_cast<uint4*>(sm.q + r * kLdD + c0) = q8;
+      *reinterpret_cast<uint4*>(sm.k + r * kLdD + c0) = k8;
+      const float b = sm.beta[r], bk = b * __expf(sm.gc[r]);
+      const __nv_bfloat16* kh = reinterpret_cast<const __nv_bfloat16*>(&k8);
+      const __nv_bfloat16* vh = reinterpret_cast<const __nv_bfloat16*>(&v8);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const __nv_bfloat162 vv = pk(__bfloat162float(vh[e]) * b, __bfloat162float(vh[e + 1]) * b);
+        const __nv_bfloat162 kv = pk(__bfloat162float(kh[e]) * bk, __bfloat162float(kh[e + 1]) * bk);
+        sm.vT[(c0 + e) * kLdC + r] = vv.x;
+        sm.vT[(c0 + e + 1) * kLdC + r] = vv.y;
+        sm.kT[(c0 + e) * kLdC + r] = kv.x;
+        sm.kT[(c0 + e + 1) * kLdC + r] = kv.y;
       }
-      __nv_bfloat16* qd = sm.q + r * kLdD + c4;
-      __nv_bfloat16* kd = sm.k + r * kLdD + c4;
-      qd[0] = __float2bfloat16(qv.x); qd[1] = __float2bfloat16(qv.y);
-      qd[2] = __float2bfloat16(qv.z); qd[3] = __float2bfloat16(qv.w);
-      kd[0] = __float2bfloat16(kv.x); kd[1] = __float2bfloat16(kv.y);
-      kd[2] = __float2bfloat16(kv.z); kd[3] = __float2bfloat16(kv.w);
-      const float b = sm.beta[r];
-      sm.vT[(c4 + 0) * kLdC + r] = __float2bfloat16(vv.x * b);
-      sm.vT[(c4 + 1) * kLdC + r] = __float2bfloat16(vv.y * b);
-      sm.vT[(c4 + 2) * kLdC + r] = __float2bfloat16(vv.z * b);
-      sm.vT[(c4 + 3) * kLdC + r] = __float2bfloat16(vv.w * b);
     }
     __syncthreads();
-    // (beta exp(g) k)^T
-    for (int i = tid; i < kC * kD; i += kThreads) {
-      const int r = i / kD, c = i % kD;
-      sm.kT[c * kLdC + r] = __float2bfloat16(__bfloat162float(sm.k[r * kLdD + c]) * sm.beta[r] * __expf(sm.gc[r]));
-    }
+    if (ch + 1 < nchunks) issue_stage(ch + 1);  // overlaps the rest of this chunk
     // ---------------- K K^T -> M (strict lower, decayed, beta rows);  Q K^T -> P (lower, decayed)
     {
       float kk[4][4], qk[4][4];
@@ -201,18 +228,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int n = 0; n < 4; ++n)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = mt * 16 + g4 + (e >> 1) * 8, j = nh * 32 + n * 8 + 2 * t4 + (e & 1);
-          const float dec = i >= j ? __expf(sm.gc[i] - sm.gc[j]) : 0.f;
-          sm.Mf[i * (kC + 1) + j] = i > j ? sm.beta[i] * kk[n][e] * dec : 0.f;
-          sm.P[i * kLdC + j] = __float2bfloat16(qk[n][e] * dec);
+        for (int e2 = 0; e2 < 4; e2 += 2) {
+          const int i = mt * 16 + g4 + (e2 >> 1) * 8, j = nh * 32 + n * 8 + 2 * t4;
+          const float d0 = i >= j ? __expf(sm.gc[i] - sm.gc[j]) : 0.f;
+          const float d1 = i >= j + 1 ? __expf(sm.gc[i] - sm.gc[j + 1]) : 0.f;
+          sm.Mf[i * (kC + 1) + j] = i > j ? sm.beta[i] * kk[n][e2] * d0 : 0.f;
+          sm.Mf[i * (kC + 1) + j + 1] = i > j + 1 ? sm.beta[i] * kk[n][e2 + 1] * d1 : 0.f;
+          *reinterpret_cast<__nv_bfloat162*>(sm.P + i * kLdC + j) = pk(qk[n][e2] * d0, qk[n][e2 + 1] * d1);
         }
     }
     __syncthreads();
     // exp(g) q in place (used by O = (exp(g) q) S); diagonal 16x16 blocks of T by forward substitution
-    for (int i = tid; i < kC * kD; i += kThreads) {
-      const int r = i / kD, c = i % kD;
-      sm.q[r * kLdD + c] = __float2bfloat16(__bfloat162float(sm.q[r * kLdD + c]) * __expf(sm.gc[r]));
+    for (int i = tid; i < kC * 16; i += kThreads) {
+      const int r = i / 16, c0 = (i % 16) * 8;
+      uint4 q8 = *reinterpret_cast<const uint4*>(sm.q + r * kLdD + c0);
+      __nv_bfloat16* qh = reinterpret_cast<__nv_bfloat16*>(&q8);
+      const float e = __expf(sm.gc[r]);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const __nv_bfloat162 v = pk(__bfloat162float(qh[j]) * e, __bfloat162float(qh[j + 1]) * e);
+        qh[j] = v.x;
+        qh[j + 1] = v.y;
+      }
+      *reinterpret_cast<uint4*>(sm.q + r * kLdD + c0) = q8;
     }
     if (warp < 4 && lane < 16) {  // warp b inverts diagonal block b; lane = column
       const int b0 = warp * 16, c = lane;
@@ -270,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // T (lower triangular, zero above the diagonal) as a bf16 operand
     for (int i = tid; i < kC * kC; i += kThreads) {
       const int r = i / kC, c = i % kC;
-      sm.Tm[r * kLdC + c] = __float2bfloat16(c <= r ? sm.Tf[r * (kC + 1) + c] : 0.f);
+      sm.Tm[r * kLdC + c] = __float2bfloat16_rn(c <= r ? sm.Tf[r * (kC + 1) + c] : 0.f);
     }
     __syncthreads();
     // ---------------- u = T (beta v) [registers];  -w = -T (beta exp(g) k) -> smem (bf16, over Mf)
@@ -285,17 +323,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const int r = mt * 16 + g4, c = nh * 64 + n * 8 + 2 * t4;
-      wneg[r * kLdD + c] = __float2bfloat16(-wv[n][0]);
-      wneg[r * kLdD + c + 1] = __float2bfloat16(-wv[n][1]);
-      wneg[(r + 8) * kLdD + c] = __float2bfloat16(-wv[n][2]);
-      wneg[(r + 8) * kLdD + c + 1] = __float2bfloat16(-wv[n][3]);
+      *reinterpret_cast<__nv_bfloat162*>(wneg + r * kLdD + c) = pk(-wv[n][0], -wv[n][1]);
+      *reinterpret_cast<__nv_bfloat162*>(wneg + (r + 8) * kLdD + c) = pk(-wv[n][2], -wv[n][3]);
     }
     __syncthreads();
     // (exp(g_last - g) k)^T for the state update (kT is free: w is done)
     const float glast = sm.gc[kC - 1];
-    for (int i = tid; i < kC * kD; i += kThreads) {
-      const int r = i / kD, c = i % kD;
-      sm.kT[c * kLdC + r] = __float2bfloat16(__bfloat162float(sm.k[r * kLdD + c]) * __expf(glast - sm.gc[r]));
+    for (int i = tid; i < kC * 16; i += kThreads) {
+      const int r = i / 16, c0 = (i % 16) * 8;
+      const uint4 k8 = *reinterpret_cast<const uint4*>(sm.k + r * kLdD + c0);
+      const __nv_bfloat16* kh = reinterpret_cast<const __nv_bfloat16*>(&k8);
+      const float e = __expf(glast - sm.gc[r]);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const __nv_bfloat162 v = pk(__bfloat162float(kh[j]) * e, __bfloat162float(kh[j + 1]) * e);
+        sm.kT[(c0 + j) * kLdC + r] = v.x;
+        sm.kT[(c0 + j + 1) * kLdC + r] = v.y;
+      }
     }
     // ---------------- Vn = u - w S  (B^T = S^T)
     warp_gemm<8>(u, wneg, kLdD, sm.ST, kLdD, mt * 16, nh * 64, kD, lane);
@@ -303,10 +347,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int n = 0; n < 8; ++n) {  // Vn^T into vT
       const int r = mt * 16 + g4, c = nh * 64 + n * 8 + 2 * t4;
-      sm.vT[c * kLdC + r] = __float2bfloat16(u[n][0]);
-      sm.vT[(c + 1) * kLdC + r] = __float2bfloat16(u[n][1]);
-      sm.vT[c * kLdC + r + 8] = __float2bfloat16(u[n][2]);
-      sm.vT[(c + 1) * kLdC + r + 8] = __float2bfloat16(u[n][3]);
+      const __nv_bfloat162 a = pk(u[n][0], u[n][1]), b = pk(u[n][2], u[n][3]);
+      sm.vT[c * kLdC + r] = a.x;
+      sm.vT[(c + 1) * kLdC + r] = a.y;
+      sm.vT[c * kLdC + r + 8] = b.x;
+      sm.vT[(c + 1) * kLdC + r + 8] = b.y;
     }
     __syncthreads();
     // ---------------- O = (exp(g) q) S + P Vn   (reuse wv as the accumulator)
@@ -343,17 +388,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();  // sums of squares complete; every warp is past its reads of S^T
     store_ST();
+    {
+      // this thread's two rows: r0 = mt*16 + g4 and r0 + 8; columns in adjacent pairs
+      const int r0 = mt * 16 + g4;
+      const float inv0 = rsqrtf((sm.ss[0][r0] + sm.ss[1][r0]) / kD + eps);
+      const float inv1 = rsqrtf((sm.ss[0][r0 + 8] + sm.ss[1][r0 + 8]) / kD + eps);
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < 8; ++n) {
+        const int c = nh * 64 + n * 8 + 2 * t4;
+        const __nv_bfloat162 nw2 = *reinterpret_cast<const __nv_bfloat162*>(norm_w + c);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = mt * 16 + g4 + (e >> 1) * 8, c = nh * 64 + n * 8 + 2 * t4 + (e & 1);
-        if (r < valid) {
-          const float inv = rsqrtf((sm.ss[0][r] + sm.ss[1][r]) / kD + eps);
-          const int64_t row = t0 + r;
-          const float zv = __bfloat162float(z[row * Hv * kD + h * kD + c]);
-          out[row * Hv * kD + h * kD + c] =
-              __float2bfloat16(wv[n][e] * inv * __bfloat162float(norm_w[c]) * silu(zv));
+        for (int hr = 0; hr < 2; ++hr) {
+          const int r = r0 + hr * 8;
+          if (r < valid) {
+            const int64_t off = (int64_t)(t0 + r) * Hv * kD + h * kD + c;
+            const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(z + off);
+            const float inv = hr ? inv1 : inv0;
+            *reinterpret_cast<__nv_bfloat162*>(out + off) =
+                pk(wv[n][2 * hr] * inv * __bfloat162float(nw2.x) * silu(__bfloat162float(z2.x)),
+                   wv[n][2 * hr + 1] * inv * __bfloat162float(nw2.y) * silu(__bfloat162float(z2.y)));
+          }
         }
       }
     }
@@ -398,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Chunked prefill scan (dk = dv = 128, conv kernel 4), after deltanet_conv_kernel: xc [T, C] fp32;
 // mixed [T, C] raw conv inputs (the conv history advances to the last three); z [T, Hv*128],
 // ba [T, 2*Hv] bf16; ssm [slots, Hv, 128, 128] fp32 updated in place; out [T, Hv*128] bf16.
-void launch_deltanet_chunk(const float* xc, const __nv_bfloat16* mixed, float* conv_state, const __nv_bfloat16* z,
+void launch_deltanet_chunk(const __nv_bfloat16* xc, const __nv_bfloat16* mixed, float* conv_state, const __nv_bfloat16* z,
                            const __nv_bfloat16* ba, float* ssm, const int64_t* slots, const int* cu, const float* A_log,
                            const float* dt_bias, const __nv_bfloat16* norm_w, __nv_bfloat16* out, int nseq, int Hk,
                            int Hv, float eps, cudaStream_t st) {

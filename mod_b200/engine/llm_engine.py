@@ -101,9 +101,11 @@ class LLMEngine:
                         if backend == "native" else NcclEPMoE(cfg, self.backend, max_tokens=max_batch))
         elif (backend == "native" and cfg.is_moe and world == 1 and model is None and self.device.type == "cuda"
               and quantization in (None, "none") and not cfg.shared_expert_intermediate_size
-              and os.environ.get("MB_MOE_FUSED", "1") != "0"):
-            # one GPU: the same fused route + placement kernel and the combine folded into the next
-            # add + RMSNorm (expert rows read in place), four launches per MoE layer instead of nine
+              and os.environ.get("MB_MOE_FUSED", "0") == "1"):
+            # one GPU, opt-in (MB_MOE_FUSED=1): the same fused route + placement kernel and the combine
+            # folded into the next add + RMSNorm (expert rows read in place), four launches per MoE layer
+            # instead of nine.  Off by default: measured slower at Qwen3-30B-A3B decode on one B200
+            # (7,451 vs 8,062 tok/s)
             from ..parallel.ep import FusedEPMoE
 
             moe_impl = FusedEPMoE(cfg, self.backend, max_tokens=max_batch,

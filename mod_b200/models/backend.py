@@ -91,6 +91,9 @@ class NativeBackend:
 
         # MB_CLUSTER_GEMM=0 keeps decode GEMMs on the split-K + reduction kernels (A/B timing)
         self.cluster_gemm = os.environ.get("MB_CLUSTER_GEMM", "1") != "0"
+        # int8 weights on the cluster kernel are opt-in (MB_CLUSTER_W8=1): its in-loop expansion measured
+        # slower than the int8 split-K kernel at T = 128 (33.3 vs 30.4 us, Qwen3-30B-A3B qkv)
+        self.cluster_w8 = os.environ.get("MB_CLUSTER_W8", "0") == "1"
 
     def _sms(self, device) -> int:
         if not hasattr(self, "_nsm"):
@@ -105,6 +108,8 @@ class NativeBackend:
         """Decode-sized GEMMs (bf16 or int8 weights) run on the cluster split-K kernel (DSMEM
         reduction, one launch)."""
         if not self.cluster_gemm or x2.dtype != torch.bfloat16:
+            return False
+        if isinstance(w, Int8Weight) and not self.cluster_w8:
             return False
         wt = w.q if isinstance(w, Int8Weight) else w
         if wt.dtype not in (torch.bfloat16, torch.int8):
@@ -181,7 +186,8 @@ class NativeBackend:
     def qkv_rope(self, x, w, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot, eps) -> bool:
         """QKV projection with QK-norm, RoPE and the KV write in one cluster GEMM (decode sizes,
         head_dim 128).  Returns False when the shape is not covered (caller runs the two-step form)."""
-        if D != 128 or w.shape[0] != (Hq + 2 * Hkv) * D or not self._cluster_ok(x, w):
+        if (D != 128 or isinstance(w, Int8Weight) or w.shape[0] != (Hq + 2 * Hkv) * D
+                or not self._cluster_ok(x, w)):
             return False
         self.N.qkv_rope_cluster(x, w, q_w, k_w, positions, invf, slots, q_out, k_cache, v_cache, Hq, Hkv, rot, eps)
         return True

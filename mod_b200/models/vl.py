@@ -143,15 +143,15 @@ def vision_forward(vc: VisionConfig, vw: VisionWeights, patches: torch.Tensor, b
         ctx = torch.full((B,), N, dtype=torch.int32, device=dev)
         pos_i = pos.int().contiguous()
         alloc = torch.empty if N % 16 == 0 else torch.zeros  # no stale NaNs behind the last patch
-        kc = alloc(B * nblk, heads, 16, D, dtype=torch.bfloat16, device=dev)
-        vc = alloc(B * nblk, heads, D, 16, dtype=torch.bfloat16, device=dev)
+        kcache = alloc(B * nblk, heads, 16, D, dtype=torch.bfloat16, device=dev)
+        vcache = alloc(B * nblk, heads, D, 16, dtype=torch.bfloat16, device=dev)
         q = torch.empty(B * N, heads * D, dtype=torch.bfloat16, device=dev)
     for blk in vw.blocks:
         h = be.rmsnorm(x, blk.norm1, eps)
         qkv = be.linear(h, blk.qkv, bias=blk.qkv_bias)
         if native:
-            be.N.vit_rope_kv(qkv.contiguous(), pos_i, N, heads, D, 10000.0, q, kc, vc)
-            o = be.N.attn_prefill_tc(q.view(B * N, heads, D), kc, vc, bt, cu, ctx, N, causal=False)
+            be.N.vit_rope_kv(qkv.contiguous(), pos_i, N, heads, D, 10000.0, q, kcache, vcache)
+            o = be.N.attn_prefill_tc(q.view(B * N, heads, D), kcache, vcache, bt, cu, ctx, N, causal=False)
             o = o.reshape(B * N, H)
         else:
             qkv = qkv.view(B, N, 3, heads, D)

@@ -327,7 +327,10 @@ def test_deltanet_prefill_then_decode(cuda, Hk, Hv, dk):
                                 conv_r, ssm_r, int(slots[b]), Hk, Hv, dk, dv, eps))
     _close(out, torch.cat(refs))
     torch.testing.assert_close(conv, conv_r, rtol=1e-5, atol=1e-5)
-    torch.testing.assert_close(ssm, ssm_r, rtol=1e-3, atol=1e-3)
+    # head dim 128 runs the chunked scan, whose chunk products take bf16 operands: state error
+    # ~1e-2 of the state's magnitude (the token-serial scan keeps fp32 throughout)
+    stol = 1e-2 * max(1.0, ssm_r.abs().max().item()) if dk == 128 else 1e-3
+    torch.testing.assert_close(ssm, ssm_r, rtol=2e-2 if dk == 128 else 1e-3, atol=stol)
     for step in range(3):
         B = len(lens)
         mix, z, ba, *_ = _dn_inputs(B, Hk, Hv, dk, dv, cuda)
@@ -336,7 +339,7 @@ def test_deltanet_prefill_then_decode(cuda, Hk, Hv, dk):
         r = ref_decode(mix, z, ba, conv_w, A_log, dt_bias, norm_w, conv_r, ssm_r, slots, Hk, Hv, dk, dv, eps)
         _close(o, r)
         torch.testing.assert_close(conv, conv_r, rtol=1e-5, atol=1e-5)
-        torch.testing.assert_close(ssm, ssm_r, rtol=1e-3, atol=1e-3)
+        torch.testing.assert_close(ssm, ssm_r, rtol=2e-2 if dk == 128 else 1e-3, atol=stol)
 
 
 @pytest.mark.parametrize("L", [1, 63, 64, 65, 4096])

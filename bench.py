@@ -41,6 +41,10 @@ sys.path.insert(0, HERE)
 
 METRIC = "decode tok/s (box, max over ranks) Qwen3-30B-A3B"
 MODEL = "qwen3-30b-a3b"
+# The reference has no runnable GPU path, so the bar is this repository's library-only arm
+# (`--impl baseline`: NCCL all-to-all + cuBLAS / torch grouped GEMMs, CUDA-graph captured), measured
+# on a B200 box with the same command and recorded with its date in the benchmark notes.  None: not measured.
+BASELINE_TOKS = {1: 2783.7, 2: 3166.7, 4: None, 8: None}
 
 
 def parse():
@@ -279,7 +283,9 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(dev_ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random token ids, random-init N(0,0.02) weights, seed 0)",
+            "vs_baseline": (round(value / BASELINE_TOKS.get(world, 0), 3) if args.impl == "native" and
+                            BASELINE_TOKS.get(world) else None),
+            "dtype": "bf16", "data": "synthetic (uniform-random token ids, random-init N(0,0.02) weights, seed 0)",
             "impl": args.impl,
             "config": {"model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt_len,
                        "parallelism": f"ep{world}+dp_attn{world}" if world > 1 else "single",
@@ -299,6 +305,12 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if backend == "torch":
+            # the baseline's captured decode graphs hold NCCL collectives; tearing the process group down
+            # under them has hung at exit, so the baseline ranks leave without the teardown (results are out)
+            torch.cuda.synchronize()
+            sys.stdout.flush()
+            os._exit(0)
         dist.destroy_process_group()
 
 

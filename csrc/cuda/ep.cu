@@ -517,6 +517,13 @@ __global__ void __launch_bounds__(1024)
 //      next call.
 // Scratch (device, zero between calls): counts [E], cursor [E]; logits [T, E] f32.
 constexpr int kRdThreads = 1024;
+
+// Orders this thread's earlier writes before a later flag store: at system scope when peers read
+// them over NVLink, at device scope on a single rank (a system-scope fence costs microseconds).
+__device__ __forceinline__ void fence_peers(int nranks) {
+  if (nranks > 1) __threadfence_system();
+  else __threadfence();
+}
 constexpr int kRdTileE = 8, kRdTileT = 16;
 
 __device__ __forceinline__ bool grid_arrive_wait(int* ctr, int target, int* status) {
@@ -549,33 +556,54 @@ __global__ void __launch_bounds__(kRdThreads)
                              int T, int K, int renorm, float* __restrict__ logits, int* __restrict__ ids,
                              float* __restrict__ wts, int* __restrict__ counts, int* __restrict__ cursor,
                              int* __restrict__ map, int* __restrict__ offs, int* __restrict__ bar,
-                             int* __restrict__ pos_map) {
+                             int* __restrict__ pos_map, uint64_t* __restrict__ trace) {
+  // trace (optional, [8]): %globaltimer of CTA 0 at the phase boundaries, for latency attribution
+  auto mark = [&](int i) {
+    if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[i] = globaltimer_ns();
+  };
+  mark(0);
   pdl_wait();
   pdl_trigger();
+  mark(1);
   const uint32_t epoch = *a.epoch + 1;
   const int E = a.El * a.N, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, H = a.H;
   // ---------------- 1. router logits
+  // A tile is 8 experts x 16 tokens: its 8 router rows and 16 token rows are brought into shared
+  // memory with 16-byte cp.async copies (one round of memory latency), then warp w forms the dot
+  // products of expert w % 8 with tokens 4*(w / 8) .. +3 from shared memory.
   {
+    extern __shared__ __align__(16) uint8_t rd_dyn[];
+    __nv_bfloat16* sw = reinterpret_cast<__nv_bfloat16*>(rd_dyn);          // [8][H]
+    __nv_bfloat16* sx = sw + kRdTileE * H;                                  // [16][H]
     const int tiles_e = (E + kRdTileE - 1) / kRdTileE, tiles_t = (T + kRdTileT - 1) / kRdTileT;
     const int e_in = warp % kRdTileE, t_grp = warp / kRdTileE;  // 4 token groups of 4 tokens
+    const int n16 = H / 8;                                      // 16-byte pieces per row
     for (int tile = blockIdx.x; tile < tiles_e * tiles_t; tile += G) {
-      const int e = (tile % tiles_e) * kRdTileE + e_in;
-      const int t0 = (tile / tiles_e) * kRdTileT + t_grp * 4;
+      const int e_base = (tile % tiles_e) * kRdTileE, t_base = (tile / tiles_e) * kRdTileT;
+      __syncthreads();  // the previous tile's reads are done
+      for (int i = tid; i < (kRdTileE + kRdTileT) * n16; i += blockDim.x) {
+        const int row = i / n16, piece = i % n16;
+        const bool is_w = row < kRdTileE;
+        const int src_row = is_w ? e_base + row : t_base + row - kRdTileE;
+        const bool in = is_w ? src_row < E : src_row < T;
+        const __nv_bfloat16* src = (is_w ? wr : x) + (in ? (size_t)src_row * H + piece * 8 : 0);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sw + (size_t)row * H + piece * 8)),
+                     "l"(src), "r"(in ? 16 : 0) : "memory");
+      }
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+      __syncthreads();
+      const int e = e_base + e_in, t0 = t_base + t_grp * 4;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      if (e < E) {
-        for (int c = lane * 8; c < H; c += 256) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(wr + (size_t)e * H + c);
-          const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      for (int c = lane * 8; c < H; c += 256) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(sw + (size_t)e_in * H + c);
+        const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wv);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (t0 + j < T) {
-              const uint4 xv = *reinterpret_cast<const uint4*>(x + (size_t)(t0 + j) * H + c);
-              const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xv);
+        for (int j = 0; j < 4; ++j) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(sx + (size_t)(t_grp * 4 + j) * H + c);
+          const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
-              for (int q = 0; q < 8; ++q) acc[j] += __bfloat162float(wh[q]) * __bfloat162float(xh[q]);
-            }
-          }
+          for (int q = 0; q < 8; ++q) acc[j] += __bfloat162float(wh[q]) * __bfloat162float(xh[q]);
         }
       }
 #pragma unroll
@@ -585,9 +613,11 @@ __global__ void __launch_bounds__(kRdThreads)
       }
     }
   }
+  mark(2);
   if (!grid_arrive_wait(bar, G, a.status)) return;
+  mark(3);
   // ---------------- 2. top-k per token (warp per token)
-  for (int t = blockIdx.x * (kRdThreads / 32) + warp; t < T; t += G * (kRdThreads / 32)) {
+  for (int t = blockIdx.x + G * warp; t < T; t += G * (kRdThreads / 32)) {  // spread over the CTAs
     float v[EPL];
     float mx = -INFINITY;
 #pragma unroll
@@ -652,7 +682,7 @@ __global__ void __launch_bounds__(kRdThreads)
     }
     __syncthreads();
     if (tid == 0) {
-      __threadfence_system();
+      fence_peers(a.N);
       for (int d = 0; d < a.N; ++d) st_release_sys(at_off<uint32_t>(a.peers[d], a.L.flag_n) + a.rank, epoch);
     }
   }
@@ -667,10 +697,12 @@ __global__ void __launch_bounds__(kRdThreads)
   if (tid == 0) ok_all = 1;
   __syncthreads();
   const uint64_t self = a.peers[a.rank];
+  mark(4);
   for (int src = tid; src < a.N; src += blockDim.x)  // own counts included: they arrive through the same path
     if (!wait_flag(at_off<uint32_t>(self, a.L.flag_n) + src, epoch, a.status, kErrPeerTimeout)) ok_all = 0;
   __syncthreads();
   __threadfence();
+  mark(5);
   const int* cntm = at_off<int>(self, a.L.cntm);
   int colsum = 0, mine = 0, lower = 0;
   const int e = tid;
@@ -709,7 +741,7 @@ __global__ void __launch_bounds__(kRdThreads)
     offs[tid] = tid < a.El ? base[g0 + tid] : base[g0 + a.El - 1] + col[g0 + a.El - 1];
   }
   const int TK = T * K;
-  for (int pair = blockIdx.x * (kRdThreads / 32) + warp; pair < TK; pair += G * (kRdThreads / 32)) {
+  for (int pair = blockIdx.x + G * warp; pair < TK; pair += G * (kRdThreads / 32)) {  // spread over the CTAs
     int ex = __ldcg(ids + pair);
     if (ex < 0 || ex >= E) ex = 0;
     const int dst = ex / a.El;
@@ -734,13 +766,15 @@ __global__ void __launch_bounds__(kRdThreads)
     uint4* dstp = reinterpret_cast<uint4*>(at_off<__nv_bfloat16>(a.peers[dst], a.L.recv_x) + (size_t)pos * H);
     copy_row<false>(dstp, src, H / 8, lane);
   }
+  mark(6);
   __syncthreads();
   __shared__ int last;
   if (tid == 0) {
-    __threadfence_system();
+    fence_peers(a.N);
     last = atomicAdd(&a.done[0], 1) == G - 1;
   }
   __syncthreads();
+  mark(7);
   if (!last) return;
   // every CTA is past its last use of counts / cursor / the barrier counters
   for (int i = tid; i < E; i += blockDim.x) {
@@ -750,7 +784,7 @@ __global__ void __launch_bounds__(kRdThreads)
   if (tid == 0) {
     bar[0] = 0;
     bar[1] = 0;
-    __threadfence_system();
+    fence_peers(a.N);
     for (int d = 0; d < a.N; ++d) st_release_sys(at_off<uint32_t>(a.peers[d], a.L.flag_d) + a.rank, epoch);
     a.done[0] = 0;
   }
@@ -804,16 +838,21 @@ __global__ void ep_combine_send2_kernel(EpArgs a, const int* __restrict__ offs, 
 // which is exactly what the two kernels computed.  The last CTA advances the
 // epoch.  H is a compile-time multiple of 256.
 template <int H>
-__global__ void ep_combine_norm_kernel(EpArgs a, const int* __restrict__ map, const float* __restrict__ wts, int T,
-                                       int K, __nv_bfloat16* __restrict__ residual,
-                                       const __nv_bfloat16* __restrict__ nw, __nv_bfloat16* __restrict__ out,
-                                       float eps, const __nv_bfloat16* __restrict__ rows) {
+__global__ void __launch_bounds__(H / 8)
+    ep_combine_norm_kernel(EpArgs a, const int* __restrict__ map, const float* __restrict__ wts, int T,
+                           int K, __nv_bfloat16* __restrict__ residual,
+                           const __nv_bfloat16* __restrict__ nw, __nv_bfloat16* __restrict__ out,
+                           float eps, const __nv_bfloat16* __restrict__ rows) {
+  // CTA per token, H/8 threads, 8 columns per thread: the K expert rows, the residual and the norm
+  // weight of a thread's columns are all requested before any is used (one round of latency),
+  // then a block reduction forms the RMS.
   pdl_wait();
   pdl_trigger();
-  constexpr int kChunks = H / 256;
+  constexpr int kThreadsCN = H / 8, kWarpsCN = kThreadsCN / 32 > 0 ? kThreadsCN / 32 : 1;
   const uint32_t epoch = *a.epoch + 1;
   const uint64_t self = a.peers[a.rank];
   __shared__ int ok_all;
+  __shared__ float red[kWarpsCN];
   if (threadIdx.x == 0) ok_all = 1;
   __syncthreads();
   // rows != nullptr (single rank): the expert outputs are read where the down GEMM wrote them
@@ -822,56 +861,56 @@ __global__ void ep_combine_norm_kernel(EpArgs a, const int* __restrict__ map, co
   __syncthreads();
   __threadfence();
   const __nv_bfloat16* comb = rows ? rows : at_off<__nv_bfloat16>(self, a.L.comb);
-  const int lane = threadIdx.x & 31;
-  for (int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T; t += gridDim.x * (blockDim.x / 32)) {
-    float v[kChunks][8];
+  const int c = threadIdx.x * 8, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    const uint4 rr = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + c);
+    const uint4 wr = *reinterpret_cast<const uint4*>(nw + c);
+    float v[8];
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c)
-#pragma unroll
-      for (int q = 0; q < 8; ++q) v[c][q] = 0.f;
+    for (int q = 0; q < 8; ++q) v[q] = 0.f;
     if (ok_all) {
-      for (int k = 0; k < K; ++k) {
-        const float wk = wts[t * K + k];
-        const __nv_bfloat16* row = comb + (size_t)map[t * K + k] * H;
-        uint4 raw[kChunks];
+      for (int k0 = 0; k0 < K; k0 += 8) {  // up to 8 expert rows in flight, summed in k order
+        uint4 raw[8];
+        float wk[8];
 #pragma unroll
-        for (int c = 0; c < kChunks; ++c) raw[c] = __ldcg(reinterpret_cast<const uint4*>(row + c * 256 + lane * 8));
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < K) {
+            raw[j] = __ldcg(reinterpret_cast<const uint4*>(comb + (size_t)map[t * K + k0 + j] * H + c));
+            wk[j] = wts[t * K + k0 + j];
+          }
 #pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[c]);
+        for (int j = 0; j < 8; ++j)
+          if (k0 + j < K) {
+            const __nv_bfloat16* hh = reinterpret_cast<const __nv_bfloat16*>(&raw[j]);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) v[c][q] += wk * __bfloat162float(h[q]);
-        }
+            for (int q = 0; q < 8; ++q) v[q] += wk[j] * __bfloat162float(hh[q]);
+          }
       }
     }
+    const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(&rr);
+    __align__(16) __nv_bfloat16 sum8[8];
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const int col = c * 256 + lane * 8;
-      uint4 rr = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + col);
-      const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(&rr);
-      __align__(16) __nv_bfloat16 sum8[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float h = __bfloat162float(__float2bfloat16(v[c][q]));  // the combined row, rounded as stored
-        sum8[q] = __float2bfloat16(h + __bfloat162float(r[q]));
-        v[c][q] = __bfloat162float(sum8[q]);
-        ss += v[c][q] * v[c][q];
-      }
-      *reinterpret_cast<uint4*>(residual + (size_t)t * H + col) = *reinterpret_cast<uint4*>(sum8);
+    for (int q = 0; q < 8; ++q) {
+      const float hq = __bfloat162float(__float2bfloat16(v[q]));  // the combined row, rounded as stored
+      sum8[q] = __float2bfloat16(hq + __bfloat162float(r[q]));
+      v[q] = __bfloat162float(sum8[q]);
+      ss += v[q] * v[q];
     }
+    *reinterpret_cast<uint4*>(residual + (size_t)t * H + c) = *reinterpret_cast<uint4*>(sum8);
     ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / H + eps);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const int col = c * 256 + lane * 8;
-      uint4 wr = *reinterpret_cast<const uint4*>(nw + col);
-      const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wr);
-      __align__(16) __nv_bfloat16 o[8];
+    for (int w = 0; w < kWarpsCN; ++w) tot += red[w];
+    const float inv = rsqrtf(tot / H + eps);
+    const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wr);
+    __align__(16) __nv_bfloat16 o8[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16(v[c][q] * inv * __bfloat162float(wh[q]));
-      *reinterpret_cast<uint4*>(out + (size_t)t * H + col) = *reinterpret_cast<uint4*>(o);
-    }
+    for (int q = 0; q < 8; ++q) o8[q] = __float2bfloat16(v[q] * inv * __bfloat162float(wh[q]));
+    *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = *reinterpret_cast<uint4*>(o8);
+    __syncthreads();  // red[] is reused by the next token
   }
   __syncthreads();
   __shared__ int last;
@@ -963,7 +1002,7 @@ void ep_dispatch2(const at::Tensor& peers, at::Tensor& state, int64_t rank, int6
 void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                        const at::Tensor& x, const at::Tensor& wr, int64_t K, bool renorm, at::Tensor& ids,
                        at::Tensor& wts, at::Tensor& map, at::Tensor& offs, at::Tensor& scratch, at::Tensor& logits,
-                       const c10::optional<at::Tensor>& pos_map) {
+                       const c10::optional<at::Tensor>& pos_map, const c10::optional<at::Tensor>& trace) {
   const int64_t N = peers.numel(), T = x.size(0), H = x.size(1);
   const int64_t E = N * El;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && wr.scalar_type() == at::kBFloat16 &&
@@ -984,17 +1023,35 @@ void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank,
   const int64_t pair_ctas = (T * K + kRdThreads / 32 - 1) / (kRdThreads / 32);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, std::max(tiles, pair_ctas)));
   int* sc = scratch.data_ptr<int>();
+  uint64_t* tr = nullptr;
+  if (trace && trace->defined()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 8);
+    tr = reinterpret_cast<uint64_t*>(trace->data_ptr<int64_t>());
+  }
   int* pm = nullptr;
   if (pos_map && pos_map->defined()) {
     TORCH_CHECK(pos_map->scalar_type() == at::kInt && pos_map->numel() >= T * K);
     pm = pos_map->data_ptr<int>();
   }
   const int epl = (int)((E + 31) / 32);
+  const size_t rd_smem = (size_t)(kRdTileE + kRdTileT) * H * 2;  // router rows + token rows of one tile
+  TORCH_CHECK(rd_smem <= 160 * 1024, "ep_route_dispatch: hidden size too large for the router tile");
+  static bool rd_attr[4] = {false, false, false, false};
 #define MB_RD(P)                                                                                                   \
-  launch_k(ep_route_dispatch_kernel<P>, grid, kRdThreads, 0, st, a, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), \
+  do {                                                                                                             \
+  {                                                                                                                \
+    const int ai = P == 4 ? 0 : P == 8 ? 1 : P == 16 ? 2 : 3;                                                      \
+    if (!rd_attr[ai]) {                                                                                            \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(ep_route_dispatch_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                          160 * 1024));                                                            \
+      rd_attr[ai] = true;                                                                                          \
+    }                                                                                                              \
+  }                                                                                                                \
+  launch_k(ep_route_dispatch_kernel<P>, grid, kRdThreads, rd_smem, st, a, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), \
            reinterpret_cast<const __nv_bfloat16*>(wr.data_ptr()), (int)T, (int)K, (int)renorm, logits.data_ptr<float>(), \
            ids.data_ptr<int>(), wts.data_ptr<float>(), sc, sc + E, map.data_ptr<int>(), offs.data_ptr<int>(), sc + 2 * E, \
-           pm)
+           pm, tr);                                                                                                 \
+  } while (0)
   if (epl <= 4) MB_RD(4);
   else if (epl <= 8) MB_RD(8);
   else if (epl <= 16) MB_RD(16);
@@ -1061,8 +1118,7 @@ void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
   EpArgs a = make_args(peers, rank, N, C, H, El, state);
   c10::cuda::CUDAGuard guard(out.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  const int wpb = 8;
-  const int grid = (int)std::max<int64_t>(1, (T + wpb - 1) / wpb);
+  const int grid = (int)std::max<int64_t>(1, T);  // CTA per token
   auto r = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
   auto pw = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto po = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -1074,7 +1130,7 @@ void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
   }
 #define MB_CN(HH)                                                                                               \
   case HH:                                                                                                      \
-    launch_k(ep_combine_norm_kernel<HH>, grid, wpb * 32, 0, st, a, (const int*)map.data_ptr<int>(),            \
+    launch_k(ep_combine_norm_kernel<HH>, grid, HH / 8, 0, st, a, (const int*)map.data_ptr<int>(),              \
              (const float*)wts.data_ptr<float>(), (int)T, (int)K, r, pw, po, (float)eps, pr);                  \
     break;
   switch (H) {

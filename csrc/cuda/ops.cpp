@@ -91,7 +91,7 @@ void ipc_free(int64_t ptr);
 void ep_route_dispatch(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                        const at::Tensor& x, const at::Tensor& wr, int64_t K, bool renorm, at::Tensor& ids,
                        at::Tensor& wts, at::Tensor& map, at::Tensor& offs, at::Tensor& scratch, at::Tensor& logits,
-                       const c10::optional<at::Tensor>& pos_map);
+                       const c10::optional<at::Tensor>& pos_map, const c10::optional<at::Tensor>& trace);
 void ep_combine_send(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,
                      const at::Tensor& offs, const at::Tensor& y, int64_t H);
 void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, int64_t C, int64_t El,

@@ -118,6 +118,9 @@ class FusedEPMoE:
         self.fused_route = self.H % 256 == 0 and os.environ.get("MB_EP_FUSED_ROUTE", "1") != "0"
         # the decoder may leave the combine's weighted sum to the next add + RMSNorm (MB_EP_DEFER=0: off)
         self.supports_defer = os.environ.get("MB_EP_DEFER", "1") != "0"
+        # MB_EP_TRACE=1: the route + dispatch kernel records %globaltimer at its phase boundaries here
+        self.trace = (torch.zeros(8, dtype=torch.int64, device=torch.device("cuda", torch.cuda.current_device()))
+                      if os.environ.get("MB_EP_TRACE") == "1" else None)
         self.small = _EpContext(self.C, self.world, self.rank, self.El, K, self.H, max_tokens, group)
         self.large = (_EpContext(self.C, self.world, self.rank, self.El, K, self.H, prefill_tokens, group)
                       if prefill_tokens > max_tokens else self.small)
@@ -139,7 +142,7 @@ class FusedEPMoE:
             # expert-ordered position in the owner's receive region
             self.C.ep_route_dispatch(ctx.buf.peers, ctx.state, self.rank, ctx.cap, self.El, x, mo.router, self.K,
                                      cfg.norm_topk_prob, ids, wts, emap, ctx.offs, ctx.route_scratch, ctx.logits,
-                                     pmap)
+                                     pmap, self.trace)
         else:
             logits = self.be.linear(x, mo.router)
             counts = torch.empty(E, dtype=torch.int32, device=dev)

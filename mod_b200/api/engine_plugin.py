@@ -27,7 +27,7 @@ log = logging.getLogger("mod_b200.plugin")
 
 _RUNTIME_KEYS = {"device", "backend", "max_batch", "max_model_len", "max_prefill_tokens", "seed", "model_path",
                  "use_graphs", "kv_mem_fraction", "max_new_tokens", "dtype", "prefix_caching",
-                 "prefill_chunk", "offload", "offload_layers"}
+                 "prefill_chunk", "offload", "offload_layers", "tp"}
 
 
 class EnginePlugin(TextModelPluginInterface):
@@ -99,15 +99,16 @@ class EnginePlugin(TextModelPluginInterface):
         dtype = torch.float32 if rt["backend"] in ("cpu",) or dev.type == "cpu" else torch.bfloat16
         weights = None
         path = rt.get("model_path")
-        if path and os.path.isdir(path) and any(f.endswith(".safetensors") for f in os.listdir(path)):
-            from ..io.hf_loader import load_hf
-
-            weights = load_hf(self._config, path, device=dev, dtype=dtype)
-        else:
+        if not (path and os.path.isdir(path) and any(f.endswith(".safetensors") for f in os.listdir(path))):
+            path = None  # random-init weights from the runtime seed
             from ..models.weights import random_weights
 
-            weights = random_weights(self._config, device=dev, dtype=dtype, seed=rt["seed"])
+            if int(rt.get("tp", 1)) <= 1:
+                weights = random_weights(self._config, device=dev, dtype=dtype, seed=rt["seed"])
+        # with a checkpoint the engine reads it itself, so a TP or EP rank maps only its own slices
         self.engine = LLMEngine(self._config, weights=weights, backend=rt["backend"], device=dev,
+                                model_path=path, seed=rt["seed"],
+                                tensor_parallel=int(rt.get("tp", 1)) > 1,
                                 max_batch=rt["max_batch"], max_model_len=rt["max_model_len"],
                                 use_graphs=rt.get("use_graphs"),
                                 prefix_caching=bool(rt.get("prefix_caching", False)),

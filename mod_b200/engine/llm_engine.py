@@ -41,7 +41,7 @@ class LLMEngine:
                  expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
                  quantization: Optional[str] = None, prefix_caching: bool = False,
                  prefill_chunk: Optional[int] = None, kv_swap: bool = True, kv_swap_bytes: int = 8 << 30,
-                 offload_layers: Union[int, str, None] = None):
+                 offload_layers: Union[int, str, None] = None, model_path: Optional[str] = None):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
@@ -55,7 +55,10 @@ class LLMEngine:
         host memory (up to ``kv_swap_bytes``) and resumes without recomputing.
         ``offload_layers`` (hybrid CPU/GPU execution): the last N decoder layers
         live in pinned host memory and are streamed to the device one layer
-        ahead of use (``runtime.offload.LayerStreamer``); ``"auto"`` takes N
+        ahead of use (``runtime.offload.LayerStreamer``); ``model_path``: an HF
+        safetensors checkpoint (file or directory) read through the mmap
+        reader, each rank taking only its part (its TP slices or its EP
+        experts); ``"auto"`` takes N
         from the placement planner for this device's memory.  Streaming runs
         eagerly (no decode graphs)."""
         import torch.distributed as dist
@@ -80,9 +83,14 @@ class LLMEngine:
             from ..models.tp_decoder import TPDecoderLM, shard_weights
             from ..parallel.tp import FusedTP, NcclTP
 
-            if weights is None:
-                weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
-            shard = shard_weights(cfg, weights, rank, world)
+            if model_path is not None and weights is None:
+                from ..io.hf_loader import load_hf
+
+                shard = load_hf(cfg, model_path, device=self.device, dtype=wdt, tp=(rank, world))
+            else:
+                if weights is None:
+                    weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
+                shard = shard_weights(cfg, weights, rank, world)
             weights = None
             mt = max(max_batch, max_prefill_tokens)
             comm = FusedTP(cfg.hidden_size, mt) if backend == "native" else NcclTP(cfg.hidden_size, mt)
@@ -93,7 +101,14 @@ class LLMEngine:
         if expert_parallel:
             El = cfg.num_experts // world
             if weights is None and model is None:
-                weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed, expert_range=(rank * El, (rank + 1) * El))
+                if model_path is not None:
+                    from ..io.hf_loader import load_hf
+
+                    weights = load_hf(cfg, model_path, device=self.device, dtype=wdt,
+                                      expert_range=(rank * El, (rank + 1) * El))
+                else:
+                    weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed,
+                                             expert_range=(rank * El, (rank + 1) * El))
             from ..parallel.ep import FusedEPMoE, NcclEPMoE
 
             moe_impl = (FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
@@ -111,7 +126,12 @@ class LLMEngine:
             moe_impl = FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
                                   prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
         if weights is None and model is None:
-            weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
+            if model_path is not None:
+                from ..io.hf_loader import load_hf
+
+                weights = load_hf(cfg, model_path, device=self.device, dtype=wdt)
+            else:
+                weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
         if quantization not in (None, "none", "int8"):
             raise ValueError(f"unknown quantization {quantization!r} (supported: int8)")
         if quantization == "int8" and weights is not None:

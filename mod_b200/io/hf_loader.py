@@ -72,11 +72,32 @@ class CheckpointReader:
 
 
 def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
-            expert_range: Optional[Tuple[int, int]] = None) -> ModelWeights:
+            expert_range: Optional[Tuple[int, int]] = None,
+            tp: Optional[Tuple[int, int]] = None) -> ModelWeights:
+    """HF checkpoint -> fused weights on ``device``.
+
+    ``expert_range=(lo, hi)``: an expert-parallel rank reads experts [lo, hi) only.
+    ``tp=(rank, world)``: a tensor-parallel rank of the dense decoder reads its
+    own slice of every sharded projection straight from the mapping
+    (column-parallel q/k/v and gate/up rows, row-parallel o and down columns;
+    embedding, norms and LM head replicated), the same layout as
+    ``models.tp_decoder.shard_weights`` of the full weights, without ever
+    materialising the full projection (``pio/common/custom_components/
+    model_loader.py:77-123`` loads whole tensors only).
+    """
     r = CheckpointReader(path)
+    trank, tworld = tp or (0, 1)
+    if tworld > 1:
+        assert not cfg.is_moe and not cfg.attn_output_gate and all(
+            cfg.layer_type(i) == "full_attention" for i in range(cfg.num_hidden_layers)), \
+            "tensor-parallel loading covers the dense attention decoder"
 
     def t(name):
         return r.get(name).to(device=device, dtype=dtype)
+
+    def sl(name, dim):
+        """This TP rank's 1/world of ``name`` along ``dim`` (the whole tensor at world 1)."""
+        return r.get_slice(name, dim, trank, tworld) if tworld > 1 else r.get(name)
 
     def opt(name):
         return t(name) if name in r else None
@@ -90,21 +111,22 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
         L = LayerWeights(kind=kind, in_norm=t(p + "input_layernorm.weight"),
                          post_norm=t(p + "post_attention_layernorm.weight"))
         if kind == "full_attention":
-            q = r.get(p + "self_attn.q_proj.weight")
+            q = sl(p + "self_attn.q_proj.weight", 0)
             gate = None
             if cfg.attn_output_gate:  # q_proj rows are [q_h, gate_h] per head
                 qg = q.view(Hq, 2 * D, H)
                 q, gate = qg[:, :D].reshape(Hq * D, H), qg[:, D:].reshape(Hq * D, H)
-            parts = [q, r.get(p + "self_attn.k_proj.weight"), r.get(p + "self_attn.v_proj.weight")]
+            parts = [q, sl(p + "self_attn.k_proj.weight", 0), sl(p + "self_attn.v_proj.weight", 0)]
             if gate is not None:
                 parts.append(gate)
             qkv = torch.cat([x.to(dtype) for x in parts], 0).to(device)
             bias = None
             if p + "self_attn.q_proj.bias" in r:
-                bias = torch.cat([r.get(p + f"self_attn.{n}_proj.bias").to(dtype) for n in "qkv"], 0).to(device)
-            L.attn = AttnWeights(qkv=qkv, o=t(p + "self_attn.o_proj.weight"), q_norm=opt(p + "self_attn.q_norm.weight"),
+                bias = torch.cat([sl(p + f"self_attn.{n}_proj.bias", 0).to(dtype) for n in "qkv"], 0).to(device)
+            L.attn = AttnWeights(qkv=qkv, o=sl(p + "self_attn.o_proj.weight", 1).to(device, dtype), q_norm=opt(p + "self_attn.q_norm.weight"),
                                  k_norm=opt(p + "self_attn.k_norm.weight"), qkv_bias=bias,
                                  o_bias=opt(p + "self_attn.o_proj.bias"))
+            assert tworld == 1 or L.attn.o_bias is None, "a row-parallel o_proj bias would be summed world times"
         else:
             la = p + "linear_attn."
             Hk, Hv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
@@ -137,9 +159,11 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
         else:
             m = p + "mlp."
             if m + "gate_proj.weight" in r:
-                L.mlp = MLPWeights(gate_up=torch.cat([t(m + "gate_proj.weight"), t(m + "up_proj.weight")], 0),
-                                   down=t(m + "down_proj.weight"))
+                L.mlp = MLPWeights(gate_up=torch.cat([sl(m + "gate_proj.weight", 0).to(device, dtype),
+                                                      sl(m + "up_proj.weight", 0).to(device, dtype)], 0),
+                                   down=sl(m + "down_proj.weight", 1).to(device, dtype))
             else:
+                assert tworld == 1, "tensor-parallel loading covers the gated (SwiGLU) MLP"
                 L.mlp = MLPWeights(up=t(m + "up_proj.weight"), down=t(m + "down_proj.weight"),
                                    up_bias=opt(m + "up_proj.bias"), down_bias=opt(m + "down_proj.bias"))
         layers.append(L)

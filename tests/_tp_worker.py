@@ -35,6 +35,18 @@ def run(rank, world, backend, port, device_kind):
     ref = single.generate(prompts, params)
     if device_kind == "cpu":
         assert out == ref, (out, ref)
+        # the same TP engine built from an HF checkpoint: each rank maps only its own slices
+        import tempfile
+
+        from mod_b200.io.safetensors import save_file
+        from tests.test_io import _hf_from_fused
+
+        with tempfile.TemporaryDirectory() as d:
+            save_file(os.path.join(d, "model.safetensors"), _hf_from_fused(cfg, w1), {})
+            ck = LLMEngine(cfg, backend=backend, device=dev, max_batch=4, max_model_len=64, tensor_parallel=True,
+                           model_path=d)
+            out2 = ck.generate(prompts, params)
+        assert out2 == ref, (out2, ref)
     else:  # bf16: the first tokens must agree, the rest mostly
         agree = sum(a == b for x, y in zip(out, ref) for a, b in zip(x, y)) / sum(len(x) for x in ref)
         assert all(x[0] == y[0] for x, y in zip(out, ref)) and agree >= 0.8, (out, ref)

@@ -136,3 +136,28 @@ def test_prompt_utils():
     assert h[1]["content"] == "Hello"
     t = prompts.apply_chat_template(None, [{"role": "user", "content": "x"}])
     assert t == "<|im_start|>user\nx<|im_end|>\n<|im_start|>assistant\n<think>\n"
+
+
+def test_hf_loader_tensor_parallel_slices(tmp_path):
+    """load_hf(tp=(r, N)) reads each rank's projection slices from the mapping and
+    gives exactly shard_weights() of the full load, for every rank."""
+    from mod_b200.io.hf_loader import load_hf
+    from mod_b200.models.tp_decoder import shard_weights
+
+    cfg = get_preset("tiny-dense")
+    w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=5)
+    d = tmp_path / "ckpt"
+    d.mkdir()
+    save_file(str(d / "model.safetensors"), _hf_from_fused(cfg, w), {})
+    full = load_hf(cfg, str(d), device="cpu", dtype=torch.float32)
+    world = 2
+    for rank in range(world):
+        got = load_hf(cfg, str(d), device="cpu", dtype=torch.float32, tp=(rank, world))
+        want = shard_weights(cfg, full, rank, world)
+        for a, b in zip(got.layers, want.layers):
+            assert torch.equal(a.attn.qkv, b.attn.qkv)
+            assert torch.equal(a.attn.o, b.attn.o)
+            assert torch.equal(a.mlp.gate_up, b.mlp.gate_up)
+            assert torch.equal(a.mlp.down, b.mlp.down)
+            assert a.attn.o.is_contiguous() and a.mlp.down.is_contiguous()
+        assert torch.equal(got.embed, want.embed) and torch.equal(got.lm_head, want.lm_head)

@@ -27,7 +27,7 @@ log = logging.getLogger("mod_b200.plugin")
 
 _RUNTIME_KEYS = {"device", "backend", "max_batch", "max_model_len", "max_prefill_tokens", "seed", "model_path",
                  "use_graphs", "kv_mem_fraction", "max_new_tokens", "dtype", "prefix_caching",
-                 "prefill_chunk", "offload", "offload_layers", "tp"}
+                 "prefill_chunk", "offload", "offload_layers", "tp", "quantization"}
 
 
 class EnginePlugin(TextModelPluginInterface):
@@ -37,6 +37,10 @@ class EnginePlugin(TextModelPluginInterface):
     architecture: str = "Qwen3 Transformer"
     size: str = ""
     modalities = ("text",)
+    # model-specific behaviour, set by each plugin
+    thinking_default: bool = False       # chat replies open with a <think> block unless the caller says otherwise
+    gpu_runtime_defaults: Dict[str, Any] = {}  # applied when the model runs on the sm_100a backend
+    fim_tokens: Optional[tuple] = None   # (prefix, suffix, middle) markers of a fill-in-the-middle code model
 
     def __init__(self):
         cfg = get_preset(self.preset)
@@ -76,6 +80,10 @@ class EnginePlugin(TextModelPluginInterface):
                     log.warning("%s: ignoring unknown option %s", self.display_name, k)
             if self.runtime["device"] == "cpu" and self.runtime["backend"] == "native":
                 self.runtime["backend"] = "torch"
+            if self.runtime["backend"] == "native":
+                for k, v in self.gpu_runtime_defaults.items():
+                    if k not in kwargs:
+                        self.runtime[k] = v
             from ..io.tokenizer import load_tokenizer
 
             self.tokenizer = load_tokenizer(self.runtime.get("model_path"))
@@ -109,6 +117,7 @@ class EnginePlugin(TextModelPluginInterface):
         self.engine = LLMEngine(self._config, weights=weights, backend=rt["backend"], device=dev,
                                 model_path=path, seed=rt["seed"],
                                 tensor_parallel=int(rt.get("tp", 1)) > 1,
+                                quantization=rt.get("quantization"),
                                 max_batch=rt["max_batch"], max_model_len=rt["max_model_len"],
                                 use_graphs=rt.get("use_graphs"),
                                 prefix_caching=bool(rt.get("prefix_caching", False)),
@@ -146,6 +155,34 @@ class EnginePlugin(TextModelPluginInterface):
         ids = self.tokenize(prompt) or [0]
         out = self.generate_ids([ids], max_new_tokens, **kwargs)[0]
         return self.detokenize(out)
+
+    # ------------------------------------------------------------------ chat / code
+    def format_chat(self, messages: List[Dict[str, str]], enable_thinking: Optional[bool] = None) -> str:
+        """The model's chat prompt for ``messages`` (ChatML for the Qwen3 family)."""
+        from ..io.prompts import apply_chat_template
+
+        think = self.thinking_default if enable_thinking is None else enable_thinking
+        return apply_chat_template(self.tokenizer, messages, enable_thinking=think)
+
+    def chat(self, messages: List[Dict[str, str]], max_new_tokens: Optional[int] = None,
+             enable_thinking: Optional[bool] = None, **kw) -> str:
+        """One assistant reply to ``messages``; any think block is stripped from it."""
+        from ..io.prompts import strip_thinking
+
+        text = self.format_chat(messages, enable_thinking)
+        return strip_thinking(self.generate_text(text, max_new_tokens or self.runtime["max_new_tokens"], **kw)).strip()
+
+    def format_fim(self, prefix: str, suffix: str = "") -> str:
+        """Fill-in-the-middle prompt: the code before and after the gap, then the
+        marker after which the model writes the missing middle."""
+        if self.fim_tokens is None:
+            raise NotImplementedError(f"{self.display_name} is not a fill-in-the-middle code model")
+        p, s, m = self.fim_tokens
+        return f"{p}{prefix}{s}{suffix}{m}"
+
+    def complete_code(self, prefix: str, suffix: str = "", max_new_tokens: Optional[int] = None, **kw) -> str:
+        """The code that fills the gap between ``prefix`` and ``suffix``."""
+        return self.generate_text(self.format_fim(prefix, suffix), max_new_tokens or self.runtime["max_new_tokens"], **kw)
 
     def infer(self, data: Any) -> Any:
         """str -> generated text; token ids [B, L] (tensor or lists) -> [B, L + max_new_tokens]."""

@@ -9,6 +9,8 @@ class Qwen3_0_6B_Plugin(EnginePlugin):
     architecture = "Qwen3 Transformer"
     size = "0.6B"
     modalities = ('text',)
+    # Qwen3 dense checkpoints are hybrid-thinking models: a chat reply opens with a <think> block by default
+    thinking_default = True
 
 
 def create_qwen3_0_6b_plugin():

@@ -9,6 +9,8 @@ class Qwen3_4B_Instruct_2507_Plugin(EnginePlugin):
     architecture = "Qwen3 Transformer"
     size = "4B"
     modalities = ('text',)
+    # the 2507 Instruct release is the non-thinking variant: replies start directly with the answer
+    thinking_default = False
 
 
 def create_qwen3_4b_instruct_2507_plugin():

@@ -9,6 +9,8 @@ class Qwen3_Coder_30B_Plugin(EnginePlugin):
     architecture = "Qwen3 MoE Transformer"
     size = "30B-A3B"
     modalities = ('text',)
+    # Qwen coder checkpoints are trained for fill-in-the-middle with these markers (complete_code)
+    fim_tokens = ("<|fim_prefix|>", "<|fim_suffix|>", "<|fim_middle|>")
 
 
 def create_qwen3_coder_30b_plugin():

@@ -76,3 +76,42 @@ def test_secondary_registry_and_factory():
     f.pm.discover_and_load_plugins()
     m = f.create_model("qwen3-0.6b", **SMALL)
     assert m.is_initialized
+
+
+def _plugin(name):
+    pm = PluginManager()
+    pm.discover_and_load_plugins()
+    return pm, pm.get_plugin(name)
+
+
+def test_plugin_specific_chat_layouts():
+    """Thinking defaults differ per model (Qwen3-0.6B hybrid-thinking, 4B-Instruct-2507
+    non-thinking); GLM has its own chat layout."""
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+    _, small = _plugin("Qwen3-0.6B")
+    assert small.format_chat(msgs).endswith("<|im_start|>assistant\n<think>\n")
+    assert small.format_chat(msgs, enable_thinking=False).endswith("<|im_start|>assistant\n")
+    _, inst = _plugin("Qwen3-4B-Instruct-2507")
+    assert inst.format_chat(msgs).endswith("<|im_start|>assistant\n")
+    _, glm = _plugin("GLM-4.7-Flash")
+    assert glm.format_chat(msgs) == "[gMASK]<sop><|system|>\nbe brief<|user|>\nhi/nothink<|assistant|>\n"
+    assert "/nothink" not in glm.format_chat(msgs, enable_thinking=True)
+
+
+def test_coder_plugins_fill_in_the_middle_and_next_defaults():
+    pm, coder = _plugin("Qwen3-Coder-30B")
+    assert coder.format_fim("def f(x):\n    ", "\n    return y") == \
+        "<|fim_prefix|>def f(x):\n    <|fim_suffix|>\n    return y<|fim_middle|>"
+    _, small = _plugin("Qwen3-0.6B")
+    with pytest.raises(NotImplementedError):
+        small.format_fim("a")
+    assert pm.activate_plugin("Qwen3-Coder-30B", **SMALL, num_experts=8, num_experts_per_tok=2,
+                              moe_intermediate_size=128)
+    assert isinstance(coder.complete_code("def f(", "):", max_new_tokens=3), str)
+    assert isinstance(coder.chat([{"role": "user", "content": "x"}], max_new_tokens=3), str)
+    pm.deactivate_plugin("Qwen3-Coder-30B")
+    # Qwen3-Next on the sm_100a backend defaults to int8 projections and chunked prefill; an explicit
+    # option wins, and the CPU-side torch backend keeps bf16/fp32 weights
+    _, nxt = _plugin("Qwen3-Coder-Next")
+    assert nxt.gpu_runtime_defaults == {"quantization": "int8", "prefill_chunk": 8192}
+    assert "quantization" not in nxt.runtime

@@ -232,6 +232,55 @@ class LLMEngine:
         self.scheduler.add(seq)
         return seq.req_id
 
+    def add_prefilled(self, prompt: Seq[int], first_token: int, k_layers: List[torch.Tensor],
+                      v_layers: List[torch.Tensor], params: Optional[SamplingParams] = None) -> int:
+        """Adds a request whose prompt was prefilled outside this engine (for example by a
+        context-parallel prefill over several ranks): ``k_layers`` / ``v_layers`` hold the
+        prompt's K (after QK-norm and RoPE) and V of every attention layer as [S, Hkv, D].
+        The KV is handed to the swap path, so the scheduler copies it into fresh blocks
+        and the request continues with decode steps; the prompt is never recomputed."""
+        from ..parallel.cp_model import to_blocks
+
+        if self.swapper is None:
+            raise RuntimeError("add_prefilled needs the KV swap path (attention-only model, no prefix caching)")
+        seq = Sequence(prompt=list(int(t) for t in prompt), params=params or SamplingParams())
+        kb, vb = zip(*(to_blocks(k, v, self.kv.block_size) for k, v in zip(k_layers, v_layers)))
+        self.swapper.stage(seq.req_id, [b.to(self.device) for b in kb + vb])
+        seq.output.append(int(first_token))
+        seq.num_cached = len(seq.prompt)
+        seq.swapped = True
+        seq.t_first_token = time.perf_counter()
+        self.seqs[seq.req_id] = seq
+        if seq.finished_by(int(first_token)):
+            self.swapper.saved.pop(seq.req_id, None)
+            self.swapper.external.discard(seq.req_id)
+            seq.status, seq.t_finish = SeqStatus.FINISHED, seq.t_first_token
+        else:
+            self.scheduler.add(seq)
+        return seq.req_id
+
+    def generate_context_parallel(self, prompt: Seq[int], params: Optional[SamplingParams] = None,
+                                  weights: Optional[ModelWeights] = None, group=None,
+                                  mode: str = "ring") -> List[int]:
+        """Collective: every rank of ``group`` passes the same long prompt.  The prompt is
+        prefilled context-parallel (``parallel.cp_model.cp_prefill``: 1/N of the tokens per
+        rank, ring or Ulysses attention across ranks), its KV lands in this engine's paged
+        pool and the request decodes here.  ``weights`` defaults to the engine's own
+        (unsharded) weights.  The first output token is the greedy choice."""
+        from ..parallel.cp_model import cp_prefill
+
+        w = weights if weights is not None else getattr(self.model, "w", None)
+        if w is None:
+            raise RuntimeError("generate_context_parallel needs the model's unsharded weights")
+        logits, ks, vs = cp_prefill(self.cfg, w, prompt, group=group, mode=mode)
+        rid = self.add_prefilled(prompt, int(logits.argmax()), ks, vs, params)
+        seq = self.seqs[rid]
+        while seq.status not in (SeqStatus.FINISHED, SeqStatus.FAILED, SeqStatus.ABORTED):
+            self.step()
+        if seq.error:
+            raise RuntimeError(seq.error)
+        return list(seq.output)
+
     def abort(self, req_id: int) -> bool:
         """Cancel a waiting or running request between steps; its KV blocks are freed.
         Returns False when the request is unknown or already finished."""

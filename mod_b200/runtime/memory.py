@@ -105,6 +105,7 @@ class KVSwapper:
         self.pool = pool or PinnedPool()
         self.stream = torch.cuda.Stream() if torch.cuda.is_available() and kv.k and kv.k[0].is_cuda else None
         self.saved: Dict[int, List[torch.Tensor]] = {}
+        self.external: set = set()   # requests whose saved blocks were handed in (``stage``), not pool buffers
 
     def _block_bytes(self) -> int:
         k = self.kv.k[0]
@@ -126,6 +127,19 @@ class KVSwapper:
             self.stream.synchronize()
         self.saved[req_id] = bufs
 
+    def stage(self, req_id: int, bufs: List[torch.Tensor]) -> None:
+        """Registers KV computed elsewhere (e.g. a context-parallel prefill) as the saved
+        blocks of ``req_id``: one tensor per K layer then per V layer, each shaped like
+        ``nblk`` blocks of that cache.  The next ``swap_in`` copies them into the
+        sequence's blocks; they are not returned to the pinned pool."""
+        if len(bufs) != len(self.kv.k) + len(self.kv.v):
+            raise ValueError(f"stage: {len(bufs)} tensors for {len(self.kv.k)} K + {len(self.kv.v)} V layers")
+        for t, b in zip(self.kv.k + self.kv.v, bufs):
+            if tuple(b.shape[1:]) != tuple(t.shape[1:]):
+                raise ValueError(f"stage: block shape {tuple(b.shape[1:])} != cache block {tuple(t.shape[1:])}")
+        self.saved[req_id] = [b.to(self.kv.k[0].dtype) for b in bufs]
+        self.external.add(req_id)
+
     def swap_in(self, req_id: int, blocks: List[int]) -> None:
         bufs = self.saved.pop(req_id)
         idx = torch.tensor(blocks[:bufs[0].shape[0]], device=self.kv.k[0].device)  # the saved blocks' new homes
@@ -133,6 +147,9 @@ class KVSwapper:
             t.index_copy_(0, idx, host.to(t.device, non_blocking=True))
         if t.is_cuda:  # the host buffers go back to the pool only after the copies have read them
             torch.cuda.current_stream(t.device).synchronize()
+        if req_id in self.external:
+            self.external.discard(req_id)
+            return
         for host in bufs:
             self.pool.put(host.view(torch.uint8).view(-1))
 

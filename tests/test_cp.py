@@ -90,3 +90,48 @@ def test_merge_partials_handles_empty_sides():
     empty = torch.full_like(l1, float("-inf"))
     o, l = merge_partials(torch.zeros_like(o1), empty, o1, l1)
     assert torch.allclose(o, o1, atol=1e-6) and torch.allclose(l, l1)
+
+
+def _engine_worker(rank, world, port, name, mode, q_out):
+    import torch.distributed as dist
+
+    from mod_b200.config import get_preset
+    from mod_b200.engine import SamplingParams
+    from mod_b200.engine.llm_engine import LLMEngine
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = get_preset(name)
+    g = torch.Generator().manual_seed(11)
+    prompt = torch.randint(0, cfg.vocab_size, (37,), generator=g).tolist()   # 37: the last chunk is padded
+    params = SamplingParams(max_new_tokens=6, ignore_eos=True)
+    eng = LLMEngine(cfg, backend="torch", device="cpu", max_batch=2, max_model_len=64, seed=0,
+                    expert_parallel=False, use_graphs=False)
+    got = eng.generate_context_parallel(prompt, params, mode=mode)
+    single = LLMEngine(cfg, backend="torch", device="cpu", max_batch=2, max_model_len=64, seed=0,
+                       expert_parallel=False, use_graphs=False)
+    want = single.generate([prompt], params)[0]
+    q_out.put((rank, got, want, eng.scheduler.num_resumed))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name,mode", [("tiny-dense", "ring"), ("tiny-dense", "ulysses"), ("tiny-moe", "ring")])
+def test_engine_context_parallel_prefill_then_decode(name, mode):
+    """A 37-token prompt prefilled over 2 gloo ranks (ring / Ulysses attention), its KV put
+    into the engine's paged pool, then decoded by the engine: the same tokens as the
+    single-process engine, with no recomputation of the prompt (one swap-in resume)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_engine_worker, args=(r, world, port, name, mode, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(world)]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got, want, resumed in res:
+        assert got == want, (rank, got, want)
+        assert resumed == 1

@@ -219,6 +219,59 @@ def case(name: str, T: int = 128):
         return ((lambda: N.deltanet_prefill(mix, z, ba, cw, conv, ssm, slots, cu, seq_of, A, dtb, nw, Hk, Hv, d, d,
                                             1e-6, out=out, xc=xc)), Tt * C * (2 + 4 + 4) + Tt * Hv * d * 4,
                 Tt * Hv * d * d * 6)
+    if name == "rope_qknorm":  # Qwen3-30B-A3B decode: 32 q / 4 kv heads of 128, paged KV write
+        from ..ops import reference as R
+
+        Hq, Hkv, D = 32, 4, 128
+        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev).to(bf)
+        qw = torch.ones(D, device=dev, dtype=bf)
+        kw = torch.ones(D, device=dev, dtype=bf)
+        pos = torch.randint(0, 4096, (T,), device=dev, dtype=torch.int32)
+        invf = R.inv_freq(D, 1e6, device=dev)
+        nb = T + 8
+        kc = torch.zeros(nb, Hkv, 16, D, device=dev, dtype=bf)
+        vc = torch.zeros(nb, Hkv, D, 16, device=dev, dtype=bf)
+        slots = (torch.randperm(nb - 1, device=dev)[:T] * 16).int()
+        q = torch.empty(T, Hq, D, device=dev, dtype=bf)
+        return ((lambda: N.rope_qknorm(qkv, qw, kw, pos, invf, slots, q, kc, vc, Hq, Hkv, D, D, 1e-6)),
+                qkv.numel() * 2 * 2, 0)
+    if name == "moe_route":  # softmax top-8 of 128 experts, counts / offsets / cursors
+        E, k = 128, 8
+        logits = torch.randn(T, E, device=dev).to(bf)
+        ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+        wts = torch.empty(T, k, dtype=torch.float32, device=dev)
+        counts = torch.empty(E, dtype=torch.int32, device=dev)
+        offs = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        cursor = torch.empty(E, dtype=torch.int32, device=dev)
+        return ((lambda: N.moe_route(logits, k, True, ids, wts, counts, offs, cursor)),
+                logits.numel() * 2 + T * k * 8, 0)
+    if name in ("sample", "argmax"):  # T rows of the 151,936-entry vocabulary
+        V = 151936
+        logits = torch.randn(T, V, device=dev).to(bf)
+        if name == "argmax":
+            out = torch.empty(T, dtype=torch.long, device=dev)
+            return (lambda: N.argmax(logits, out=out)), logits.numel() * 2, 0
+        temp = torch.full((T,), 0.7, device=dev)
+        tk = torch.full((T,), 50, device=dev, dtype=torch.int32)
+        tp = torch.full((T,), 0.9, device=dev)
+        seeds = torch.arange(T, device=dev, dtype=torch.int64)
+        steps = torch.zeros(T, device=dev, dtype=torch.int64)
+        out = torch.empty(T, dtype=torch.int64, device=dev)
+        return (lambda: N.sample_tokens(logits, temp, tk, tp, seeds, steps, out=out)), logits.numel() * 2, 0
+    if name == "embed":
+        table = (torch.randn(151936, 2048, device=dev) * 0.02).to(bf)
+        ids = torch.randint(0, 151936, (T,), device=dev)
+        out = torch.empty(T, 2048, device=dev, dtype=bf)
+        return (lambda: N.embed(ids, table, out=out)), T * 2048 * 2 * 2, 0
+    if name == "patchify":  # 16 images 3 x 448 x 448 f32 -> 784 patches of 3*16*16 (merge-group order)
+        imgs = torch.rand(16, 3, 448, 448, device=dev)
+        out = torch.empty(16, 784, 768, device=dev, dtype=bf)
+        mean, std = (0.48, 0.46, 0.41), (0.27, 0.26, 0.28)
+        return (lambda: N.patchify(imgs, 448, 16, 2, mean, std, out=out)), imgs.numel() * 4 + out.numel() * 2, 0
+    if name == "bias_gelu":  # ViT MLP up-projection output: 16 images x 784 patches x 4096
+        y = torch.randn(16 * 784, 4096, device=dev).to(bf)
+        b = torch.randn(4096, device=dev).to(bf)
+        return (lambda: N.bias_act(y, b, True)), y.numel() * 2 * 2, 0
     if name == "rmsnorm":
         x = torch.randn(65536, 2048, device=dev).to(bf)
         w = torch.ones(2048, device=dev, dtype=bf)
@@ -228,7 +281,8 @@ def case(name: str, T: int = 128):
 
 
 CASES = ["qkv", "o", "router", "lm_head", "moe_gateup", "moe_down", "attn_decode", "attn_prefill", "rmsnorm",
-         "w8_qkv", "w8_prefill", "w8_moe_gateup", "deltanet_decode", "deltanet_prefill"]
+         "w8_qkv", "w8_prefill", "w8_moe_gateup", "deltanet_decode", "deltanet_prefill", "rope_qknorm", "moe_route",
+         "sample", "argmax", "embed", "patchify", "bias_gelu"]
 
 
 def main(argv=None):

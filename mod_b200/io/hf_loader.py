@@ -20,6 +20,7 @@ from typing import Dict, Iterable, Optional, Tuple
 import torch
 
 from ..config.models import ModelConfig
+from .upload import StagedUploader
 from ..models.weights import (AttnWeights, DeltaNetWeights, LayerWeights, MLPWeights, ModelWeights, MoEWeights)
 
 
@@ -92,8 +93,14 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
             cfg.layer_type(i) == "full_attention" for i in range(cfg.num_hidden_layers)), \
             "tensor-parallel loading covers the dense attention decoder"
 
+    # CUDA targets go through two pinned staging buffers, so mapping reads overlap the copies
+    up = StagedUploader(device) if torch.device(device).type == "cuda" else None
+
+    def put(x, dt=dtype):
+        return up.upload(x, dt) if up is not None else x.to(device=device, dtype=dt)
+
     def t(name):
-        return r.get(name).to(device=device, dtype=dtype)
+        return put(r.get(name))
 
     def sl(name, dim):
         """This TP rank's 1/world of ``name`` along ``dim`` (the whole tensor at world 1)."""
@@ -119,11 +126,11 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
             parts = [q, sl(p + "self_attn.k_proj.weight", 0), sl(p + "self_attn.v_proj.weight", 0)]
             if gate is not None:
                 parts.append(gate)
-            qkv = torch.cat([x.to(dtype) for x in parts], 0).to(device)
+            qkv = put(torch.cat([x.to(dtype) for x in parts], 0))
             bias = None
             if p + "self_attn.q_proj.bias" in r:
-                bias = torch.cat([sl(p + f"self_attn.{n}_proj.bias", 0).to(dtype) for n in "qkv"], 0).to(device)
-            L.attn = AttnWeights(qkv=qkv, o=sl(p + "self_attn.o_proj.weight", 1).to(device, dtype), q_norm=opt(p + "self_attn.q_norm.weight"),
+                bias = put(torch.cat([sl(p + f"self_attn.{n}_proj.bias", 0).to(dtype) for n in "qkv"], 0))
+            L.attn = AttnWeights(qkv=qkv, o=put(sl(p + "self_attn.o_proj.weight", 1)), q_norm=opt(p + "self_attn.q_norm.weight"),
                                  k_norm=opt(p + "self_attn.k_norm.weight"), qkv_bias=bias,
                                  o_bias=opt(p + "self_attn.o_proj.bias"))
             assert tworld == 1 or L.attn.o_bias is None, "a row-parallel o_proj bias would be summed world times"
@@ -137,18 +144,19 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
                               w[:, 2 * dk:2 * dk + rep * dv].reshape(-1, H), w[:, 2 * dk + rep * dv:].reshape(-1, H)], 0)
             ba = r.get(la + "in_proj_ba.weight").view(Hk, 2 * rep, H)
             ba = torch.cat([ba[:, :rep].reshape(-1, H), ba[:, rep:].reshape(-1, H)], 0)
-            L.delta = DeltaNetWeights(in_qkvz=qkvz.to(device, dtype), in_ba=ba.to(device, dtype),
-                                      conv=r.get(la + "conv1d.weight").reshape(-1, cfg.linear_conv_kernel_dim).to(device, dtype),
-                                      A_log=r.get(la + "A_log").to(device, torch.float32),
-                                      dt_bias=r.get(la + "dt_bias").to(device, torch.float32),
+            L.delta = DeltaNetWeights(in_qkvz=put(qkvz), in_ba=put(ba),
+                                      conv=put(r.get(la + "conv1d.weight").reshape(-1, cfg.linear_conv_kernel_dim)),
+                                      A_log=put(r.get(la + "A_log"), torch.float32),
+                                      dt_bias=put(r.get(la + "dt_bias"), torch.float32),
                                       norm=t(la + "norm.weight"), out=t(la + "out_proj.weight"))
         if cfg.is_moe:
             E = cfg.num_experts
             lo, hi = expert_range or (0, E)
             m = p + "mlp."
             w13 = torch.cat([torch.cat([r.get(m + f"experts.{e}.gate_proj.weight"), r.get(m + f"experts.{e}.up_proj.weight")], 0)
-                             .to(dtype) for e in range(lo, hi)], 0).to(device)
-            w2 = torch.cat([r.get(m + f"experts.{e}.down_proj.weight").to(dtype) for e in range(lo, hi)], 0).to(device)
+                             .to(dtype) for e in range(lo, hi)], 0)
+            w13 = put(w13)
+            w2 = put(torch.cat([r.get(m + f"experts.{e}.down_proj.weight").to(dtype) for e in range(lo, hi)], 0))
             mo = MoEWeights(router=t(m + "gate.weight"), w13=w13, w2=w2, e_lo=lo, e_hi=hi)
             if m + "shared_expert.gate_proj.weight" in r:
                 mo.shared = MLPWeights(gate_up=torch.cat([t(m + "shared_expert.gate_proj.weight"),
@@ -159,9 +167,9 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
         else:
             m = p + "mlp."
             if m + "gate_proj.weight" in r:
-                L.mlp = MLPWeights(gate_up=torch.cat([sl(m + "gate_proj.weight", 0).to(device, dtype),
-                                                      sl(m + "up_proj.weight", 0).to(device, dtype)], 0),
-                                   down=sl(m + "down_proj.weight", 1).to(device, dtype))
+                L.mlp = MLPWeights(gate_up=put(torch.cat([sl(m + "gate_proj.weight", 0).to(dtype),
+                                                          sl(m + "up_proj.weight", 0).to(dtype)], 0)),
+                                   down=put(sl(m + "down_proj.weight", 1)))
             else:
                 assert tworld == 1, "tensor-parallel loading covers the gated (SwiGLU) MLP"
                 L.mlp = MLPWeights(up=t(m + "up_proj.weight"), down=t(m + "down_proj.weight"),
@@ -169,7 +177,10 @@ def load_hf(cfg: ModelConfig, path: str, device="cuda", dtype=torch.bfloat16,
         layers.append(L)
     embed = t("model.embed_tokens.weight")
     lm = embed if cfg.tie_word_embeddings or "lm_head.weight" not in r else t("lm_head.weight")
-    return ModelWeights(embed=embed, layers=layers, final_norm=t("model.norm.weight"), lm_head=lm)
+    out = ModelWeights(embed=embed, layers=layers, final_norm=t("model.norm.weight"), lm_head=lm)
+    if up is not None:
+        up.finish()   # the staging buffers are released only after their last copy
+    return out
 
 
 def save_weights(w: ModelWeights, path: str, cfg: Optional[ModelConfig] = None) -> None:

@@ -84,3 +84,25 @@ def test_preemption_swaps_kv_on_gpu(cuda):
     assert st["preempted"] > 0 and st["resumed"] == st["swapped_out"] == st["preempted"]
     agree = sum(a == b for x, y in zip(out, ref) for a, b in zip(x, y)) / sum(len(x) for x in ref)
     assert all(x[:4] == y[:4] for x, y in zip(out, ref)) and agree >= 0.9, (out, ref)
+
+
+def test_staged_upload_and_hf_load_on_gpu(cuda, tmp_path):
+    """Pinned double-buffered upload: many small chunks, a dtype cast on the device, and a
+    whole HF checkpoint loaded onto the GPU equal to the same checkpoint loaded on the host."""
+    from mod_b200.io.hf_loader import load_hf
+    from mod_b200.io.safetensors import save_file
+    from mod_b200.io.upload import StagedUploader
+    from tests.test_io import _hf_from_fused
+
+    up = StagedUploader(cuda, chunk_bytes=4096)
+    src = torch.randn(257, 33)                              # 33,924 bytes: 9 chunks over both buffers
+    got = up.upload(src[:, 1:])                             # non-contiguous source
+    assert torch.equal(got.cpu(), src[:, 1:]) and up.nchunks == 9
+    assert torch.equal(up.upload(src, torch.bfloat16).cpu(), src.bfloat16())
+    cfg = get_preset("tiny-moe")
+    w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=2)
+    save_file(str(tmp_path / "model.safetensors"), _hf_from_fused(cfg, w), {})
+    host = load_hf(cfg, str(tmp_path), device="cpu", dtype=torch.bfloat16)
+    dev = load_hf(cfg, str(tmp_path), device=cuda, dtype=torch.bfloat16)
+    for (n, a), (_, b) in zip(host.tensors(), dev.tensors()):
+        assert b.is_cuda and torch.equal(a, b.cpu()), n

@@ -82,6 +82,8 @@ void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_
                int64_t rs_off, int64_t ag_flag_off, int64_t rs_flag_off, at::Tensor& state,
                const c10::optional<at::Tensor>& x_add, at::Tensor& residual, const at::Tensor& w, double eps,
                const c10::optional<at::Tensor>& local_out);
+void tp_argmax_exchange(const at::Tensor& peers, int64_t rank, int64_t cap, int64_t slot_off, int64_t flag_off,
+                        at::Tensor& state, const at::Tensor& vals, const at::Tensor& idxs, at::Tensor& out);
 void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, int64_t ag_off, int64_t ag_flag_off,
                     at::Tensor& state, const at::Tensor& idx, at::Tensor& out);
 std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
@@ -159,6 +161,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wrap_bf16", &mb::wrap_bf16);
   m.def("tp_reduce", &mb::tp_reduce);
   m.def("tp_gather_rows", &mb::tp_gather_rows);
+  m.def("tp_argmax_exchange", &mb::tp_argmax_exchange);
   m.def("ipc_alloc", [](int64_t b) {
     auto r = mb::ipc_alloc(b);
     return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));

@@ -338,4 +338,92 @@ void vis_wait_merge(const at::Tensor& peers, int64_t rank, int64_t off, int64_t 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------ vocab-parallel greedy LM head
+// Each rank holds rows [r*V/N, (r+1)*V/N) of the LM head and has found, per
+// token row, the best logit of its slice (value + global index, argmax kernel
+// with an index offset).  One CTA: the pairs are stored into slot [rank][t] of
+// every rank's exchange buffer over NVLink, one fence + release flag per rank,
+// then a bounded wait for every peer's flag and a reduction over the ranks in
+// order (strictly greater wins, so a tie keeps the lower rank = lower index, as
+// a full-vocabulary argmax does).  8 bytes per token row cross each link
+// instead of the all-gathered logits.
+struct ValIdx {
+  float v;
+  int i;
+};
+
+__global__ void __launch_bounds__(1024)
+    tp_argmax_exchange_kernel(const uint64_t* __restrict__ peers, int rank, int nranks, int cap, int64_t slot_off,
+                              int64_t flag_off, uint32_t* epoch, const float* __restrict__ vals,
+                              const int64_t* __restrict__ idxs, int T, int64_t* __restrict__ out, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t e = *epoch + 1;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    ValIdx vi;
+    vi.v = vals[t];
+    vi.i = (int)idxs[t];
+    const uint64_t packed = *reinterpret_cast<const uint64_t*>(&vi);
+    for (int p = 0; p < nranks; ++p)
+      reinterpret_cast<uint64_t*>(peers[p] + slot_off)[(size_t)rank * cap + t] = packed;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < nranks; ++p)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(reinterpret_cast<uint32_t*>(peers[p] + flag_off) + rank),
+                   "r"(e)
+                   : "memory");
+  }
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  const uint64_t self = peers[rank];
+  const uint32_t* f = reinterpret_cast<const uint32_t*>(self + flag_off);
+  for (int p = threadIdx.x; p < nranks; p += blockDim.x) {
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acq(f + p) - e) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_status(status, kErrPeerTimeout);
+        ok_all = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  __threadfence();
+  const uint64_t* slots = reinterpret_cast<const uint64_t*>(self + slot_off);
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    float bv = -INFINITY;
+    int bi = 0;
+    for (int p = 0; ok_all && p < nranks; ++p) {
+      const uint64_t raw = __ldcg(reinterpret_cast<const unsigned long long*>(slots + (size_t)p * cap + t));
+      const ValIdx vi = *reinterpret_cast<const ValIdx*>(&raw);
+      if (p == 0 || vi.v > bv) {
+        bv = vi.v;
+        bi = vi.i;
+      }
+    }
+    out[t] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch = e;
+}
+
+void tp_argmax_exchange(const at::Tensor& peers, int64_t rank, int64_t cap, int64_t slot_off, int64_t flag_off,
+                        at::Tensor& state, const at::Tensor& vals, const at::Tensor& idxs, at::Tensor& out) {
+  const int T = (int)vals.numel();
+  TORCH_CHECK(vals.scalar_type() == at::kFloat && idxs.scalar_type() == at::kLong && out.scalar_type() == at::kLong);
+  TORCH_CHECK(idxs.numel() == T && out.numel() == T && T <= cap, "tp_argmax_exchange: ", T, " rows > capacity ", cap);
+  TORCH_CHECK(slot_off % 8 == 0 && flag_off % 4 == 0);
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(out.device());
+  const int threads = std::min(1024, std::max(32, (T + 31) / 32 * 32));
+  launch_k(tp_argmax_exchange_kernel, 1, threads, 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), (int)rank, (int)peers.numel(), (int)cap,
+           slot_off, flag_off, reinterpret_cast<uint32_t*>(state.data_ptr<int>()), vals.data_ptr<float>(),
+           idxs.data_ptr<int64_t>(), T, out.data_ptr<int64_t>(), status_ptr(out.device().index()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace mb

@@ -95,7 +95,21 @@ class TPDecoderLM:
         return self.be.linear(h, self.w.lm_head)
 
     def sample_greedy(self, h: torch.Tensor) -> torch.Tensor:
-        return self.be.argmax(self.logits(h))
+        """Greedy tokens.  With the fused boundaries the LM head is vocabulary-parallel: each rank
+        multiplies its 1/N row slice of the (replicated) head, takes the best logit of its slice
+        and the ranks exchange one (value, index) pair per token row over NVLink, so a step reads
+        1/N of the head instead of all of it (``pio/plugins/cuda/c_src/tensor_ops_cuda.cu:782-788``
+        is the reference's full-vocabulary argmax launch)."""
+        V = self.w.lm_head.shape[0]
+        if (not hasattr(self.comm, "argmax_exchange") or V % self.world or not hasattr(self.be, "N")
+                or not isinstance(self.w.lm_head, torch.Tensor)):
+            return self.be.argmax(self.logits(h))
+        Vl = V // self.world
+        r = self.comm.rank
+        local = self.be.linear(h, self.w.lm_head[r * Vl:(r + 1) * Vl])   # a row slice: a contiguous view
+        vals = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
+        idxs = self.be.N.argmax(local, out_val=vals, index_offset=r * Vl)
+        return self.comm.argmax_exchange(vals, idxs)
 
 
 def _prefill_ref(q, kc, vc, fb):

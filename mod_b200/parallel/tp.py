@@ -62,13 +62,18 @@ class FusedTP:
         self.rs_off = al(N * cap * H * 2)
         self.ag_flag_off = al(self.rs_off + N * cap * H * 2)
         self.rs_flag_off = al(self.ag_flag_off + N * 4)
-        total = al(self.rs_flag_off + N * 4)
+        # vocab-parallel greedy head: (best logit, index) of every rank's vocabulary slice per token row
+        self.am_cap = padded_tokens(max_tokens, self.world)
+        self.am_off = al(self.rs_flag_off + N * 4)
+        self.am_flag_off = al(self.am_off + N * self.am_cap * 8)
+        total = al(self.am_flag_off + N * 4)
         self.buf = ExchangeBuffer(total, group)
         self.peers = self.buf.peers
         self.own = self.peers.tolist()[self.rank]
         self.ag_flags_addr = self.own + self.ag_flag_off
         dev = torch.device("cuda", torch.cuda.current_device())
         self.state = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.am_state = torch.zeros(2, dtype=torch.int32, device=dev)
         self.gathered = self.C.wrap_bf16(self.own + self.ag_off, N * cap, H)
 
     # -------------------------------------------------------------- boundaries
@@ -103,6 +108,14 @@ class FusedTP:
         ws = torch.empty(16 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
         self.C.tp_gemm(x, w, x, False, True, False, 0, self.state, self.rank, self.world, T // self.world,
                        self.peers, self.rs_off, self.rs_flag_off, ws)
+
+    def argmax_exchange(self, vals: torch.Tensor, idxs: torch.Tensor) -> torch.Tensor:
+        """Per token row, the (value, global index) pair of this rank's vocabulary slice ->
+        the index of the best logit over every rank's slice (P2P pair exchange, one launch)."""
+        out = torch.empty(vals.numel(), dtype=torch.long, device=vals.device)
+        self.C.tp_argmax_exchange(self.peers, self.rank, self.am_cap, self.am_off, self.am_flag_off, self.am_state,
+                                  vals, idxs, out)
+        return out
 
     def gather_rows(self, idx: torch.Tensor, T: int) -> torch.Tensor:
         out = torch.empty(idx.numel(), self.H, dtype=torch.bfloat16, device=idx.device)

@@ -150,8 +150,8 @@ def moe_check(cfg, eng, dev, world, rank):
     import torch
     import torch.distributed as dist
 
-    from mod_b200.models.backend import TorchBackend
     from mod_b200.models.weights import random_weights
+    from mod_b200.ops import reference as R
 
     c1 = copy.deepcopy(cfg)
     c1.num_hidden_layers = 1
@@ -159,18 +159,31 @@ def moe_check(cfg, eng, dev, world, rank):
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     T = eng.runner.max_batch
     x = (torch.randn(T, cfg.hidden_size, device=dev, generator=g) * 0.5).bfloat16()
-    ref = TorchBackend().moe(x, full.layers[0].moe, cfg.num_experts_per_tok, cfg.norm_topk_prob,
-                             cfg.moe_intermediate_size).float()
+    # Routing is compared on the tokens whose top-k set is the same from fp32 and from bf16-rounded router
+    # logits.  The fused route sums the router logits in fp32, a library GEMM rounds them to bf16, and with
+    # random-init N(0, 0.02) routers near-tied top-k choices flip between the two (2 of 128 tokens at this
+    # shape): both answers are valid routings, and one token sent to a different expert would dominate a
+    # max-error check.  The count of such tokens is reported.
+    mo = full.layers[0].moe
+    logits32 = x.float() @ mo.router.float().t()
+    ids, wts = R.moe_route(logits32, cfg.num_experts_per_tok, cfg.norm_topk_prob)
+    ids16 = R.moe_route(logits32.bfloat16(), cfg.num_experts_per_tok, cfg.norm_topk_prob)[0]
+    same = (ids16.sort(-1).values == ids.sort(-1).values).all(-1)
+    ref = R.moe_experts(x, ids, wts, mo.w13, mo.w2, cfg.num_experts, cfg.moe_intermediate_size).float()
     out = eng.model.moe_impl(x, eng.model.w.layers[0].moe).float()
     torch.cuda.synchronize()
-    err = torch.tensor([((out - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()], device=dev,
-                       dtype=torch.float64)
+    diff = (out - ref).abs().amax(-1)[same]
+    err = torch.tensor([(diff.max() if diff.numel() else diff.new_zeros(())).item() /
+                        max(ref.abs().max().item(), 1e-6)], device=dev, dtype=torch.float64)
+    flips = torch.tensor([float((~same).sum())], device=dev)
     dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    dist.all_reduce(flips)
     del full
     torch.cuda.empty_cache()
     e = err.item()
     return {"status": "ok" if e < 3e-2 else "fail", "max_rel_err": round(e, 5),
-            "against": "unsharded torch MoE, layer 0, each rank's own tokens"}
+            "against": "unsharded torch MoE (fp32 router logits), layer 0, each rank's own tokens",
+            "near_tied_tokens_excluded": int(flips.item())}
 
 
 def main():

@@ -1,6 +1,7 @@
 // Fused token sampling over LM-head logits: temperature, top-k, top-p, greedy.
 //
-// One CTA per row, no sort.  With x = logit / T:
+// One CTA per row, no sort (every pass streams the row with 16-byte loads, several in flight
+// per thread).  With x = logit / T:
 //   pass 1      row max m and Z = sum exp(x - m)
 //   passes 2-8  the largest t_k with count{x >= t_k} >= k (k > 0) and the
 //               largest t_p with mass{x >= t_p} >= p, each by 8-way refinement
@@ -20,6 +21,8 @@
 //
 // The reference has only greedy argmax (tensor_ops_cuda.cu:786, undefined) and a
 // host-side top-k (pio/plugins/cpu/c_src/tensor_ops.c topk).
+#include <type_traits>
+
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -78,6 +81,40 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return r;
 }
 
+// Calls f(value, index) for every entry of a row, this thread's share.  bf16 rows whose
+// length is a multiple of 8 and whose start is 16-byte aligned (the LM head's output) are read
+// as 16-byte vectors, kUnroll of them in flight per thread before any is used: a pass is then
+// bound by L2 bandwidth instead of one load latency per element.
+constexpr int kUnroll = 4;
+template <typename T, typename F>
+__device__ __forceinline__ void row_for_each(const T* __restrict__ x, int64_t V, F&& f) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if ((V & 7) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      const uint4* x4 = reinterpret_cast<const uint4*>(x);
+      const int64_t n4 = V >> 3;
+      for (int64_t b = threadIdx.x; b < n4; b += (int64_t)kThreads * kUnroll) {
+        uint4 r[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t j = b + (int64_t)u * kThreads;
+          r[u] = j < n4 ? __ldg(x4 + j) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t j = b + (int64_t)u * kThreads;
+          if (j < n4) {
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&r[u]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) f(__bfloat162float(h[q]), j * 8 + q);
+          }
+        }
+      }
+      return;
+    }
+  }
+  for (int64_t i = threadIdx.x; i < V; i += kThreads) f(ld(x, i), i);
+}
+
 }  // namespace
 
 template <typename T>
@@ -98,12 +135,12 @@ __global__ void __launch_bounds__(kThreads)
   const float inv_t = greedy ? 1.f : 1.f / temp;
   // ---- pass 1: max and normaliser
   float m = -INFINITY;
-  for (int64_t i = tid; i < V; i += kThreads) m = fmaxf(m, ld(x, i));
+  row_for_each(x, V, [&](float v, int64_t) { m = fmaxf(m, v); });
   m = block_max(m, red) * inv_t;
   float tau = -INFINITY;
   if (!greedy) {
     float z = 0.f;
-    for (int64_t i = tid; i < V; i += kThreads) z += __expf(ld(x, i) * inv_t - m);
+    row_for_each(x, V, [&](float v, int64_t) { z += __expf(v * inv_t - m); });
     z = block_sum(z, red);
     const int k = top_k[row];
     const float p = top_p[row];
@@ -116,13 +153,13 @@ __global__ void __launch_bounds__(kThreads)
     float lo_k = m - kWindow, hi_k = m + 1e-6f, lo_p = m - kWindow, hi_p = m + 1e-6f;
     {
       float c = 0.f, ms = 0.f;
-      for (int64_t i = tid; i < V; i += kThreads) {
-        const float v = ld(x, i) * inv_t;
+      row_for_each(x, V, [&](float raw, int64_t) {
+        const float v = raw * inv_t;
         if (v >= lo_k) {
           c += 1.f;
           ms += __expf(v - m);
         }
-      }
+      });
       c = block_sum(c, red);
       ms = block_sum(ms, red) * inv_z;
       if (!use_k || c < (float)k) lo_k = -INFINITY;
@@ -138,9 +175,9 @@ __global__ void __launch_bounds__(kThreads)
         float ca = 0.f, ma = 0.f;  // entries at or above a bracket's top count for all its thresholds
 #pragma unroll
         for (int w = 0; w < kWays; ++w) c[w] = ms[w] = 0.f;
-        for (int64_t i = tid; i < V; i += kThreads) {
-          const float v = ld(x, i) * inv_t;
-          if (v < lowest) continue;
+        row_for_each(x, V, [&](float raw, int64_t) {
+          const float v = raw * inv_t;
+          if (v < lowest) return;
           if (v >= floor_k) {  // thresholds lo_k + (w+1) sk; v counts for every one <= v
             if (v >= hi_k) {
               ca += 1.f;
@@ -162,7 +199,7 @@ __global__ void __launch_bounds__(kThreads)
                 if (w <= top) ms[w] += e;
             }
           }
-        }
+        });
 #pragma unroll
         for (int w = 0; w < kWays; ++w) {
           c[w] += ca;
@@ -207,13 +244,13 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t seed = (uint64_t)seeds[row], stp = (uint64_t)steps[row];
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int64_t i = tid; i < V; i += kThreads) {
-    const float v = ld(x, i) * inv_t;
+  row_for_each(x, V, [&](float raw, int64_t i) {
+    const float v = raw * inv_t;
     float s;
     if (greedy) {
       s = v;
     } else {
-      if (!(v >= tau)) continue;
+      if (!(v >= tau)) return;
       const float u = uniform01(seed, stp, (uint32_t)i);
       s = v - __logf(-__logf(u));
     }
@@ -221,7 +258,7 @@ __global__ void __launch_bounds__(kThreads)
       bv = s;
       bi = (int)i;
     }
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);

@@ -200,7 +200,7 @@ __global__ void splitk_swiglu_kernel(const float* __restrict__ ws, int splits, i
 // y[T, I] = silu(x @ gate^T) * (x @ up^T) with w = [gate; up] ([2I, K]), dual-accumulator
 // tcgen05 GEMM; decode shapes (T <= 256) use split-K with the SwiGLU applied after the reduction.
 void swiglu_linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& workspace,
-                   int64_t wait_flags, const c10::optional<at::Tensor>& state) {
+                   int64_t wait_flags, const c10::optional<at::Tensor>& state, int64_t nranks) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && w.is_contiguous());
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.is_contiguous());
   const int64_t T = x.size(0), K = x.size(1), I = w.size(0) / 2;
@@ -215,9 +215,11 @@ void swiglu_linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, cons
   a.ldc = (int)I;
   a.out_rows = (int)T;
   a.status = status_ptr(x.device().index());
-  if (wait_flags && state && state->defined()) {
+  if (wait_flags && state && state->defined()) {  // wait for every rank's published shard
+    TORCH_CHECK(nranks >= 1, "swiglu_linear: waiting on shard flags needs the rank count");
     a.tp.ag_flags = reinterpret_cast<const uint32_t*>(wait_flags);
     a.tp.epoch = reinterpret_cast<uint32_t*>(state->data_ptr<int>());
+    a.tp.nranks = (int)nranks;
   }
   const int bn = pick_bn(T, true);
   auto ta = make_tmap_bf16(w.data_ptr(), w.size(0), K, K, 128);

@@ -71,6 +71,11 @@ struct ClusterArgs {
   float eps;
   int* status;
   const float* w_scale;   // int8 weights: per-row (output feature) scale, applied after the reduction
+  // tensor parallelism: x is the gathered buffer that the shard owners push into; the producer
+  // waits (bounded) until ag_flags[p] >= *ag_epoch for every rank p before it loads x
+  const uint32_t* ag_flags;
+  const uint32_t* ag_epoch;
+  int ag_nranks;
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -167,6 +172,23 @@ __global__ void __launch_bounds__(192, 1)
       }
       pdl_wait();
       pdl_trigger();
+      if (args.ag_flags) {  // every rank's shard of this boundary is in the gathered buffer
+        const uint32_t want = *args.ag_epoch;
+        for (int p = 0; p < args.ag_nranks; ++p) {
+          const uint64_t t0 = globaltimer_ns();
+          while (true) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(args.ag_flags + p) : "memory");
+            if ((int32_t)(v - want) >= 0) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              set_status(args.status, kErrPeerTimeout);
+              break;
+            }
+          }
+        }
+        // the peers' stores were observed through the generic proxy; the activation tiles are read by TMA
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
       for (int it = 0; it < kbs && ok; ++it) {
         const int s = it % STAGES;
         uint8_t* st = smem + s * L::kStage;
@@ -399,6 +421,15 @@ void run(const at::Tensor& x, const at::Tensor& w, ClusterArgs a, int64_t cs_req
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void set_wait(ClusterArgs& a, int64_t ag_flags, const c10::optional<at::Tensor>& state, int64_t nranks) {
+  if (!ag_flags) return;
+  TORCH_CHECK(state && state->defined() && state->scalar_type() == at::kInt && nranks >= 1,
+              "gemm_cluster: waiting on shard flags needs the boundary state and the rank count");
+  a.ag_flags = reinterpret_cast<const uint32_t*>(ag_flags);
+  a.ag_epoch = reinterpret_cast<const uint32_t*>(state->data_ptr<int>());
+  a.ag_nranks = (int)nranks;
+}
+
 void check_operands(const at::Tensor& x, const at::Tensor& w) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 &&
               (w.scalar_type() == at::kBFloat16 || w.scalar_type() == at::kChar));
@@ -410,8 +441,11 @@ void check_operands(const at::Tensor& x, const at::Tensor& w) {
 }  // namespace
 
 // y[T, N] = x @ w^T (+ residual) for decode-sized T (<= 128); cs = 0 picks the cluster size.
+// ag_flags != 0 (tensor parallelism): x is the gathered buffer; the loads of x wait until every
+// rank's flag reaches state[0] (bounded).
 void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
-                    const c10::optional<at::Tensor>& residual, int64_t cs) {
+                    const c10::optional<at::Tensor>& residual, int64_t cs, int64_t ag_flags,
+                    const c10::optional<at::Tensor>& state, int64_t nranks) {
   check_operands(x, w);
   TORCH_CHECK(w.scalar_type() == at::kBFloat16, "linear_cluster: bf16 weights (int8: linear_cluster_w8)");
   TORCH_CHECK(y.is_contiguous() && y.scalar_type() == at::kBFloat16 && y.size(0) == x.size(0) &&
@@ -425,6 +459,7 @@ void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
     TORCH_CHECK(residual->is_contiguous() && residual->sizes() == y.sizes());
     a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
   }
+  set_wait(a, ag_flags, state, nranks);
   run(x, w, a, cs);
 }
 
@@ -454,7 +489,8 @@ void linear_cluster_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tens
 void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& q_w,
                       const c10::optional<at::Tensor>& k_w, const at::Tensor& positions, const at::Tensor& inv_freq,
                       const c10::optional<at::Tensor>& slots, at::Tensor& q_out, at::Tensor& k_cache,
-                      at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs) {
+                      at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs,
+                      int64_t ag_flags, const c10::optional<at::Tensor>& state, int64_t nranks) {
   check_operands(x, w);
   TORCH_CHECK(w.scalar_type() == at::kBFloat16, "qkv_rope_cluster: bf16 weights");
   const int64_t T = x.size(0);
@@ -484,6 +520,7 @@ void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optio
   a.rot_dim = (int)rot_dim;
   a.block_size = (int)k_cache.size(2);
   a.eps = (float)eps;
+  set_wait(a, ag_flags, state, nranks);
   run(x, w, a, cs);
 }
 

@@ -6,7 +6,7 @@ namespace mb {
 void linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual,
             const c10::optional<at::Tensor>& workspace, int64_t splits, int64_t orient);
 void swiglu_linear(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& workspace,
-                   int64_t wait_flags, const c10::optional<at::Tensor>& state);
+                   int64_t wait_flags, const c10::optional<at::Tensor>& state, int64_t nranks);
 void grouped_linear(const at::Tensor& x, const at::Tensor& w, const at::Tensor& offs, at::Tensor& y, int64_t groups,
                     bool swiglu, int64_t max_rows_per_group);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
@@ -84,6 +84,11 @@ void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_
                const c10::optional<at::Tensor>& local_out);
 void tp_argmax_exchange(const at::Tensor& peers, int64_t rank, int64_t cap, int64_t slot_off, int64_t flag_off,
                         at::Tensor& state, const at::Tensor& vals, const at::Tensor& idxs, at::Tensor& out);
+void tp_nvls_reduce(int64_t self, int64_t mc, int64_t rank, int64_t nranks, bool with_partials, int64_t rows,
+                    int64_t H, int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off,
+                    at::Tensor& state, const c10::optional<at::Tensor>& x_add, at::Tensor& residual,
+                    const at::Tensor& w, double eps, const c10::optional<at::Tensor>& local_out);
+bool multicast_supported(int64_t device);
 void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, int64_t ag_off, int64_t ag_flag_off,
                     at::Tensor& state, const at::Tensor& idx, at::Tensor& out);
 std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
@@ -100,13 +105,15 @@ void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
                      const at::Tensor& map, const at::Tensor& wts, at::Tensor& residual, const at::Tensor& w,
                      at::Tensor& out, double eps, const c10::optional<at::Tensor>& rows);
 void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
-                    const c10::optional<at::Tensor>& residual, int64_t cs);
+                    const c10::optional<at::Tensor>& residual, int64_t cs, int64_t ag_flags,
+                    const c10::optional<at::Tensor>& state, int64_t nranks);
 void linear_cluster_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
                        const c10::optional<at::Tensor>& residual, int64_t cs);
 void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& q_w,
                       const c10::optional<at::Tensor>& k_w, const at::Tensor& positions, const at::Tensor& inv_freq,
                       const c10::optional<at::Tensor>& slots, at::Tensor& q_out, at::Tensor& k_cache,
-                      at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs);
+                      at::Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t rot_dim, double eps, int64_t cs,
+                      int64_t ag_flags, const c10::optional<at::Tensor>& state, int64_t nranks);
 void vit_rope_kv(const at::Tensor& qkv, const at::Tensor& pos, int64_t N, int64_t heads, int64_t D, double theta,
                  at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache);
 void decode_advance(const at::Tensor& sampled, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx, at::Tensor& slots,
@@ -162,6 +169,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce", &mb::tp_reduce);
   m.def("tp_gather_rows", &mb::tp_gather_rows);
   m.def("tp_argmax_exchange", &mb::tp_argmax_exchange);
+  m.def("tp_nvls_reduce", &mb::tp_nvls_reduce);
+  m.def("multicast_supported", &mb::multicast_supported);
   m.def("ipc_alloc", [](int64_t b) {
     auto r = mb::ipc_alloc(b);
     return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));

@@ -22,6 +22,8 @@ import torch.distributed as dist
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--impl", default="native", choices=["native", "baseline"])
+    ap.add_argument("--comm", default="p2p", choices=["p2p", "nvls", "auto"],
+                    help="layer-boundary flavour of the native path")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=16)
@@ -43,7 +45,7 @@ def main(argv=None):
     backend = "native" if a.impl == "native" else "torch"
     eng = LLMEngine(cfg, backend=backend, device=dev, max_batch=a.batch,
                     max_model_len=a.prompt_len + a.warmup + 3 * a.steps + 16, max_prefill_tokens=a.prefill_tokens,
-                    tensor_parallel=world > 1, seed=0)
+                    tensor_parallel=world > 1, seed=0, tp_comm=a.comm)
     g = torch.Generator().manual_seed(1000)
     prompts = [torch.randint(0, cfg.vocab_size, (a.prompt_len,), generator=g).tolist() for _ in range(a.batch)]
     params = SamplingParams(max_new_tokens=a.warmup + 3 * a.steps + 8, ignore_eos=True)
@@ -80,7 +82,8 @@ def main(argv=None):
 
         check_status(dev)
     if rank == 0:
-        print(json.dumps({"config": f"{a.model} TP={world}", "impl": a.impl, "batch": a.batch,
+        print(json.dumps({"config": f"{a.model} TP={world}", "impl": a.impl,
+                          "comm": a.comm if a.impl == "native" else "nccl", "batch": a.batch,
                           "prompt_len": a.prompt_len, "ttft_p50_s": round(p50, 4), "decode_ms_per_step": round(ms, 3),
                           "decode_tok_s": round(a.batch / ms * 1000, 1),
                           "timed": "graph replay" if B is not None else "eager engine steps"}), flush=True)

@@ -41,7 +41,8 @@ class LLMEngine:
                  expert_parallel: Optional[bool] = None, tensor_parallel: bool = False,
                  quantization: Optional[str] = None, prefix_caching: bool = False,
                  prefill_chunk: Optional[int] = None, kv_swap: bool = True, kv_swap_bytes: int = 8 << 30,
-                 offload_layers: Union[int, str, None] = None, model_path: Optional[str] = None):
+                 offload_layers: Union[int, str, None] = None, model_path: Optional[str] = None,
+                 tp_comm: Optional[str] = None):
         """``expert_parallel`` (default: on when a process group of >1 ranks
         exists and the model is MoE): every rank serves its own requests with a
         replicated attention stack and holds E/world experts; MoE layers
@@ -60,7 +61,10 @@ class LLMEngine:
         reader, each rank taking only its part (its TP slices or its EP
         experts); ``"auto"`` takes N
         from the placement planner for this device's memory.  Streaming runs
-        eagerly (no decode graphs)."""
+        eagerly (no decode graphs).  ``tp_comm`` (tensor parallelism, native
+        backend): the layer-boundary flavour, ``"p2p"`` (peer stores, the
+        default), ``"nvls"`` (NVSwitch multimem reduce + multicast stores) or
+        ``"auto"``; the ``MB_TP_COMM`` environment variable sets the default."""
         import torch.distributed as dist
 
         self.cfg = cfg
@@ -81,7 +85,7 @@ class LLMEngine:
         self.tensor_parallel = tensor_parallel and world > 1
         if self.tensor_parallel and model is None:
             from ..models.tp_decoder import TPDecoderLM, shard_weights
-            from ..parallel.tp import FusedTP, NcclTP
+            from ..parallel.tp import make_tp_comm
 
             if model_path is not None and weights is None:
                 from ..io.hf_loader import load_hf
@@ -93,7 +97,9 @@ class LLMEngine:
                 shard = shard_weights(cfg, weights, rank, world)
             weights = None
             mt = max(max_batch, max_prefill_tokens)
-            comm = FusedTP(cfg.hidden_size, mt) if backend == "native" else NcclTP(cfg.hidden_size, mt)
+            # boundary flavour: P2P peer stores (default), NVLS multimem, or the NCCL baseline
+            kind = tp_comm or os.environ.get("MB_TP_COMM", "p2p")
+            comm = make_tp_comm(kind if backend == "native" else "nccl", cfg.hidden_size, mt)
             model = TPDecoderLM(cfg, shard, self.backend, comm, world)
             kv_heads = model.Hkv
             expert_parallel = False

@@ -70,11 +70,15 @@ class TPDecoderLM:
         comm.publish(h, layers[0].in_norm, eps, partials=False)
         for i, L in enumerate(layers):
             aw = L.attn
-            qkv = comm.ag_gemm(aw.qkv, Tp)[:T]
             kc, vc = kv.layer(i)
-            q = torch.empty(T, self.Hq, D, dtype=qkv.dtype, device=qkv.device)
-            be.rope_qknorm(qkv, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc, vc,
-                           self.Hq, self.Hkv, D, cfg.rotary_dim, eps)
+            q = torch.empty(T, self.Hq, D, dtype=h.dtype, device=h.device)
+            fused = hasattr(comm, "ag_qkv_rope") and comm.ag_qkv_rope(
+                aw.qkv, T, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc, vc, self.Hq,
+                self.Hkv, D, cfg.rotary_dim, eps)
+            if not fused:
+                qkv = comm.ag_gemm(aw.qkv, Tp)[:T]
+                be.rope_qknorm(qkv, aw.q_norm, aw.k_norm, fb.positions, self.inv_freq, fb.slot_mapping, q, kc, vc,
+                               self.Hq, self.Hkv, D, cfg.rotary_dim, eps)
             if fb.is_decode:
                 o = be.attn_decode(q, kc, vc, fb.block_tables, fb.ctx_lens, fb.attn_splits)
             else:

@@ -36,13 +36,16 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
 
 
 def linear_cluster(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
-                   residual: Optional[torch.Tensor] = None, cs: int = 0) -> torch.Tensor:
+                   residual: Optional[torch.Tensor] = None, cs: int = 0, wait=None) -> torch.Tensor:
     """``out = x @ w.T (+ residual)`` for decode-sized x (1..128 rows): split-K over a
     thread-block cluster of ``cs`` CTAs (0: automatic) reduced through distributed
-    shared memory, one launch and no fp32 workspace."""
+    shared memory, one launch and no fp32 workspace.  ``wait = (flags_addr, state,
+    nranks)`` (tensor parallelism): x is a gathered buffer and its loads wait until
+    every rank's flag reaches ``state[0]``."""
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-    _C().linear_cluster(x, w, out, residual, cs)
+    flags, state, nranks = wait if wait is not None else (0, None, 0)
+    _C().linear_cluster(x, w, out, residual, cs, flags, state, nranks)
     return out
 
 
@@ -57,11 +60,13 @@ def linear_cluster_w8(x: torch.Tensor, wq: torch.Tensor, scale: torch.Tensor, ou
 
 
 def qkv_rope_cluster(x, w, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, rot_dim, eps,
-                     cs: int = 0):
+                     cs: int = 0, wait=None):
     """Packed QKV projection (head_dim 128) with QK-RMSNorm, RoPE and the paged KV
-    write in the cluster GEMM's epilogue; same result as ``linear`` + ``rope_qknorm``."""
+    write in the cluster GEMM's epilogue; same result as ``linear`` + ``rope_qknorm``.
+    ``wait``: as in :func:`linear_cluster`."""
+    flags, state, nranks = wait if wait is not None else (0, None, 0)
     _C().qkv_rope_cluster(x, w, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, rot_dim,
-                          eps, cs)
+                          eps, cs, flags, state, nranks)
     return q_out
 
 
@@ -73,7 +78,7 @@ def swiglu_linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] 
         out = torch.empty(T, I, dtype=x.dtype, device=x.device)
     if workspace is None:
         workspace = torch.empty(8 * T * 2 * I, dtype=torch.float32, device=x.device)
-    _C().swiglu_linear(x, w, out, workspace, 0, None)
+    _C().swiglu_linear(x, w, out, workspace, 0, None, 0)
     return out
 
 

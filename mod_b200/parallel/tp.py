@@ -21,6 +21,7 @@ The reference has tensor-parallel settings only as configuration strings
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, Optional
 
 import torch
@@ -41,6 +42,26 @@ def padded_tokens(T: int, world: int) -> int:
     return -(-T // step) * step
 
 
+def exchange_layout(hidden: int, max_tokens: int, world: int) -> Dict[str, int]:
+    """Byte offsets of one rank's exchange buffer, the same for the P2P and NVLS
+    flavours: ``ag`` (gathered shards, [N*cap, H] bf16), ``rs`` (P2P: reduce-scatter
+    slots [N, cap, H]; NVLS: this rank's full partial output [N*cap, H]), the two
+    flag arrays ([N] u32 each), the argmax pairs ([N, am_cap] 8-byte (value, index))
+    and their flags.  Every region starts on a 256-byte boundary."""
+    al = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    N, H = world, hidden
+    cap = padded_tokens(max_tokens, world) // world  # rows per rank
+    L = {"cap": cap, "ag_off": 0}
+    L["rs_off"] = al(N * cap * H * 2)
+    L["ag_flag_off"] = al(L["rs_off"] + N * cap * H * 2)
+    L["rs_flag_off"] = al(L["ag_flag_off"] + N * 4)
+    L["am_cap"] = padded_tokens(max_tokens, world)
+    L["am_off"] = al(L["rs_flag_off"] + N * 4)
+    L["am_flag_off"] = al(L["am_off"] + N * L["am_cap"] * 8)
+    L["total"] = al(L["am_flag_off"] + N * 4)
+    return L
+
+
 class FusedTP:
     """Fused boundaries.  Each rank's exchange buffer holds
     ``gathered [N*cap, H]`` (every rank's normed shard, pushed there by the
@@ -55,26 +76,19 @@ class FusedTP:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.H = hidden
-        self.cap = padded_tokens(max_tokens, self.world) // self.world  # rows per rank
-        al = lambda x: (x + 255) // 256 * 256  # noqa: E731
-        N, cap, H = self.world, self.cap, hidden
-        self.ag_off = 0
-        self.rs_off = al(N * cap * H * 2)
-        self.ag_flag_off = al(self.rs_off + N * cap * H * 2)
-        self.rs_flag_off = al(self.ag_flag_off + N * 4)
-        # vocab-parallel greedy head: (best logit, index) of every rank's vocabulary slice per token row
-        self.am_cap = padded_tokens(max_tokens, self.world)
-        self.am_off = al(self.rs_flag_off + N * 4)
-        self.am_flag_off = al(self.am_off + N * self.am_cap * 8)
-        total = al(self.am_flag_off + N * 4)
-        self.buf = ExchangeBuffer(total, group)
+        self._set_layout(exchange_layout(hidden, max_tokens, self.world))
+        self.buf = ExchangeBuffer(self.total, group)
         self.peers = self.buf.peers
         self.own = self.peers.tolist()[self.rank]
         self.ag_flags_addr = self.own + self.ag_flag_off
         dev = torch.device("cuda", torch.cuda.current_device())
         self.state = torch.zeros(8, dtype=torch.int32, device=dev)
         self.am_state = torch.zeros(2, dtype=torch.int32, device=dev)
-        self.gathered = self.C.wrap_bf16(self.own + self.ag_off, N * cap, H)
+        self.gathered = self.C.wrap_bf16(self.own + self.ag_off, self.world * self.cap, hidden)
+
+    def _set_layout(self, L: Dict[str, int]) -> None:
+        for k, v in L.items():
+            setattr(self, k, v)
 
     # -------------------------------------------------------------- boundaries
     def publish(self, residual: torch.Tensor, norm_w: torch.Tensor, eps: float, partials: bool,
@@ -89,10 +103,14 @@ class FusedTP:
         fused_swiglu = swiglu and T <= 256 and n_out % 128 == 0
         cols = n_out if fused_swiglu else w.shape[0]
         out = torch.empty(T, cols, dtype=torch.bfloat16, device=w.device)
-        ws = torch.empty(16 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
         x = self.gathered[:T]
+        if not swiglu and self._cluster_ok(T, w):
+            from ..ops import native
+
+            return native.linear_cluster(x, w, out=out, wait=(self.ag_flags_addr, self.state, self.world))
+        ws = torch.empty(16 * T * w.shape[0], dtype=torch.float32, device=w.device) if T <= 256 else None
         if fused_swiglu:  # split-K dual GEMM, SwiGLU after the reduction; waits on the shards' flags
-            self.C.swiglu_linear(x, w, out, ws, self.ag_flags_addr, self.state)
+            self.C.swiglu_linear(x, w, out, ws, self.ag_flags_addr, self.state, self.world)
             return out
         self.C.tp_gemm(x, w, out, True, False, False, self.ag_flags_addr, self.state, self.rank, self.world,
                        T // self.world, self.peers, self.rs_off, self.rs_flag_off, ws)
@@ -101,6 +119,24 @@ class FusedTP:
 
             out = native.swiglu(out)
         return out
+
+    def _cluster_ok(self, T: int, w: torch.Tensor) -> bool:
+        """Decode-sized gathered GEMMs run as one cluster split-K launch that waits on the shard
+        flags itself (no fp32 workspace, no reduction kernel); ``MB_TP_CLUSTER=1`` turns it on."""
+        return (os.environ.get("MB_TP_CLUSTER", "0") == "1" and 1 <= T <= 128 and w.dtype == torch.bfloat16
+                and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and w.is_contiguous())
+
+    def ag_qkv_rope(self, w, T, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot,
+                    eps) -> bool:
+        """QKV projection of the first T gathered rows with QK-RMSNorm, RoPE and the paged KV write
+        in the cluster GEMM's epilogue.  Returns False where the shape is not covered."""
+        if D != 128 or w.shape[0] != (Hq + 2 * Hkv) * D or not self._cluster_ok(T, w):
+            return False
+        from ..ops import native
+
+        native.qkv_rope_cluster(self.gathered[:T], w, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache,
+                                Hq, Hkv, rot, eps, wait=(self.ag_flags_addr, self.state, self.world))
+        return True
 
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor) -> None:
         """Partial [T, H] = x @ w^T, each row stored once into its owner's slot."""
@@ -122,6 +158,83 @@ class FusedTP:
         self.C.tp_gather_rows(self.peers, self.rank, T // self.world, self.ag_off, self.ag_flag_off, self.state,
                               idx, out)
         return out
+
+
+class NvlsTP(FusedTP):
+    """NVLS flavour of the fused boundaries (``csrc/cuda/tp_nvls.cu``).
+
+    The exchange buffer is symmetric memory bound to an NVLink multicast object
+    (:class:`mod_b200.parallel.symm.SymmetricBuffer`).  The row-parallel GEMM
+    writes its whole partial output into this rank's own ``part`` region (a
+    plain local GEMM); the boundary kernel then reads each owned row with one
+    ``multimem.ld_reduce`` (the NVSwitch sums the ranks' rows), adds the
+    residual, applies the next RMSNorm and writes the normed row into every
+    rank's ``gathered`` buffer with one ``multimem.st``.  The column-parallel
+    GEMMs, the vocabulary-parallel argmax and the row gather are the P2P
+    flavour's, run on the same symmetric buffer's unicast peer addresses.
+
+    Cost per boundary and rank: partial rows leave the GPU once (read by the
+    switch) and normed rows leave once (replicated by the switch), against N-1
+    peer stores of each in the P2P flavour."""
+
+    def __init__(self, hidden: int, max_tokens: int, group=None):
+        from ..ops import load_extension
+        from .symm import SymmetricBuffer
+
+        self.C = load_extension()
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.H = hidden
+        self._set_layout(exchange_layout(hidden, max_tokens, self.world))  # rs region: this rank's partial
+        self.buf = SymmetricBuffer(self.total, group)
+        self.peers = self.buf.peers
+        self.own = self.buf.own
+        self.mc = self.buf.mc
+        self.ag_flags_addr = self.own + self.ag_flag_off
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.state = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.am_state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.gathered = self.C.wrap_bf16(self.own + self.ag_off, self.world * self.cap, hidden)
+
+    def publish(self, residual, norm_w, eps, partials, x_add=None, local_out=None) -> None:
+        self.C.tp_nvls_reduce(self.own, self.mc, self.rank, self.world, partials, residual.shape[0], self.H,
+                              self.ag_off, self.rs_off, self.ag_flag_off, self.rs_flag_off, self.state, x_add,
+                              residual, norm_w, eps, local_out)
+
+    def gemm_rs(self, x: torch.Tensor, w: torch.Tensor) -> None:
+        """This rank's partial [T, H] = x @ w^T into its own ``part`` region (local stores only)."""
+        from ..ops import native
+
+        T = x.shape[0]
+        part = self.C.wrap_bf16(self.own + self.rs_off, T, self.H)
+        if T <= 128 and w.shape[0] % 128 == 0 and x.shape[1] % 64 == 0 and x.stride(1) == 1:
+            native.linear_cluster(x, w, out=part)
+            return
+        ws = None
+        if T <= 256 and w.shape[0] % 128 == 0:
+            splits = 16 if w.shape[0] <= 1024 else 8
+            ws = torch.empty(splits * T * w.shape[0], dtype=torch.float32, device=x.device)
+        native.linear(x, w, out=part, workspace=ws)
+
+    def close(self) -> None:
+        self.buf.close()
+
+
+def make_tp_comm(kind: str, hidden: int, max_tokens: int, group=None):
+    """Boundary implementation by name: ``"p2p"`` (:class:`FusedTP`), ``"nvls"``
+    (:class:`NvlsTP`), ``"nccl"`` (:class:`NcclTP`, the library baseline), or
+    ``"auto"``: NVLS where every rank's device supports multicast, else P2P."""
+    if kind == "auto":
+        from .symm import nvls_supported
+
+        kind = "nvls" if nvls_supported(group) else "p2p"
+    if kind == "nvls":
+        return NvlsTP(hidden, max_tokens, group)
+    if kind == "p2p":
+        return FusedTP(hidden, max_tokens, group)
+    if kind == "nccl":
+        return NcclTP(hidden, max_tokens, group)
+    raise ValueError(f"unknown tensor-parallel boundary flavour {kind!r} (p2p, nvls, nccl, auto)")
 
 
 class NcclTP:

@@ -96,14 +96,34 @@ def test_tp_baseline_gloo_matches_single(world):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("backend", ["native", "torch"])
-def test_tp_multi_gpu(cuda, backend):
+@pytest.mark.parametrize("backend,cluster", [("native", "0"), ("native", "1"), ("torch", "0")])
+def test_tp_multi_gpu(cuda, backend, cluster):
+    """cluster=1: decode-sized gathered GEMMs (QKV with the RoPE/KV-write epilogue) as cluster
+    launches that wait on the shard flags themselves."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs")
     n = min(n, 8)  # every visible GPU (up to 8)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MB_TP_CLUSTER=cluster)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), backend]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+def test_tp_nvls_multi_gpu(cuda):
+    """NVLS boundaries (multimem reduce + multicast stores) reproduce the single-process engine."""
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    from mod_b200.ops import load_extension
+
+    if not all(load_extension().multicast_supported(d) for d in range(n)):
+        pytest.skip("no NVLink multicast on these devices")
+    n = min(n, 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MB_TP_COMM="nvls")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), "native"]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

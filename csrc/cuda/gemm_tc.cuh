@@ -257,7 +257,8 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, DUAL, W8>::kThreads, 1)
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(args.tp.ag_flags + p) : "memory");
             if ((int32_t)(v - want) >= 0) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            // half the limit: the other warps' bounded mbarrier waits started with this one
+            if (globaltimer_ns() - t0 > kWaitLimitNs / 2) {
               set_status(args.status, kErrPeerTimeout);
               break;
             }

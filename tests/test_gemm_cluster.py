@@ -73,3 +73,36 @@ def test_linear_cluster_w8_matches_fp32(cuda, T, K, N):
     ref = x.float() @ (qw.q.float() * qw.scale[:, None]).t() + res.float()
     torch.cuda.synchronize()
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * max(1.0, ref.abs().max().item()) / 8)
+
+
+def test_linear_cluster_flag_wait(cuda):
+    """The tensor-parallel form: x is a gathered buffer and the producer waits on per-rank
+    flags.  Flags already at the epoch: same result as without the wait.  A flag that never
+    arrives: the bounded wait gives up (about 1 s), records a status code, and the context
+    stays usable."""
+    import time
+
+    from mod_b200.ops import check_status, native
+
+    check_status()
+    torch.manual_seed(5)
+    T, K, N, ranks = 16, 2048, 1024, 4
+    x = torch.randn(T, K, device=cuda).bfloat16()
+    w = (torch.randn(N, K, device=cuda) * 0.02).bfloat16()
+    state = torch.zeros(8, dtype=torch.int32, device=cuda)
+    state[0] = 3                                            # boundary epoch
+    flags = torch.full((ranks,), 3, dtype=torch.int32, device=cuda)
+    y = native.linear_cluster(x, w, wait=(flags.data_ptr(), state, ranks))
+    ref = native.linear_cluster(x, w)
+    torch.cuda.synchronize()
+    check_status()
+    torch.testing.assert_close(y, ref, rtol=0, atol=0)
+    flags[2] = 2                                            # rank 2 never publishes this boundary
+    t0 = time.time()
+    native.linear_cluster(x, w, wait=(flags.data_ptr(), state, ranks))
+    torch.cuda.synchronize()
+    assert 0.5 < time.time() - t0 < 30.0
+    with pytest.raises(RuntimeError, match="peer flag wait timed out"):
+        check_status()
+    torch.testing.assert_close(native.linear_cluster(x, w), ref, rtol=0, atol=0)
+    check_status()

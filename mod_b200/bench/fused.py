@@ -28,6 +28,7 @@ Peaks come from ``MEASURED_PEAKS.json`` when present (else 6.65 TB/s and
 from __future__ import annotations
 
 import argparse
+import os
 import json
 
 import torch
@@ -150,11 +151,12 @@ def case_ep(iters, rank, world, dev):
     return out
 
 
-def case_tp(iters, rank, world, dev):
-    from ..parallel.tp import FusedTP, NcclTP, padded_tokens
+def case_tp(iters, rank, world, dev, tokens=64):
+    from ..parallel.symm import nvls_supported
+    from ..parallel.tp import FusedTP, NcclTP, NvlsTP, padded_tokens
 
     H, Hq, Hkv, D, I = 4096, 32, 8, 128, 12288
-    T = padded_tokens(64, world)
+    T = padded_tokens(tokens, world)
     pr = T // world
     bf = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(200 + rank)
@@ -171,8 +173,20 @@ def case_tp(iters, rank, world, dev):
     # two all-gathers (this shard to every peer) and two reduce-scatters (partials of the peers' rows)
     nvl = 2 * pr * H * 2 * (world - 1) + 2 * (T - pr) * H * 2
     out = []
-    impls = [("fused", FusedTP(H, T))] + ([("nccl_baseline", NcclTP(H, T))] if world > 1 else [])
+    # fused = P2P flavour; +cluster: decode-sized gathered GEMMs as cluster launches (MB_TP_CLUSTER=1);
+    # nvls = multimem reduce + multicast stores (where every rank's device has NVLink multicast)
+    impls = [("fused", FusedTP(H, T))]
+    if T <= 128:
+        impls.append(("fused+cluster", impls[0][1]))
+    if world > 1 and nvls_supported():
+        nv = NvlsTP(H, T)
+        impls.append(("nvls", nv))
+        if T <= 128:
+            impls.append(("nvls+cluster", nv))
+    if world > 1:
+        impls.append(("nccl_baseline", NcclTP(H, T)))
     for impl, comm in impls:
+        os.environ["MB_TP_CLUSTER"] = "1" if impl.endswith("+cluster") else "0"
         def layer():
             comm.ag_gemm(w_qkv, T)
             comm.gemm_rs(attn, w_o)
@@ -181,7 +195,8 @@ def case_tp(iters, rank, world, dev):
             comm.gemm_rs(h, w_dn)
             comm.publish(resid, nw, 1e-6, partials=True)
         comm.publish(resid, nw, 1e-6, partials=False)
-        us = _time(layer, iters if impl == "fused" else max(5, iters // 5), graph=impl == "fused")
+        fused = impl != "nccl_baseline"
+        us = _time(layer, iters if fused else max(5, iters // 5), graph=fused)
         out.append(_line("tp_layer_boundaries", impl, us, flops, hbm, nvl, world, {"tokens": T}))
     from ..ops import check_status
 
@@ -193,6 +208,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="ep,tp")
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--tp-tokens", default="64", help="comma-separated token counts of the TP case")
     ap.add_argument("--profile", action="store_true", help="per-kernel table of each timed path (rank 0)")
     a = ap.parse_args(argv)
     PROFILE["on"] = a.profile
@@ -202,7 +218,10 @@ def main(argv=None):
     dev = torch.device("cuda", info.local_rank)
     torch.cuda.set_device(dev)
     for c in a.case.split(","):
-        recs = {"ep": case_ep, "tp": case_tp}[c](a.iters, info.rank, info.world, dev)
+        if c == "tp":
+            recs = [r for n in a.tp_tokens.split(",") for r in case_tp(a.iters, info.rank, info.world, dev, int(n))]
+        else:
+            recs = case_ep(a.iters, info.rank, info.world, dev)
         if info.rank == 0:
             for r in recs:
                 print(json.dumps(r), flush=True)

@@ -22,7 +22,7 @@ import torch.distributed as dist
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--impl", default="native", choices=["native", "baseline"])
-    ap.add_argument("--comm", default="p2p", choices=["p2p", "nvls", "auto"],
+    ap.add_argument("--comm", default="auto", choices=["p2p", "nvls", "auto"],
                     help="layer-boundary flavour of the native path")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=1024)
@@ -83,7 +83,7 @@ def main(argv=None):
         check_status(dev)
     if rank == 0:
         print(json.dumps({"config": f"{a.model} TP={world}", "impl": a.impl,
-                          "comm": a.comm if a.impl == "native" else "nccl", "batch": a.batch,
+                          "comm": type(getattr(eng.model, "comm", None)).__name__, "batch": a.batch,
                           "prompt_len": a.prompt_len, "ttft_p50_s": round(p50, 4), "decode_ms_per_step": round(ms, 3),
                           "decode_tok_s": round(a.batch / ms * 1000, 1),
                           "timed": "graph replay" if B is not None else "eager engine steps"}), flush=True)

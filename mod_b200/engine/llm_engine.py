@@ -62,9 +62,10 @@ class LLMEngine:
         experts); ``"auto"`` takes N
         from the placement planner for this device's memory.  Streaming runs
         eagerly (no decode graphs).  ``tp_comm`` (tensor parallelism, native
-        backend): the layer-boundary flavour, ``"p2p"`` (peer stores, the
-        default), ``"nvls"`` (NVSwitch multimem reduce + multicast stores) or
-        ``"auto"``; the ``MB_TP_COMM`` environment variable sets the default."""
+        backend): the layer-boundary flavour, ``"p2p"`` (peer stores),
+        ``"nvls"`` (NVSwitch multimem reduce + multicast stores) or ``"auto"``
+        (the default: NVLS where every rank's device has NVLink multicast, else
+        P2P); the ``MB_TP_COMM`` environment variable sets the default."""
         import torch.distributed as dist
 
         self.cfg = cfg
@@ -98,7 +99,7 @@ class LLMEngine:
             weights = None
             mt = max(max_batch, max_prefill_tokens)
             # boundary flavour: P2P peer stores (default), NVLS multimem, or the NCCL baseline
-            kind = tp_comm or os.environ.get("MB_TP_COMM", "p2p")
+            kind = tp_comm or os.environ.get("MB_TP_COMM", "auto")
             comm = make_tp_comm(kind if backend == "native" else "nccl", cfg.hidden_size, mt)
             model = TPDecoderLM(cfg, shard, self.backend, comm, world)
             kv_heads = model.Hkv

@@ -122,8 +122,8 @@ class FusedTP:
 
     def _cluster_ok(self, T: int, w: torch.Tensor) -> bool:
         """Decode-sized gathered GEMMs run as one cluster split-K launch that waits on the shard
-        flags itself (no fp32 workspace, no reduction kernel); ``MB_TP_CLUSTER=1`` turns it on."""
-        return (os.environ.get("MB_TP_CLUSTER", "0") == "1" and 1 <= T <= 128 and w.dtype == torch.bfloat16
+        flags itself (no fp32 workspace, no reduction kernel); ``MB_TP_CLUSTER=0`` turns it off."""
+        return (os.environ.get("MB_TP_CLUSTER", "1") != "0" and 1 <= T <= 128 and w.dtype == torch.bfloat16
                 and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and w.is_contiguous())
 
     def ag_qkv_rope(self, w, T, q_w, k_w, positions, inv_freq, slots, q_out, k_cache, v_cache, Hq, Hkv, D, rot,

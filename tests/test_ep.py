@@ -104,7 +104,7 @@ def test_tp_multi_gpu(cuda, backend, cluster):
     if n < 2:
         pytest.skip("needs 2 GPUs")
     n = min(n, 8)  # every visible GPU (up to 8)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MB_TP_CLUSTER=cluster)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MB_TP_CLUSTER=cluster, MB_TP_COMM="p2p")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), backend]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)

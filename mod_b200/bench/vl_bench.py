@@ -24,6 +24,8 @@ import torch.distributed as dist
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--impl", default="native", choices=["native", "baseline"])
+    ap.add_argument("--comm", default="auto", choices=["p2p", "nvls", "auto"],
+                    help="layer-boundary flavour of the native path")
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--text-len", type=int, default=64)
     ap.add_argument("--image-size", type=int, default=448)
@@ -37,7 +39,7 @@ def main(argv=None):
     from ..models.tp_decoder import shard_weights
     from ..models.vl import TPVLModel, VLModel, random_vl_weights
     from ..parallel import dist as mdist
-    from ..parallel.tp import FusedTP, FusedVisionExchange, NcclTP, NcclVisionExchange
+    from ..parallel.tp import FusedVisionExchange, NcclVisionExchange, make_tp_comm
 
     info = mdist.init()
     world, rank = info.world, info.rank
@@ -52,7 +54,7 @@ def main(argv=None):
     max_tokens = a.batch * (per_img + a.text_len)
     if world > 1:
         H = cfg.text.hidden_size
-        comm = FusedTP(H, max_tokens) if backend == "native" else NcclTP(H, max_tokens)
+        comm = make_tp_comm(a.comm if backend == "native" else "nccl", H, max_tokens)
         vx = FusedVisionExchange(H, max_tokens) if backend == "native" else NcclVisionExchange(be)
         model = TPVLModel(cfg, shard_weights(cfg.text, tw, rank, world), vw, be, comm, world, vx,
                           image_size=a.image_size)

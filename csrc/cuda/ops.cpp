@@ -85,10 +85,19 @@ void tp_reduce(const at::Tensor& peers, int64_t rank, bool with_partials, int64_
 void tp_argmax_exchange(const at::Tensor& peers, int64_t rank, int64_t cap, int64_t slot_off, int64_t flag_off,
                         at::Tensor& state, const at::Tensor& vals, const at::Tensor& idxs, at::Tensor& out);
 void tp_nvls_reduce(int64_t self, int64_t mc, int64_t rank, int64_t nranks, bool with_partials, int64_t rows,
-                    int64_t H, int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off,
+                    int64_t row_stride, bool publish, int64_t H, int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off,
                     at::Tensor& state, const c10::optional<at::Tensor>& x_add, at::Tensor& residual,
                     const at::Tensor& w, double eps, const c10::optional<at::Tensor>& local_out);
 bool multicast_supported(int64_t device);
+void ep_agrs_publish(int64_t self, int64_t mc, int64_t rank, int64_t N, int64_t cap, int64_t K, int64_t El,
+                     const at::Tensor& offsets, at::Tensor& state, const at::Tensor& x, const at::Tensor& logits,
+                     bool renorm);
+void ep_agrs_place(int64_t self, int64_t mc, int64_t rank, int64_t N, int64_t cap, int64_t K, int64_t El,
+                   int64_t H, const at::Tensor& offsets, at::Tensor& state, at::Tensor& xs, at::Tensor& slot_of,
+                   at::Tensor& offs, int64_t grid);
+void ep_agrs_combine(int64_t self, int64_t mc, int64_t rank, int64_t N, int64_t cap, int64_t K, int64_t El,
+                     int64_t H, const at::Tensor& offsets, at::Tensor& state, const at::Tensor& slot_of,
+                     const at::Tensor& y);
 void tp_gather_rows(const at::Tensor& peers, int64_t rank, int64_t peer_rows, int64_t ag_off, int64_t ag_flag_off,
                     at::Tensor& state, const at::Tensor& idx, at::Tensor& out);
 std::tuple<int64_t, std::string> ipc_alloc(int64_t bytes);
@@ -171,6 +180,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_argmax_exchange", &mb::tp_argmax_exchange);
   m.def("tp_nvls_reduce", &mb::tp_nvls_reduce);
   m.def("multicast_supported", &mb::multicast_supported);
+  m.def("ep_agrs_publish", &mb::ep_agrs_publish);
+  m.def("ep_agrs_place", &mb::ep_agrs_place);
+  m.def("ep_agrs_combine", &mb::ep_agrs_combine);
   m.def("ipc_alloc", [](int64_t b) {
     auto r = mb::ipc_alloc(b);
     return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));

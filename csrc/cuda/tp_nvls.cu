@@ -35,44 +35,18 @@
 
 #include "common.cuh"
 #include "launch.cuh"
+#include "multimem.cuh"
 #include "status.h"
 
 namespace mb {
 
-namespace {
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void mc_store_release_u32(uint64_t mc_addr, uint32_t v) {
-  asm volatile("multimem.st.release.sys.global.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
-}
-
-// Sum over every replica of 8 bf16 at mc_addr, accumulated in fp32 by the switch.
-__device__ __forceinline__ uint4 mc_ld_reduce_bf16x8(uint64_t mc_addr) {
-  uint4 r;
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(mc_addr)
-               : "memory");
-  return r;
-}
-
-// 16 bytes to every replica.
-__device__ __forceinline__ void mc_store_16(uint64_t mc_addr, uint4 v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc_addr), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
-}
-
-}  // namespace
-
+// row_stride: rows between two ranks' blocks in part / gathered (the TP layout packs them, stride = rows; the
+// expert-parallel layout keeps a fixed per-rank capacity).  publish = 0: the normed row stays local (local_out)
+// and no all-gather flag is released.  rows == 0 launches one CTA that only announces and waits, so the peers'
+// waits are met.
 __global__ void __launch_bounds__(1024)
-    tp_nvls_reduce_kernel(uint64_t self, uint64_t mc, int rank, int nranks, int with_partials, int rows, int H,
-                          int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off, uint32_t* epoch,
+    tp_nvls_reduce_kernel(uint64_t self, uint64_t mc, int rank, int nranks, int with_partials, int rows,
+                          int row_stride, int publish, int H, int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off, uint32_t* epoch,
                           int* done, const __nv_bfloat16* __restrict__ x_add, __nv_bfloat16* __restrict__ residual,
                           const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* __restrict__ local_out,
                           int* status) {
@@ -93,7 +67,7 @@ __global__ void __launch_bounds__(1024)
     const uint32_t* rf = reinterpret_cast<const uint32_t*>(self + rs_flag_off);
     for (int p = tid; p < nranks; p += blockDim.x) {
       const uint64_t t0 = globaltimer_ns();
-      while ((int32_t)(ld_acquire_sys(rf + p) - ne) < 0) {
+      while ((int32_t)(ld_acquire_sys_u32(rf + p) - ne) < 0) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           set_status(status, kErrPeerTimeout);
           ok_all = 0;
@@ -106,8 +80,9 @@ __global__ void __launch_bounds__(1024)
   } else {
     __syncthreads();
   }
+  if (t < rows) {
   const size_t off = (size_t)t * H + col;
-  const size_t grow = (size_t)rank * rows + t;  // this row's index in part / gathered
+  const size_t grow = (size_t)rank * row_stride + t;  // this row's index in part / gathered
   uint4 sum = make_uint4(0, 0, 0, 0);
   if (with_partials && ok_all) sum = mc_ld_reduce_bf16x8(mc + part_off + (grow * H + col) * 2);
   const uint4 rr = *reinterpret_cast<const uint4*>(residual + off);
@@ -135,8 +110,9 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
   for (int q = 0; q < 8; ++q)
     o[q] = __float2bfloat16(v[q] * inv * __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&wr)[q]));
-  mc_store_16(mc + ag_off + (grow * H + col) * 2, *reinterpret_cast<const uint4*>(o));
+  if (publish) mc_store_16(mc + ag_off + (grow * H + col) * 2, *reinterpret_cast<const uint4*>(o));
   if (local_out) *reinterpret_cast<uint4*>(local_out + off) = *reinterpret_cast<const uint4*>(o);
+  }
   // CTA barrier, one system-scope fence + arrive per CTA; the last CTA publishes
   __syncthreads();
   if (tid == 0) {
@@ -147,14 +123,14 @@ __global__ void __launch_bounds__(1024)
   if (!last) return;
   if (tid == 0) {
     __threadfence_system();
-    mc_store_release_u32(mc + ag_flag_off + 4ull * rank, ne);
+    if (publish) mc_store_release_u32(mc + ag_flag_off + 4ull * rank, ne);
     *epoch = ne;
     *done = 0;
   }
 }
 
 void tp_nvls_reduce(int64_t self, int64_t mc, int64_t rank, int64_t nranks, bool with_partials, int64_t rows,
-                    int64_t H, int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off,
+                    int64_t row_stride, bool publish, int64_t H, int64_t ag_off, int64_t part_off, int64_t ag_flag_off, int64_t rs_flag_off,
                     at::Tensor& state, const c10::optional<at::Tensor>& x_add, at::Tensor& residual,
                     const at::Tensor& w, double eps, const c10::optional<at::Tensor>& local_out) {
   TORCH_CHECK(H % 256 == 0 && H / 8 <= 1024, "tp_nvls_reduce: hidden size must be a multiple of 256 (<= 8192)");
@@ -171,10 +147,14 @@ void tp_nvls_reduce(int64_t self, int64_t mc, int64_t rank, int64_t nranks, bool
     TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous());
     return reinterpret_cast<__nv_bfloat16*>(t->data_ptr());
   };
-  if (rows == 0) return;
+  if (row_stride <= 0) row_stride = rows;
+  TORCH_CHECK(rows <= row_stride, "tp_nvls_reduce: ", rows, " rows exceed the per-rank stride ", row_stride);
+  TORCH_CHECK((local_out && local_out->defined()) || publish, "tp_nvls_reduce: the normed rows must go somewhere");
+  if (rows == 0 && !with_partials) return;  // nothing to publish and nothing to announce
   int* s = state.data_ptr<int>();
-  launch_k(tp_nvls_reduce_kernel, (int)rows, (int)(H / 8), 0, at::cuda::getCurrentCUDAStream(), (uint64_t)self,
-           (uint64_t)mc, (int)rank, (int)nranks, with_partials ? 1 : 0, (int)rows, (int)H, ag_off, part_off,
+  launch_k(tp_nvls_reduce_kernel, (int)std::max<int64_t>(rows, 1), (int)(H / 8), 0, at::cuda::getCurrentCUDAStream(),
+           (uint64_t)self, (uint64_t)mc, (int)rank, (int)nranks, with_partials ? 1 : 0, (int)rows, (int)row_stride,
+           publish ? 1 : 0, (int)H, ag_off, part_off,
            ag_flag_off, rs_flag_off, reinterpret_cast<uint32_t*>(s), s + 5, (const __nv_bfloat16*)bf(x_add),
            reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
            (float)eps, bf(local_out), status_ptr(residual.device().index()));

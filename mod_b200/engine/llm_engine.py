@@ -121,6 +121,14 @@ class LLMEngine:
             moe_impl = (FusedEPMoE(cfg, self.backend, max_tokens=max_batch,
                                    prefill_tokens=max(max_batch, min(2048, max_prefill_tokens)))
                         if backend == "native" else NcclEPMoE(cfg, self.backend, max_tokens=max_batch))
+            if backend == "native" and os.environ.get("MB_EP_COMM", "p2p") == "agrs":
+                # decode steps as NVLS all-gather -> local experts -> in-switch reduce (opt-in);
+                # prefill and uncovered blocks keep the point-to-point exchange
+                from ..parallel.ep_agrs import AgRsEPMoE
+                from ..parallel.symm import nvls_supported
+
+                if nvls_supported():
+                    moe_impl = AgRsEPMoE(cfg, self.backend, max_tokens=max_batch, fallback=moe_impl)
         elif (backend == "native" and cfg.is_moe and world == 1 and model is None and self.device.type == "cuda"
               and quantization in (None, "none") and not cfg.shared_expert_intermediate_size
               and os.environ.get("MB_MOE_FUSED", "0") == "1"):

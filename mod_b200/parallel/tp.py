@@ -197,7 +197,7 @@ class NvlsTP(FusedTP):
         self.gathered = self.C.wrap_bf16(self.own + self.ag_off, self.world * self.cap, hidden)
 
     def publish(self, residual, norm_w, eps, partials, x_add=None, local_out=None) -> None:
-        self.C.tp_nvls_reduce(self.own, self.mc, self.rank, self.world, partials, residual.shape[0], self.H,
+        self.C.tp_nvls_reduce(self.own, self.mc, self.rank, self.world, partials, residual.shape[0], 0, True, self.H,
                               self.ag_off, self.rs_off, self.ag_flag_off, self.rs_flag_off, self.state, x_add,
                               residual, norm_w, eps, local_out)
 

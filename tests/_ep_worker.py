@@ -37,6 +37,10 @@ def run(rank, world, impl, port, device_kind):
     ref = make_backend("torch").moe(x, full.layers[0].moe, cfg.num_experts_per_tok, True, cfg.moe_intermediate_size)
     if impl == "nccl":
         moe = NcclEPMoE(cfg, be)
+    elif impl == "agrs":  # NVLS all-gather -> local experts -> in-switch reduce; the P2P path as fallback
+        from mod_b200.parallel.ep_agrs import AgRsEPMoE
+
+        moe = AgRsEPMoE(cfg, be, max_tokens=32, fallback=FusedEPMoE(cfg, be, max_tokens=16))
     else:
         moe = FusedEPMoE(cfg, be, max_tokens=16)
     scale = ref.float().abs().max().item()
@@ -52,12 +56,12 @@ def run(rank, world, impl, port, device_kind):
             out = moe(x, shard.layers[0].moe)
             err = (out.float() - ref.float()).abs().max().item()
             assert err < tol * scale, f"rank {rank} rep {rep} fused_route={fused_route}: max err {err} vs scale {scale}"
-    if impl == "fused":
+    if impl in ("fused", "agrs"):
         # combine deferred into the next residual add + RMSNorm
         from mod_b200.ops import reference as R
 
         nw = (1.0 + 0.1 * torch.randn(cfg.hidden_size, device=dev)).to(dtype)
-        for rep in range(2):
+        for rep in range(4 if impl == "agrs" else 2):
             res = (torch.randn(T, cfg.hidden_size, device=dev) * 0.5).to(dtype)
             res_ref = res.clone()
             want = R.rmsnorm(ref.to(dtype), nw, 1e-6, residual=res_ref)

@@ -42,11 +42,17 @@ def test_fused_ep_single_gpu_self_exchange(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("impl", ["fused", "nccl"])
+@pytest.mark.parametrize("impl", ["fused", "nccl", "agrs"])
 def test_ep_multi_gpu(cuda, impl):
+    """agrs: NVLS all-gather -> local experts -> in-switch reduce (needs NVLink multicast)."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs")
+    if impl == "agrs":
+        from mod_b200.ops import load_extension
+
+        if not all(load_extension().multicast_supported(d) for d in range(n)):
+            pytest.skip("no NVLink multicast on these devices")
     n = min(n, 8)  # every visible GPU (up to 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",

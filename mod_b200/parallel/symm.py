@@ -24,7 +24,7 @@ import torch.distributed as dist
 def nvls_supported(group=None) -> bool:
     """True when every rank of ``group`` is a CUDA device with multicast support
     (symmetric memory importable and the driver reporting multicast)."""
-    if not torch.cuda.is_available() or not dist.is_initialized():
+    if not torch.cuda.is_available() or not dist.is_initialized() or dist.get_backend(group) != "nccl":
         return False
     try:
         importlib.import_module("torch.distributed._symmetric_memory")

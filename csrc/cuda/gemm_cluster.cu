@@ -49,7 +49,7 @@ CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dt, int64_t rows,
 
 namespace {
 
-enum ClusterEpi : int { kCStore = 0, kCQkvRope = 1 };
+enum ClusterEpi : int { kCStore = 0, kCQkvRope = 1, kCSwiGLU = 2 };
 
 struct ClusterArgs {
   int K, N, T;            // reduction length, output features, tokens
@@ -76,6 +76,9 @@ struct ClusterArgs {
   const uint32_t* ag_flags;
   const uint32_t* ag_epoch;
   int ag_nranks;
+  // kCSwiGLU: w = [gate; up] ([2I, K]); m tile i holds gate rows [64i, 64i+64) in its first 64 rows and
+  // up rows [up_row0 + 64i, ...) in its last 64 (two TMA boxes of 64 rows), and produces outputs [64i, 64i+64)
+  int up_row0;
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -166,9 +169,18 @@ __global__ void __launch_bounds__(192, 1)
     if (elect_one_sync()) {
       // weight tiles of the first stages go out before the dependency wait (weights are immutable)
       const int pre = min(STAGES, kbs);
+      // the weight (A) tile of K block kb: one 128-row box, or (SwiGLU) 64 gate rows + the matching 64 up rows
+      auto load_a = [&](uint8_t* dst, uint64_t* bar, int kb) {
+        if (args.mode == kCSwiGLU) {
+          tma_load_2d(dst, &tmA, bar, kb * 64, m_tile * 64);
+          tma_load_2d(dst + (W8 ? 64 * 64 : 64 * 128), &tmA, bar, kb * 64, args.up_row0 + m_tile * 64);
+        } else {
+          tma_load_2d(dst, &tmA, bar, kb * 64, m_tile * 128);
+        }
+      };
       for (int s = 0; s < pre; ++s) {
         mbar_arrive_expect_tx(&full[s], L::kTx);
-        tma_load_2d(smem + s * L::kStage + (W8 ? L::kRawOff : 0), &tmA, &full[s], (kb_lo + s) * 64, m_tile * 128);
+        load_a(smem + s * L::kStage + (W8 ? L::kRawOff : 0), &full[s], kb_lo + s);
       }
       pdl_wait();
       pdl_trigger();
@@ -197,7 +209,7 @@ __global__ void __launch_bounds__(192, 1)
         if (it >= pre) {
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, args.status)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], L::kTx);
-          tma_load_2d(st + (W8 ? L::kRawOff : 0), &tmA, &full[s], (kb_lo + it) * 64, m_tile * 128);
+          load_a(st + (W8 ? L::kRawOff : 0), &full[s], kb_lo + it);
         }
         tma_load_2d(st + L::kABytes, &tmB, &full[s], (kb_lo + it) * 64, 0);
       }
@@ -296,6 +308,13 @@ __global__ void __launch_bounds__(192, 1)
         args.out[o] = __float2bfloat16(acc);
         continue;
       }
+      if (args.mode == kCSwiGLU) {  // feature f < 64 is a gate, f + 64 its up: out = silu(gate) * up
+        rot[f] = acc;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (f < 64) args.out[(size_t)j * args.ldc + (size_t)m_tile * 64 + f] = __float2bfloat16(silu(acc) * rot[f + 64]);
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // rot[] is reused by the next token
+        continue;
+      }
       // kCQkvRope: this tile is head h of the packed [q | k | v] projection
       const int h = m_tile;
       const bool is_q = h < args.Hq, is_k = !is_q && h < args.Hq + args.Hkv;
@@ -390,11 +409,13 @@ void run(const at::Tensor& x, const at::Tensor& w, ClusterArgs a, int64_t cs_req
   const int64_t T = x.size(0), K = x.size(1), N = w.size(0);
   const bool w8 = w.scalar_type() == at::kChar;
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
-  auto ta = w8 ? make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, w.stride(0), 64, 128,
+  const bool sw = a.mode == kCSwiGLU;   // 64-row boxes, one m tile per 64 outputs
+  const int box = sw ? 64 : 128;
+  auto ta = w8 ? make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, w.stride(0), 64, box,
                               CU_TENSOR_MAP_SWIZZLE_NONE)
-               : make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), 128);
+               : make_tmap_bf16(w.data_ptr(), N, K, w.stride(0), box);
   auto tb = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), bn);
-  const int m_tiles = (int)(N / 128);
+  const int m_tiles = (int)(sw ? N / 2 / 64 : N / 128);
   const int kb_total = (int)((K + 63) / 64);
   int cs = cs_req > 0 ? (int)cs_req : pick_cs(m_tiles, kb_total, sm_count(x.device().index()));
   TORCH_CHECK(cs == 1 || cs == 2 || cs == 4 || cs == 8, "gemm_cluster: cluster size must be 1, 2, 4 or 8");
@@ -461,6 +482,29 @@ void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
     TORCH_CHECK(residual->is_contiguous() && residual->sizes() == y.sizes());
     a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
   }
+  set_wait(a, ag_flags, state, nranks);
+  run(x, w, a, cs);
+}
+
+// y[T, I] = silu(x @ gate^T) * (x @ up^T), w = [gate; up] ([2I, K], I % 64 == 0), decode-sized T;
+// one launch (the split-K partials of gate and up are reduced through DSMEM, SwiGLU in the epilogue).
+// ag_flags / state / nranks: as in linear_cluster.
+void swiglu_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, int64_t cs, int64_t ag_flags,
+                    const c10::optional<at::Tensor>& state, int64_t nranks) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "swiglu_cluster: bf16 operands");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.is_contiguous() && w.size(1) == x.size(1));
+  TORCH_CHECK(x.size(0) >= 1 && x.size(0) <= 128, "swiglu_cluster: 1..128 tokens");
+  const int64_t I = w.size(0) / 2;
+  TORCH_CHECK(w.size(0) % 128 == 0 && I % 64 == 0 && x.size(1) % 64 == 0,
+              "swiglu_cluster: w must be [2I, K] with I % 64 == 0 and K % 64 == 0");
+  TORCH_CHECK(y.is_contiguous() && y.scalar_type() == at::kBFloat16 && y.size(0) == x.size(0) && y.size(1) == I);
+  c10::cuda::CUDAGuard guard(x.device());
+  ClusterArgs a{};
+  a.mode = kCSwiGLU;
+  a.out = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.ldc = (int)I;
+  a.up_row0 = (int)I;
   set_wait(a, ag_flags, state, nranks);
   run(x, w, a, cs);
 }

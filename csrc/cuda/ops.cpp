@@ -116,6 +116,8 @@ void ep_combine_norm(const at::Tensor& peers, at::Tensor& state, int64_t rank, i
 void linear_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
                     const c10::optional<at::Tensor>& residual, int64_t cs, int64_t ag_flags,
                     const c10::optional<at::Tensor>& state, int64_t nranks);
+void swiglu_cluster(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, int64_t cs, int64_t ag_flags,
+                    const c10::optional<at::Tensor>& state, int64_t nranks);
 void linear_cluster_w8(const at::Tensor& x, const at::Tensor& wq, const at::Tensor& scale, at::Tensor& y,
                        const c10::optional<at::Tensor>& residual, int64_t cs);
 void qkv_rope_cluster(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& q_w,
@@ -138,6 +140,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mod_b200 sm_100a kernels";
   m.def("linear", &mb::linear);
   m.def("linear_cluster", &mb::linear_cluster);
+  m.def("swiglu_cluster", &mb::swiglu_cluster);
   m.def("qkv_rope_cluster", &mb::qkv_rope_cluster);
   m.def("linear_cluster_w8", &mb::linear_cluster_w8);
   m.def("grouped_linear", &mb::grouped_linear);

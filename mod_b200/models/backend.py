@@ -11,6 +11,7 @@ the ctypes ``Tensor`` method table (``pio/core/engine/backend.py:332-654``).
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -87,8 +88,6 @@ class NativeBackend:
         load_extension()
         self.N = N
         self._one_group = {}
-        import os
-
         # MB_CLUSTER_GEMM=0 keeps decode GEMMs on the split-K + reduction kernels (A/B timing)
         self.cluster_gemm = os.environ.get("MB_CLUSTER_GEMM", "1") != "0"
         # int8 weights on the cluster kernel are opt-in (MB_CLUSTER_W8=1): its in-loop expansion measured
@@ -170,6 +169,9 @@ class NativeBackend:
                 h = self.N.linear_w8(x2, gate_up.q, gate_up.scale, workspace=ws, swiglu=True)
             else:
                 h = self.N.swiglu(self.linear(x2, gate_up))
+        elif (T <= 128 and I % 64 == 0 and x2.shape[1] % 64 == 0 and gate_up.is_contiguous()
+              and os.environ.get("MB_SWIGLU_CLUSTER", "0") == "1"):
+            h = self.N.swiglu_cluster(x2, gate_up)   # one cluster launch (opt-in until measured)
         elif I % 128 == 0 and T <= 256:
             h = self.N.swiglu_linear(x2, gate_up)
         elif I % 128 == 0:
@@ -195,8 +197,6 @@ class NativeBackend:
     def attn_decode(self, q, k_cache, v_cache, block_tables, ctx_lens, splits=1):
         B, Hq, D = q.shape
         tc = self.N.attn_decode_tc_supported(D, Hq // k_cache.shape[1])
-        import os
-
         impl = os.environ.get("MB_ATTN_IMPL", "tc")  # A/B timing: "cuda" forces the CUDA-core kernel
         tc = tc and impl != "cuda"
         dynamic = os.environ.get("MB_ATTN_DYNAMIC", "1") != "0"

@@ -49,6 +49,18 @@ def linear_cluster(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]
     return out
 
 
+def swiglu_cluster(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, cs: int = 0,
+                   wait=None) -> torch.Tensor:
+    """``silu(x @ gate^T) * (x @ up^T)``, w = [gate; up] ([2I, K], I % 64 == 0), for decode-sized
+    x (1..128 rows): one cluster split-K launch whose tiles pair 64 gate rows with the matching
+    64 up rows, SwiGLU applied after the DSMEM reduction.  ``wait``: as in :func:`linear_cluster`."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0] // 2, dtype=x.dtype, device=x.device)
+    flags, state, nranks = wait if wait is not None else (0, None, 0)
+    _C().swiglu_cluster(x, w, out, cs, flags, state, nranks)
+    return out
+
+
 def linear_cluster_w8(x: torch.Tensor, wq: torch.Tensor, scale: torch.Tensor, out: Optional[torch.Tensor] = None,
                       residual: Optional[torch.Tensor] = None, cs: int = 0) -> torch.Tensor:
     """int8 weight-only ``out = (x @ wq.T) * scale (+ residual)`` for decode-sized x: the cluster

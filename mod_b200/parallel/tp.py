@@ -100,6 +100,11 @@ class FusedTP:
     def ag_gemm(self, w: torch.Tensor, T: int, swiglu: bool = False) -> torch.Tensor:
         """[T, N_out] = gathered activations @ w^T (w: [N_out, H] or [2*N_out, H] for SwiGLU)."""
         n_out = w.shape[0] // 2 if swiglu else w.shape[0]
+        if (swiglu and os.environ.get("MB_SWIGLU_CLUSTER", "0") == "1" and 1 <= T <= 128 and n_out % 64 == 0
+                and w.shape[1] % 64 == 0 and w.is_contiguous() and w.dtype == torch.bfloat16):
+            from ..ops import native
+
+            return native.swiglu_cluster(self.gathered[:T], w, wait=(self.ag_flags_addr, self.state, self.world))
         fused_swiglu = swiglu and T <= 256 and n_out % 128 == 0
         cols = n_out if fused_swiglu else w.shape[0]
         out = torch.empty(T, cols, dtype=torch.bfloat16, device=w.device)

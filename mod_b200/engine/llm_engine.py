@@ -218,6 +218,10 @@ class LLMEngine:
         # optional ``parallel.health.Heartbeat``: checked before every step so a lost
         # peer raises ``RankFailure`` here instead of stalling the next exchange
         self.health = None
+        # expert parallelism with data-parallel attention: every rank takes part in every MoE
+        # exchange, so the ranks step together (see ``_ep_step``)
+        self._ep_lockstep = self.expert_parallel and world > 1 and moe_impl is not None
+        self._ep_all_done = False
 
     @classmethod
     def from_preset(cls, name: str, **kw) -> "LLMEngine":
@@ -315,17 +319,62 @@ class LLMEngine:
         return self.scheduler.has_work()
 
     def step(self) -> List[Sequence]:
-        """Runs one prefill or decode step; returns sequences that finished in it."""
+        """Runs one prefill or decode step; returns sequences that finished in it.
+
+        Under expert parallelism (several ranks) every rank must call ``step`` the same
+        number of times: a rank with nothing to run takes part in its peers' MoE exchanges
+        with a forward of one padding row."""
         sched = self.scheduler.schedule()
+        if self._ep_lockstep:
+            return self._ep_step(sched)
         if not sched.seqs:
             return []
+        return self._run(sched)
+
+    def _ep_step(self, sched) -> List[Sequence]:
+        """One lock-step of every expert-parallel rank.  One small all-reduce decides, for
+        all ranks alike: whether any rank has work (if none, nothing runs); whether the step
+        is eager (some rank prefills or samples, which takes the exchange's eager path with
+        its own per-call agreement) or every rank replays a captured decode graph; and which
+        decode graphs must be captured first (captures run collectively, since their warm-up
+        forwards exchange too).  A rank without work runs a one-padding-row forward."""
+        import torch.distributed as dist
+
+        r = self.runner
+        local_eager = bool(sched.seqs) and (not sched.is_decode or r.needs_sampling(sched.seqs))
+        need = torch.zeros(2 + len(r.buckets), dtype=torch.int64)
+        need[0] = int(local_eager)
+        need[1] = int(bool(sched.seqs))
+        if r.use_graphs:
+            n = len(sched.seqs) if sched.seqs and sched.is_decode else 1
+            need[2 + r.bucket_index(n)] = 1
+        dev = self.device if dist.get_backend() == "nccl" else torch.device("cpu")
+        need = need.to(dev)
+        dist.all_reduce(need)
+        need = need.cpu().tolist()
+        if not need[1]:
+            self._ep_all_done = True
+            return []
+        self._ep_all_done = False
+        eager = bool(need[0])
+        if r.use_graphs and not eager:
+            for i, b in enumerate(r.buckets):  # same buckets, same order, on every rank
+                if need[2 + i] and b not in r.graphs:
+                    r._copy_in(b)
+                    r.capture(b)
+        if not sched.seqs:
+            r.idle_step(eager=eager)
+            return []
+        return self._run(sched, eager=eager)
+
+    def _run(self, sched, eager: bool = False) -> List[Sequence]:
         if self.health is not None:
             self.health.check()
         t0 = time.perf_counter()
         try:
             with tracing.nvtx_range("decode" if sched.is_decode else "prefill"):
                 if sched.is_decode:
-                    toks = self.runner.decode(sched.seqs)
+                    toks = self.runner.decode(sched.seqs, eager=eager)
                 else:
                     toks = self.runner.prefill(sched.seqs, sched.query_lens, self._embeds(sched))
         except Exception as e:  # fail the step's requests, keep serving others
@@ -360,7 +409,9 @@ class LLMEngine:
 
     def generate(self, prompts: List[Seq[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
         ids = [self.add_request(p, params) for p in prompts]
-        while self.has_unfinished():
+        self._ep_all_done = False
+        # expert parallelism: keep stepping (idle) until every rank is done
+        while self.has_unfinished() or (self._ep_lockstep and not self._ep_all_done):
             self.step()
         out = []
         for i in ids:

@@ -134,11 +134,12 @@ class ModelRunner:
         self.graphs[B] = g
         self.graph_out[B] = out
 
-    def _prepare_decode(self, seqs: List[Sequence]) -> int:
+    def _prepare_decode(self, seqs: List[Sequence], B: Optional[int] = None) -> int:
         """Fills the pinned step buffers for ``seqs`` and copies them to the
-        device; returns the padded batch size."""
+        device; returns the padded batch size (``B``, or the graph bucket)."""
         n = len(seqs)
-        B = _bucket(n, self.buckets) if self.use_graphs else n
+        if B is None:
+            B = _bucket(n, self.buckets) if self.use_graphs else n
         bs = self.blocks.block_size
         pos = [s.length - 1 for s in seqs]
         self.n_ids[:n] = [s.last_token for s in seqs]
@@ -172,16 +173,51 @@ class ModelRunner:
         self._copy_in(B)
         return B
 
-    def decode(self, seqs: List[Sequence], return_logits: bool = False):
+    def bucket_index(self, n: int) -> int:
+        """Index in ``buckets`` of the padded decode batch size for ``n`` sequences."""
+        b = _bucket(n, self.buckets)
+        return self.buckets.index(b) if b in self.buckets else len(self.buckets) - 1
+
+    def needs_sampling(self, seqs: List[Sequence]) -> bool:
+        return self.sampler is not None and any(s.params.temperature > 0 for s in seqs)
+
+    def idle_step(self, eager: bool = False) -> None:
+        """A decode forward of padding rows only (no KV write, empty context, the dummy state
+        slot) whose only effect is taking part in the expert-parallel exchanges of a step that
+        the other ranks run: the smallest captured graph, or (``eager``) one row outside it."""
+        graphs = self.use_graphs and not eager
+        B = self.buckets[0] if graphs else 1
+        self.n_ids[:B] = 0
+        self.n_pos[:B] = 0
+        self.n_slots[:B] = -1
+        self.n_ctx[:B] = 0
+        self.n_sslot[:B] = self.pad_slot
+        for i in range(B):
+            if self._bt_rows[i] != (-1, 0, 0):
+                self.n_bt[i, :] = 0
+                self._bt_rows[i] = (-1, 0, 0)
+        self._copy_in(B)
+        if graphs:
+            self.graphs[B].replay()
+        else:
+            self.model.forward(self._fb_decode(B), self.kv, self.states)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+
+    def decode(self, seqs: List[Sequence], return_logits: bool = False, eager: bool = False):
+        """``eager``: run the forward outside the captured graphs (expert-parallel steps in
+        which another rank prefills)."""
         n = len(seqs)
-        B = self._prepare_decode(seqs)
-        sampling = self.sampler is not None and any(s.params.temperature > 0 for s in seqs)
+        graphs = self.use_graphs and not eager
+        B = _bucket(n, self.buckets) if graphs else n
+        B = self._prepare_decode(seqs, B)
+        sampling = self.needs_sampling(seqs)
         if return_logits:
             h = self.model.forward(self._fb_decode(B), self.kv, self.states)
             for s in seqs:
                 s.num_cached = s.length
             return self.model.logits(h)[:n].float()
-        if self.use_graphs and not sampling:
+        if graphs and not sampling:
             if B not in self.graphs:
                 self._copy_in(B)
                 self.capture(B)

@@ -51,7 +51,10 @@ class BatchManager:
         return list(self.engine.seqs[self.requests[request_id]].output)
 
     def run_all(self) -> Dict[Any, List[int]]:
-        while self.engine.has_unfinished():
+        eng = self.engine
+        if getattr(eng, "_ep_lockstep", False):
+            eng._ep_all_done = False
+        while eng.keep_stepping() if hasattr(eng, "keep_stepping") else eng.has_unfinished():
             self.step()
         return {rid: self.get_output(rid) for rid in self.requests}
 
@@ -105,9 +108,14 @@ class StreamingEngine:
             yield item
 
     def _loop(self):
+        # expert parallelism: the engine steps in lock-step with the other ranks, so this loop keeps
+        # stepping while idle (a short sleep when no rank has work) and stops when every rank has
+        # asked to (``LLMEngine.request_stop``)
+        lockstep = getattr(self.engine, "_ep_lockstep", False)
         while True:
             with self._lock:
-                while not self._stop and not self._pq and not self._cancel and not self.engine.has_unfinished():
+                while (not lockstep and not self._stop and not self._pq and not self._cancel
+                       and not self.engine.has_unfinished()):
                     self._cv.wait(timeout=0.1)
                 if self._cancel:
                     for rid in self._cancel:
@@ -126,7 +134,9 @@ class StreamingEngine:
                     self._cancel.clear()
                 # pending cancellations are applied even at shutdown, so their blocks are freed
                 if self._stop:
-                    return
+                    if not lockstep:
+                        return
+                    self.engine.request_stop()
                 while self._pq:
                     _, rid, ids, params, images = heapq.heappop(self._pq)
                     q = self._streams[rid]
@@ -145,12 +155,19 @@ class StreamingEngine:
                 if q is not None:
                     q.put(RuntimeError(s.error) if s.status == SeqStatus.FAILED else None)
                     self.stats["completed"] += 1
+            if lockstep:
+                if self.engine.ep_stopped:
+                    return
+                if self.engine._ep_all_done:
+                    time.sleep(0.001)
 
-    def shutdown(self):
+    def shutdown(self, timeout: float = 10.0):
+        """Stops the engine thread.  Under expert parallelism the thread ends once every rank
+        has shut down, so this waits up to ``timeout`` seconds for the peers."""
         with self._lock:
             self._stop = True
             self._cv.notify()
-        self._thread.join(timeout=10)
+        self._thread.join(timeout=timeout)
 
 
 class ReplicaRouter:

@@ -222,6 +222,9 @@ class LLMEngine:
         # exchange, so the ranks step together (see ``_ep_step``)
         self._ep_lockstep = self.expert_parallel and world > 1 and moe_impl is not None
         self._ep_all_done = False
+        self._ep_world = world
+        self._ep_stop_requested = False
+        self.ep_stopped = False   # every rank asked to stop: no further exchanges
 
     @classmethod
     def from_preset(cls, name: str, **kw) -> "LLMEngine":
@@ -331,6 +334,17 @@ class LLMEngine:
             return []
         return self._run(sched)
 
+    def keep_stepping(self) -> bool:
+        """True while this rank must keep calling ``step``: it has work, or (expert
+        parallelism) another rank may still have some."""
+        return self.has_unfinished() or (self._ep_lockstep and not self._ep_all_done and not self.ep_stopped)
+
+    def request_stop(self) -> None:
+        """Expert parallelism: this rank will serve no more requests.  Stepping stops on every
+        rank (``ep_stopped``) once all ranks have asked; until then this rank keeps taking
+        part in its peers' steps."""
+        self._ep_stop_requested = True
+
     def _ep_step(self, sched) -> List[Sequence]:
         """One lock-step of every expert-parallel rank.  One small all-reduce decides, for
         all ranks alike: whether any rank has work (if none, nothing runs); whether the step
@@ -340,18 +354,25 @@ class LLMEngine:
         forwards exchange too).  A rank without work runs a one-padding-row forward."""
         import torch.distributed as dist
 
+        if self.ep_stopped:
+            return []
         r = self.runner
         local_eager = bool(sched.seqs) and (not sched.is_decode or r.needs_sampling(sched.seqs))
-        need = torch.zeros(2 + len(r.buckets), dtype=torch.int64)
+        need = torch.zeros(3 + len(r.buckets), dtype=torch.int64)
         need[0] = int(local_eager)
         need[1] = int(bool(sched.seqs))
+        need[2] = int(self._ep_stop_requested and not sched.seqs)
         if r.use_graphs:
             n = len(sched.seqs) if sched.seqs and sched.is_decode else 1
-            need[2 + r.bucket_index(n)] = 1
+            need[3 + r.bucket_index(n)] = 1
         dev = self.device if dist.get_backend() == "nccl" else torch.device("cpu")
         need = need.to(dev)
         dist.all_reduce(need)
         need = need.cpu().tolist()
+        if need[2] == self._ep_world:  # every rank is idle and asked to stop
+            self.ep_stopped = True
+            self._ep_all_done = True
+            return []
         if not need[1]:
             self._ep_all_done = True
             return []
@@ -359,7 +380,7 @@ class LLMEngine:
         eager = bool(need[0])
         if r.use_graphs and not eager:
             for i, b in enumerate(r.buckets):  # same buckets, same order, on every rank
-                if need[2 + i] and b not in r.graphs:
+                if need[3 + i] and b not in r.graphs:
                     r._copy_in(b)
                     r.capture(b)
         if not sched.seqs:
@@ -411,7 +432,7 @@ class LLMEngine:
         ids = [self.add_request(p, params) for p in prompts]
         self._ep_all_done = False
         # expert parallelism: keep stepping (idle) until every rank is done
-        while self.has_unfinished() or (self._ep_lockstep and not self._ep_all_done):
+        while self.keep_stepping():
             self.step()
         out = []
         for i in ids:

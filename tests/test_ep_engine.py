@@ -65,3 +65,41 @@ def _worker(rank, world, port, empty_rank):
 @pytest.mark.parametrize("world,empty_rank", [(2, 1), (4, 0)])
 def test_ep_engine_uneven_load_matches_single_process(world, empty_rank):
     mp.spawn(_worker, args=(world, _port(), empty_rank), nprocs=world, join=True)
+
+
+def _stream_worker(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+
+    from mod_b200.api.managers import StreamingEngine
+    from mod_b200.config import get_preset
+    from mod_b200.engine import SamplingParams
+    from mod_b200.engine.llm_engine import LLMEngine
+    from mod_b200.parallel import dist as mdist
+
+    mdist.init(backend="gloo")
+    cfg = get_preset("tiny-moe")
+    g = torch.Generator().manual_seed(30)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (6, 11)]
+    params = SamplingParams(max_new_tokens=5)
+    ep = LLMEngine(cfg, backend="torch", device="cpu", max_batch=4, max_model_len=64, expert_parallel=True,
+                   use_graphs=False)
+    front = StreamingEngine(ep)
+    got = []
+    if rank == 0:  # rank 1 serves nothing: its loop only joins rank 0's exchanges
+        rids = [front.submit_request(p, params) for p in prompts]
+        got = [list(front.generate_stream(r, timeout=120)) for r in rids]
+    front.shutdown(timeout=180)        # returns once every rank has shut down
+    assert not front._thread.is_alive() and ep.ep_stopped, f"rank {rank}: engine thread still running"
+    if rank == 0:
+        ref = LLMEngine(cfg, backend="torch", device="cpu", max_batch=4, max_model_len=64, expert_parallel=False,
+                        use_graphs=False).generate(prompts, params)
+        assert all(x[:2] == y[:2] for x, y in zip(got, ref)), (got, ref)
+        assert sum(a == b for x, y in zip(got, ref) for a, b in zip(x, y)) >= 0.9 * sum(len(y) for y in ref)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_streaming_front_end_with_an_idle_rank():
+    mp.spawn(_stream_worker, args=(2, _port()), nprocs=2, join=True)

@@ -256,8 +256,8 @@ class AsyncEngine:
     """
 
     def __init__(self, engine, max_queue: int = 1024):
-        self.streaming = (engine if isinstance(engine, (StreamingEngine, ReplicaRouter))
-                          else StreamingEngine(engine, max_queue))
+        # a streaming front-end (StreamingEngine, ReplicaRouter, DistributedFrontEnd) is used as is
+        self.streaming = engine if hasattr(engine, "submit_request") else StreamingEngine(engine, max_queue)
 
     async def stream(self, token_ids: List[int], params: Optional[SamplingParams] = None, priority: int = 0,
                      images=None):

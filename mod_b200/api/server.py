@@ -71,7 +71,7 @@ def create_app(engine, tokenizer=None, model_name: str = "model"):
 
     app = FastAPI(title="mod_b200", version="0.1.0", lifespan=lifespan)
     app.state.front = front
-    m = _Metrics(engine)
+    m = _Metrics(getattr(engine, "engine", engine))  # a front-end's engine
 
     def _ids(req: CompletionRequest) -> List[int]:
         if isinstance(req.prompt, list):
@@ -227,6 +227,8 @@ class _Metrics:
         from prometheus_client import CONTENT_TYPE_LATEST, generate_latest
 
         e = self.engine
+        if not hasattr(e, "scheduler"):  # a router over several engines: no single scheduler to report
+            return generate_latest(self.registry), CONTENT_TYPE_LATEST
         self.running.set(len(e.scheduler.running))
         self.waiting.set(len(e.scheduler.waiting))
         self.free_blocks.set(e.blocks.num_free)

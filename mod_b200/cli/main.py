@@ -214,14 +214,39 @@ def cmd_trace(args) -> int:
 
 
 def cmd_serve(args) -> int:
+    """One process: the server over its engine.  Under ``torch.distributed.run`` (one process
+    per GPU): every rank builds its part of the model (``--set tp=N`` for tensor parallelism;
+    MoE models are expert parallel), rank 0 serves HTTP through a front-end that broadcasts the
+    requests, and the other ranks run the same loop without a server."""
+    import os
+
     from ..api.server import serve
 
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    opts = _opts(args)
+    if world > 1:
+        from ..parallel import dist as mdist
+
+        info = mdist.init()
+        if opts.get("device", "cuda") != "cpu":
+            opts["device"] = f"cuda:{info.local_rank}"
     pm = _pm()
-    if not pm.activate_plugin(args.model, **_opts(args)):
+    if not pm.activate_plugin(args.model, **opts):
         print("initialisation failed", file=sys.stderr)
         return 1
     p = pm.get_plugin(args.model)
-    serve(p.engine, p.tokenizer, args.model, host=args.host, port=args.port)
+    if world == 1:
+        serve(p.engine, p.tokenizer, args.model, host=args.host, port=args.port)
+        return 0
+    from ..api.dist_front import DistributedFrontEnd
+
+    eng = p.engine
+    mode = "tp" if eng.tensor_parallel else ("ep" if eng.expert_parallel else "dp")
+    front = DistributedFrontEnd(eng, mode)
+    if front.rank == 0:
+        serve(front, p.tokenizer, args.model, host=args.host, port=args.port)
+    else:
+        front.run()
     return 0
 
 
@@ -278,7 +303,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--hbm-gb", type=float, default=180.0)
     p.add_argument("--int8", action="store_true")
     p.set_defaults(fn=cmd_plan)
-    p = sub.add_parser("serve", help="HTTP completions server over one engine")
+    p = sub.add_parser("serve", help="HTTP completions server (one engine, or one per GPU under torchrun)")
     p.add_argument("model")
     p.add_argument("--device")
     p.add_argument("--backend", choices=["native", "torch", "cpu"])

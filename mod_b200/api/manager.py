@@ -259,6 +259,11 @@ def register_defaults(m: SecondaryPluginManager) -> SecondaryPluginManager:
 
         return ep.NcclEPMoE if parallelism == "ep" else tp.NcclTP
 
+    def nvls_comm(parallelism="ep", **kw):
+        from ..parallel import ep_agrs, tp
+
+        return ep_agrs.AgRsEPMoE if parallelism == "ep" else tp.NvlsTP
+
     def admission(**kw):
         from .managers import AdaptiveAdmission
 
@@ -299,6 +304,9 @@ def register_defaults(m: SecondaryPluginManager) -> SecondaryPluginManager:
         call=lambda inst, *a, **k: inst.report()))
     m.register_plugin(T.DISTRIBUTED_EXECUTION, SecondaryPlugin(
         "fused-nvlink", fused_comm, "in-kernel NVLink dispatch/combine (EP) and fused TP boundaries",
+        call=lambda inst, *a, **k: inst(*a, **k) if a or k else inst))
+    m.register_plugin(T.DISTRIBUTED_EXECUTION, SecondaryPlugin(
+        "nvls", nvls_comm, "NVLink multicast: in-switch reduce + multicast stores (TP boundaries, EP decode)",
         call=lambda inst, *a, **k: inst(*a, **k) if a or k else inst))
     m.register_plugin(T.DISTRIBUTED_EXECUTION, SecondaryPlugin(
         "nccl", nccl_comm, "NCCL all-to-all / all-reduce with library GEMMs (baseline)",

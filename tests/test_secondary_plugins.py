@@ -8,7 +8,7 @@ def test_defaults_cover_every_kind():
     m = get_secondary_plugin_manager()
     listing = m.list()
     assert all(listing[k.value] for k in T), listing
-    assert set(listing["distributed_execution"]) == {"fused-nvlink", "nccl"}
+    assert set(listing["distributed_execution"]) == {"fused-nvlink", "nvls", "nccl"}
 
 
 def test_activate_execute_deactivate():
@@ -21,6 +21,8 @@ def test_activate_execute_deactivate():
     assert isinstance(m.execute_plugin(T.MEMORY_MANAGER), dict)
     assert m.activate_plugin(T.DISTRIBUTED_EXECUTION, "nccl", parallelism="ep")
     assert m.execute_plugin(T.DISTRIBUTED_EXECUTION).__name__ == "NcclEPMoE"
+    assert m.activate_plugin(T.DISTRIBUTED_EXECUTION, "nvls", parallelism="tp")
+    assert m.execute_plugin(T.DISTRIBUTED_EXECUTION).__name__ == "NvlsTP"
     assert m.deactivate_plugin(T.SHARDING) and m.execute_plugin(T.SHARDING) is None
 
 

@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--impl", default="native", choices=["native", "baseline", "reference"])
     p.add_argument("--model", default=MODEL)
     p.add_argument("--batch", type=int, default=128)
+    p.add_argument("--attn", default="dp", choices=["dp", "tp"],
+                   help="N > 1: attention data-parallel (each rank its batch/N sequences) or tensor-parallel "
+                        "(every rank all sequences, its heads); experts are expert-parallel either way")
     p.add_argument("--prompt-len", type=int, default=512)
     p.add_argument("--profile", action="store_true",
                    help="after the timed runs, print per-kernel device times of one decode step to stderr")
@@ -217,8 +220,9 @@ def main():
     cfg = get_preset(args.model)
     if args.layers:
         cfg.num_hidden_layers = args.layers
-    per_rank = args.batch // world
-    assert per_rank * world == args.batch, "global batch must divide by the GPU count"
+    tp_attn = world > 1 and args.attn == "tp"
+    per_rank = args.batch if tp_attn else args.batch // world
+    assert tp_attn or per_rank * world == args.batch, "global batch must divide by the GPU count"
     K, W = args.steps, args.warmup
     backend = "native" if args.impl == "native" else "torch"
     max_len = args.prompt_len + W + 3 * K + 16
@@ -226,10 +230,11 @@ def main():
     # collectives), which keeps its decode step free of host syncs and so CUDA-graph capturable
     ep = True if (backend == "torch" and cfg.is_moe) else None
     eng = LLMEngine(cfg, backend=backend, device=dev, max_batch=per_rank, max_model_len=max_len,
-                    max_prefill_tokens=16384, seed=0, use_graphs=True, expert_parallel=ep)
+                    max_prefill_tokens=16384, seed=0, use_graphs=True, expert_parallel=ep,
+                    tensor_parallel=tp_attn)
     if world > 1:
         dist.barrier()
-    g = torch.Generator().manual_seed(1000 + rank)
+    g = torch.Generator().manual_seed(1000 + (0 if tp_attn else rank))  # TP: every rank the same requests
     prompts = [torch.randint(0, cfg.vocab_size, (args.prompt_len,), generator=g).tolist() for _ in range(per_rank)]
     params = SamplingParams(max_new_tokens=W + 3 * K + 8, ignore_eos=True)
     if world > 1:
@@ -308,7 +313,7 @@ def main():
             "dtype": "bf16", "data": "synthetic (uniform-random token ids, random-init N(0,0.02) weights, seed 0)",
             "impl": args.impl,
             "config": {"model": cfg.name, "global_batch": args.batch, "seq_len": args.prompt_len,
-                       "parallelism": f"ep{world}+dp_attn{world}" if world > 1 else "single",
+                       "parallelism": (f"ep{world}+{args.attn}_attn{world}" if world > 1 else "single"),
                        "layers": cfg.num_hidden_layers, "decode_batch_per_gpu": per_rank,
                        "moe_exchange": type(getattr(eng.model, "moe_impl", None)).__name__,
                        "timed": "CUDA-graph replays of the decode step, context advanced on the device each step",

@@ -88,22 +88,49 @@ class LLMEngine:
             from ..models.tp_decoder import TPDecoderLM, shard_weights
             from ..parallel.tp import make_tp_comm
 
+            # hybrid (DeltaNet) or MoE models: heads split, experts expert-parallel over the same ranks
+            hybrid = cfg.is_moe or any(cfg.layer_type(i) == "linear_attention"
+                                       for i in range(cfg.num_hidden_layers))
             if model_path is not None and weights is None:
+                assert not hybrid, "tensor-parallel checkpoint loading covers dense decoders"
                 from ..io.hf_loader import load_hf
 
                 shard = load_hf(cfg, model_path, device=self.device, dtype=wdt, tp=(rank, world))
             else:
-                if weights is None:
-                    weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed)
-                shard = shard_weights(cfg, weights, rank, world)
+                if weights is None:  # MoE: only this rank's experts are made
+                    er = None
+                    if cfg.is_moe:
+                        El = cfg.num_experts // world
+                        er = (rank * El, (rank + 1) * El)
+                    weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed, expert_range=er)
+                if hybrid:
+                    from ..models.tp_hybrid import shard_hybrid_weights
+
+                    shard = shard_hybrid_weights(cfg, weights, rank, world)
+                else:
+                    shard = shard_weights(cfg, weights, rank, world)
             weights = None
             mt = max(max_batch, max_prefill_tokens)
             # boundary flavour: P2P peer stores (default), NVLS multimem, or the NCCL baseline
             kind = tp_comm or os.environ.get("MB_TP_COMM", "auto")
             comm = make_tp_comm(kind if backend == "native" else "nccl", cfg.hidden_size, mt)
-            model = TPDecoderLM(cfg, shard, self.backend, comm, world)
+            if hybrid:
+                from ..models.tp_hybrid import TPHybridLM
+                from ..parallel.ep import FusedEPMoE, NcclEPMoE
+                from ..parallel.tp import padded_tokens
+
+                tp_moe = None
+                if cfg.is_moe:  # the tokens a rank owns (its sequence-parallel rows) go through the exchange
+                    rows = padded_tokens(max_batch, world) // world
+                    tp_moe = (FusedEPMoE(cfg, self.backend, max_tokens=rows,
+                                         prefill_tokens=max(rows, min(2048, padded_tokens(mt, world) // world)))
+                              if backend == "native" else NcclEPMoE(cfg, self.backend, max_tokens=rows))
+                model = TPHybridLM(cfg, shard, self.backend, comm, world, moe_impl=tp_moe)
+            else:
+                model = TPDecoderLM(cfg, shard, self.backend, comm, world)
             kv_heads = model.Hkv
             expert_parallel = False
+            self.expert_parallel = False  # experts of a TP model are exchanged inside its MoE layers
         moe_impl = None
         if expert_parallel:
             El = cfg.num_experts // world
@@ -176,7 +203,11 @@ class LLMEngine:
         # decode step may write into (library-only path), so no live sequence's KV is touched
         self.kv = KVCache(cfg, num_blocks + 1, self.device, dtype=torch.float32 if backend == "cpu" else self.model.w.embed.dtype, block_size=bs, num_kv_heads=kv_heads or self.model.Hkv)
         has_delta = any(cfg.layer_type(i) == "linear_attention" for i in range(cfg.num_hidden_layers))
-        self.states = StateCache(cfg, max_batch + 1, self.device) if has_delta else None
+        if has_delta:  # a tensor-parallel model keeps only its heads' recurrent state
+            sc = getattr(self.model, "state_cache", None)
+            self.states = sc(max_batch + 1, self.device) if sc else StateCache(cfg, max_batch + 1, self.device)
+        else:
+            self.states = None
         # prefix caching shares KV blocks of common prompt prefixes; models with recurrent
         # (DeltaNet) state keep the plain manager, since their state is not in the KV blocks
         self.prefix_caching = bool(prefix_caching) and self.states is None

@@ -183,6 +183,37 @@ class DeltaNetLayer:
                                   dtb, nw, self.Hk, self.Hv, self.dk, self.dv, self.cfg.rms_norm_eps)
         return be.linear(o, self.w.out)
 
+    def core(self, be, mixed, z, ba, conv_state, ssm_state, fb):
+        """Conv, gates, delta rule and gated RMSNorm from already projected inputs (mixed q|k|v
+        channels, z, beta/decay logits) for every sequence of the step; returns the rows that
+        go into the output projection.  Tensor parallelism calls it with this rank's heads."""
+        if self._native(be, mixed):
+            A, dtb, cw, nw = self._gates_f32()
+            mixed, z, ba = mixed.contiguous(), z.contiguous(), ba.contiguous()
+            if fb.is_decode:
+                return be.N.deltanet_decode(mixed, z, ba, cw, conv_state, ssm_state, fb.state_slots, A, dtb, nw,
+                                            self.Hk, self.Hv, self.dk, self.dv, self.cfg.rms_norm_eps)
+            ql = torch.tensor(fb.query_lens, dtype=torch.int32)
+            cu = torch.zeros(len(fb.query_lens) + 1, dtype=torch.int32)
+            cu[1:] = ql.cumsum(0)
+            seq_of = torch.repeat_interleave(torch.arange(len(fb.query_lens), dtype=torch.int32), ql)
+            dev = mixed.device
+            return be.N.deltanet_prefill(mixed, z, ba, cw, conv_state, ssm_state, fb.state_slots, cu.to(dev),
+                                         seq_of.to(dev), A, dtb, nw, self.Hk, self.Hv, self.dk, self.dv,
+                                         self.cfg.rms_norm_eps)
+        w = self.w
+        if fb.is_decode:
+            o = ref_decode(mixed, z, ba, w.conv, w.A_log, w.dt_bias, w.norm, conv_state, ssm_state, fb.state_slots,
+                           *self._dims())
+            return o.to(mixed.dtype)
+        outs, start = [], 0
+        for b, ql in enumerate(fb.query_lens):
+            sl = slice(start, start + ql)
+            outs.append(ref_prefill(mixed[sl], z[sl], ba[sl], w.conv, w.A_log, w.dt_bias, w.norm, conv_state,
+                                    ssm_state, int(fb.state_slots[b]), *self._dims()))
+            start += ql
+        return torch.cat(outs, 0).to(mixed.dtype)
+
     def _dims(self):
         return self.Hk, self.Hv, self.dk, self.dv, self.cfg.rms_norm_eps
 

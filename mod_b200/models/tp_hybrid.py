@@ -132,13 +132,15 @@ class TPHybridLM:
         self.inv_freq = R.inv_freq(cfg.rotary_dim, cfg.rope_theta, device=self.device)
         self.delta = {i: DeltaNetLayer(cfg, L.delta, num_k_heads=self.hk, num_v_heads=self.hv)
                       for i, L in enumerate(weights.layers) if L.delta is not None}
-        # the mixer's column-parallel input weights, one GEMM per layer
+        # the mixer's column-parallel input weights, one GEMM per layer, padded with zero rows to a
+        # multiple of 128 outputs (the decode GEMMs' tile; the extra columns are never read)
         self.in_w = []
         for L in weights.layers:
-            if L.attn is not None:
-                self.in_w.append(L.attn.qkv)
-            else:
-                self.in_w.append(torch.cat([L.delta.in_qkvz, L.delta.in_ba]).contiguous())
+            w = L.attn.qkv if L.attn is not None else torch.cat([L.delta.in_qkvz, L.delta.in_ba])
+            pad = -w.shape[0] % 128
+            if pad:
+                w = torch.cat([w, w.new_zeros(pad, w.shape[1])])
+            self.in_w.append(w.contiguous())
         self.layer_source = None
 
     def state_cache(self, max_seqs: int, device) -> StateCache:
@@ -167,7 +169,8 @@ class TPHybridLM:
         layer = self.delta[i]
         kd, vd = self.hk * self.cfg.linear_key_head_dim, self.hv * self.cfg.linear_value_head_dim
         conv, ssm = states.layer(i)
-        return layer.core(self.be, y[:, :2 * kd + vd], y[:, 2 * kd + vd:2 * kd + 2 * vd], y[:, 2 * kd + 2 * vd:],
+        b0 = 2 * kd + 2 * vd
+        return layer.core(self.be, y[:, :2 * kd + vd], y[:, 2 * kd + vd:b0], y[:, b0:b0 + 2 * self.hv],
                           conv, ssm, fb)
 
     def forward(self, fb: ForwardBatch, kv: Optional[KVCache], states: Optional[StateCache] = None) -> torch.Tensor:

@@ -8,7 +8,9 @@ layer by layer so the bf16 model is never resident), uniform-random prompt
 ids.  Reports the prefill wall time of the batch (all prompts arrive at once,
 chunked by --prefill-tokens), and decode tokens/s: device-timed CUDA-graph
 replays (CUDA events) and end to end through ``LLMEngine.step()``.  Under
-``torch.distributed.run`` with N processes: expert parallelism over N GPUs with
+``torch.distributed.run`` with N processes: the TP/EP form (``--attn tp``, the
+default: DeltaNet and attention heads split over the ranks, experts expert-parallel),
+or expert parallelism with
 data-parallel attention (sequence i on rank i % N; ranks without a sequence take
 part in the MoE exchanges with padding rows), times as the max over ranks.
 """
@@ -30,6 +32,9 @@ def main(argv=None):
     ap.add_argument("--quant", default="int8", choices=["int8", "none"])
     ap.add_argument("--prefill-tokens", type=int, default=32768)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (smoke runs only)")
+    ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
+                    help="N > 1: heads tensor-parallel (every rank all sequences) or attention data-parallel "
+                         "(sequence i on rank i %% N); experts expert-parallel either way")
     a = ap.parse_args(argv)
     import os
 
@@ -53,7 +58,10 @@ def main(argv=None):
     if a.layers:
         cfg.num_hidden_layers = a.layers
         cfg.layer_types = cfg.layer_types[:a.layers]
-    per_rank = max(1, -(-a.batch // world))
+    tp_attn = world > 1 and a.attn == "tp"
+    if tp_attn and a.quant != "none":
+        raise SystemExit("the tensor-parallel form runs bf16 weights: pass --quant none (or --attn dp for int8)")
+    per_rank = a.batch if tp_attn else max(1, -(-a.batch // world))
     max_len = a.prompt_len + a.warmup + 3 * a.steps + 16
     t0 = time.perf_counter()
     if world == 1:
@@ -64,13 +72,14 @@ def main(argv=None):
                         max_prefill_tokens=a.prefill_tokens)
     else:  # this rank's experts (bf16 under expert parallelism), int8 projections with --quant int8
         eng = LLMEngine(cfg, backend="native", device=dev, max_batch=per_rank, max_model_len=max_len,
-                        max_prefill_tokens=a.prefill_tokens, expert_parallel=True, seed=0,
+                        max_prefill_tokens=a.prefill_tokens, expert_parallel=not tp_attn,
+                        tensor_parallel=tp_attn, seed=0,
                         quantization=None if a.quant == "none" else a.quant)
         torch.cuda.synchronize()
         init_s = time.perf_counter() - t0
     g = torch.Generator().manual_seed(7)
     prompts = [torch.randint(0, cfg.vocab_size, (a.prompt_len,), generator=g).tolist() for _ in range(a.batch)]
-    mine = prompts[rank::world]
+    mine = prompts if tp_attn else prompts[rank::world]
     params = SamplingParams(max_new_tokens=a.warmup + 3 * a.steps + 8, ignore_eos=True)
 
     def pending_anywhere(ids) -> bool:  # every rank must agree on when to stop stepping
@@ -120,7 +129,7 @@ def main(argv=None):
         print(json.dumps({"config": "qwen3-next hybrid (3 DeltaNet : 1 gated attention, 512 experts top-10 + shared)",
                           "quant": a.quant, "batch": a.batch, "prompt_len": a.prompt_len,
                           "layers": cfg.num_hidden_layers, "n_gpus": world,
-                          "parallelism": f"ep{world}+dp_attn{world}" if world > 1 else "single",
+                          "parallelism": f"ep{world}+{a.attn}_attn{world}" if world > 1 else "single",
                           "weights_init_s": round(init_s, 1), "prefill_s": round(prefill_s, 3),
                           "prefill_tok_s": round(a.batch * a.prompt_len / prefill_s, 1),
                           "decode_ms_per_step": round(dev_ms, 3), "decode_tok_s": round(a.batch / dev_ms * 1000, 1),

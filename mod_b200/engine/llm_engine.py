@@ -85,6 +85,8 @@ class LLMEngine:
         wdt = torch.float32 if backend == "cpu" else torch.bfloat16
         self.tensor_parallel = tensor_parallel and world > 1
         if self.tensor_parallel and model is None:
+            if quantization not in (None, "none"):
+                raise ValueError("tensor parallelism runs bf16 weights (int8 weight-only is single-GPU / EP)")
             from ..models.tp_decoder import TPDecoderLM, shard_weights
             from ..parallel.tp import make_tp_comm
 

@@ -82,6 +82,8 @@ class EnginePlugin(TextModelPluginInterface):
                 self.runtime["backend"] = "torch"
             if self.runtime["backend"] == "native":
                 for k, v in self.gpu_runtime_defaults.items():
+                    if k == "quantization" and int(self.runtime.get("tp", 1)) > 1:
+                        continue  # tensor parallelism runs bf16 weights
                     if k not in kwargs:
                         self.runtime[k] = v
             from ..io.tokenizer import load_tokenizer

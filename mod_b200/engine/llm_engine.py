@@ -93,17 +93,21 @@ class LLMEngine:
             # hybrid (DeltaNet) or MoE models: heads split, experts expert-parallel over the same ranks
             hybrid = cfg.is_moe or any(cfg.layer_type(i) == "linear_attention"
                                        for i in range(cfg.num_hidden_layers))
-            if model_path is not None and weights is None:
-                assert not hybrid, "tensor-parallel checkpoint loading covers dense decoders"
+            er = None  # MoE: only this rank's experts are read or made
+            if cfg.is_moe:
+                El = cfg.num_experts // world
+                er = (rank * El, (rank + 1) * El)
+            if model_path is not None and weights is None and not hybrid:
                 from ..io.hf_loader import load_hf
 
                 shard = load_hf(cfg, model_path, device=self.device, dtype=wdt, tp=(rank, world))
             else:
-                if weights is None:  # MoE: only this rank's experts are made
-                    er = None
-                    if cfg.is_moe:
-                        El = cfg.num_experts // world
-                        er = (rank * El, (rank + 1) * El)
+                if weights is None and model_path is not None:
+                    # hybrid / MoE checkpoint: this rank's experts, then the dense parts sliced by heads
+                    from ..io.hf_loader import load_hf
+
+                    weights = load_hf(cfg, model_path, device=self.device, dtype=wdt, expert_range=er)
+                elif weights is None:
                     weights = random_weights(cfg, device=self.device, dtype=wdt, seed=seed, expert_range=er)
                 if hybrid:
                     from ..models.tp_hybrid import shard_hybrid_weights

@@ -4,6 +4,7 @@ together, and gloo CPU ranks running the TP engine (heads split, experts
 expert-parallel over the same ranks) reproduce the single-process engine."""
 import os
 import socket
+import sys
 
 import pytest
 import torch
@@ -55,6 +56,7 @@ def _worker(rank, world, port, preset):
     from mod_b200.models.tp_hybrid import TPHybridLM
     from mod_b200.parallel import dist as mdist
 
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     mdist.init(backend="gloo")
     cfg = get_preset(preset)
     g = torch.Generator().manual_seed(3)
@@ -72,6 +74,17 @@ def _worker(rank, world, port, preset):
     # exactly and the rest nearly all (a near-tied greedy choice of this random model can flip)
     assert all(x[:2] == y[:2] for x, y in zip(out, ref)), (rank, out, ref)
     assert sum(a == b for x, y in zip(out, ref) for a, b in zip(x, y)) >= 0.9 * sum(len(y) for y in ref)
+    if preset == "tiny-moe":  # the same TP engine from an HF checkpoint: experts and heads read per rank
+        import tempfile
+
+        from mod_b200.io.safetensors import save_file
+        from tests.test_io import _hf_from_fused
+
+        with tempfile.TemporaryDirectory() as d:
+            save_file(os.path.join(d, "model.safetensors"), _hf_from_fused(cfg, w), {})
+            ck = LLMEngine(cfg, backend="torch", device="cpu", max_batch=4, max_model_len=64, tensor_parallel=True,
+                           use_graphs=False, model_path=d, weights=None)
+            assert ck.generate(prompts, params) == out, rank
     dist.barrier()
     dist.destroy_process_group()
 

@@ -9,7 +9,7 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
-def run(rank, world, backend, port, device_kind):
+def run(rank, world, backend, port, device_kind, preset="tiny-dense"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     from mod_b200.config import get_preset
@@ -21,8 +21,9 @@ def run(rank, world, backend, port, device_kind):
     mdist.init(backend="gloo" if device_kind == "cpu" else "nccl")
     dev = torch.device("cpu") if device_kind == "cpu" else torch.device("cuda", rank)
     dtype = torch.float32 if device_kind == "cpu" else torch.bfloat16
-    cfg = get_preset("tiny-dense")
-    cfg.num_attention_heads, cfg.num_key_value_heads = max(8, 2 * world), max(4, world)  # heads divide the ranks
+    cfg = get_preset(preset)
+    if preset == "tiny-dense":
+        cfg.num_attention_heads, cfg.num_key_value_heads = max(8, 2 * world), max(4, world)  # heads divide the ranks
     w = random_weights(cfg, device=dev, dtype=dtype, seed=0)
     g = torch.Generator().manual_seed(3)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (7, 19, 3)]
@@ -58,4 +59,5 @@ def run(rank, world, backend, port, device_kind):
 
 
 if __name__ == "__main__":
-    run(int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), sys.argv[1], int(os.environ["MASTER_PORT"]), "cuda")
+    run(int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), sys.argv[1], int(os.environ["MASTER_PORT"]), "cuda",
+        sys.argv[2] if len(sys.argv) > 2 else "tiny-dense")

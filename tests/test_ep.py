@@ -133,3 +133,18 @@ def test_tp_nvls_multi_gpu(cuda):
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), "native"]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("preset", ["tiny-next", "tiny-moe"])
+def test_tp_hybrid_multi_gpu(cuda, preset):
+    """Tensor-parallel hybrid / MoE model on 2 GPUs (heads split, experts expert-parallel) against the
+    single-process engine."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MB_TP_COMM="p2p")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_tp_worker.py"), "native",
+           preset]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

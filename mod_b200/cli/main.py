@@ -254,7 +254,8 @@ def cmd_plan(args) -> int:
     from ..config import get_preset
     from ..parallel.planner import plan
 
-    p = plan(get_preset(args.model), args.gpus, hbm_bytes=int(args.hbm_gb * 1e9), int8=args.int8)
+    p = plan(get_preset(args.model), args.gpus, hbm_bytes=int(args.hbm_gb * 1e9), int8=args.int8,
+             attn=getattr(args, "attn", "dp"))
     print(json.dumps(p.as_dict(), indent=1))
     return 0 if p.fits else 2
 
@@ -302,6 +303,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--gpus", type=int, default=8)
     p.add_argument("--hbm-gb", type=float, default=180.0)
     p.add_argument("--int8", action="store_true")
+    p.add_argument("--attn", default="dp", choices=["dp", "tp"], help="MoE models: attention data- or tensor-parallel")
     p.set_defaults(fn=cmd_plan)
     p = sub.add_parser("serve", help="HTTP completions server (one engine, or one per GPU under torchrun)")
     p.add_argument("model")

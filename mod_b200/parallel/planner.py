@@ -105,9 +105,27 @@ def _tp_degree(cfg, n: int) -> int:
     return t
 
 
+def _tp_degree_heads(cfg, n: int) -> int:
+    """Largest tensor-parallel degree dividing ``n`` whose head split the hybrid / MoE decoder
+    supports: query heads split evenly, KV heads split evenly or each rank's query heads share
+    one KV head, DeltaNet key and value heads split evenly."""
+    Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    t = 1
+    for d in range(1, n + 1):
+        if n % d or Hq % d:
+            continue
+        kv_ok = Hkv % d == 0 or (d % Hkv == 0 and (Hq // Hkv) % (Hq // d) == 0)
+        lin_ok = all(h % d == 0 for h in (cfg.linear_num_key_heads, cfg.linear_num_value_heads) if h)
+        if kv_ok and lin_ok:
+            t = d
+    return t
+
+
 def plan(cfg, n_gpus: int, hbm_bytes: int = 180 * 10**9, reserve_bytes: int = 6 * GIB,
-         workspace_bytes: int = 2 * GIB, block_size: int = 16, int8: bool = False) -> Plan:
-    """Placement of ``cfg`` on ``n_gpus`` GPUs of ``hbm_bytes`` each."""
+         workspace_bytes: int = 2 * GIB, block_size: int = 16, int8: bool = False, attn: str = "dp") -> Plan:
+    """Placement of ``cfg`` on ``n_gpus`` GPUs of ``hbm_bytes`` each.  MoE models put their
+    experts expert-parallel; ``attn`` picks their attention: ``"dp"`` (each GPU its own
+    sequences, replicated attention weights) or ``"tp"`` (heads split over the GPUs)."""
     if n_gpus < 1:
         raise ValueError("need at least one GPU")
     w = weight_bytes(cfg, int8_projections=int8)
@@ -122,7 +140,16 @@ def plan(cfg, n_gpus: int, hbm_bytes: int = 180 * 10**9, reserve_bytes: int = 6 
         p.ep, p.dp = ep, n_gpus // ep
         per_gpu = w.total - w.experts + w.experts // ep
         kv_heads = cfg.num_key_value_heads
-        p.notes.append(f"expert parallel {ep}: {cfg.num_experts // ep} experts per GPU, data-parallel attention")
+        tp = _tp_degree_heads(cfg, ep) if attn == "tp" else 1
+        if tp > 1:
+            p.tp = tp
+            sharded = w.attention + w.deltanet
+            per_gpu -= sharded - sharded // tp
+            kv_heads = max(1, cfg.num_key_value_heads // tp)
+            p.notes.append(f"expert parallel {ep}: {cfg.num_experts // ep} experts per GPU, "
+                           f"attention / DeltaNet heads tensor-parallel {tp}")
+        else:
+            p.notes.append(f"expert parallel {ep}: {cfg.num_experts // ep} experts per GPU, data-parallel attention")
     else:
         tp = _tp_degree(cfg, n_gpus)
         p.tp, p.dp = tp, n_gpus // tp

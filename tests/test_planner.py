@@ -52,3 +52,10 @@ def test_cli_plan(capsys):
     assert main(["plan", "qwen3-30b-a3b", "--gpus", "8"]) == 0
     out = json.loads(capsys.readouterr().out)
     assert out["ep"] == 8 and out["fits"]
+
+
+def test_moe_with_tensor_parallel_attention():
+    nx = plan(get_preset("qwen3-next"), 8, attn="tp")           # 16 q / 2 KV heads, 16 / 32 DeltaNet heads
+    assert nx.tp == 8 and nx.ep == 8 and nx.fits
+    assert nx.weight_bytes_per_gpu < plan(get_preset("qwen3-next"), 8).weight_bytes_per_gpu
+    assert plan(get_preset("qwen3-30b-a3b"), 8, attn="tp").tp == 8   # 32 q / 4 KV heads: KV replicated x2

@@ -30,6 +30,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--quant", default="int8", choices=["int8", "none"])
+    ap.add_argument("--impl", default="native", choices=["native", "baseline"],
+                    help="baseline: PyTorch + cuBLAS + NCCL (library exchange and GEMMs, same engine)")
     ap.add_argument("--prefill-tokens", type=int, default=32768)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (smoke runs only)")
     ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
@@ -59,6 +61,9 @@ def main(argv=None):
         cfg.num_hidden_layers = a.layers
         cfg.layer_types = cfg.layer_types[:a.layers]
     tp_attn = world > 1 and a.attn == "tp"
+    backend = "native" if a.impl == "native" else "torch"
+    if backend == "torch" and a.quant != "none":
+        raise SystemExit("the library baseline runs bf16 weights: pass --quant none")
     if tp_attn and a.quant != "none":
         raise SystemExit("the tensor-parallel form runs bf16 weights: pass --quant none (or --attn dp for int8)")
     per_rank = a.batch if tp_attn else max(1, -(-a.batch // world))
@@ -68,10 +73,10 @@ def main(argv=None):
         w = random_weights(cfg, device=dev, seed=0, quantize=None if a.quant == "none" else a.quant)
         torch.cuda.synchronize()
         init_s = time.perf_counter() - t0
-        eng = LLMEngine(cfg, weights=w, backend="native", device=dev, max_batch=a.batch, max_model_len=max_len,
+        eng = LLMEngine(cfg, weights=w, backend=backend, device=dev, max_batch=a.batch, max_model_len=max_len,
                         max_prefill_tokens=a.prefill_tokens)
     else:  # this rank's experts (bf16 under expert parallelism), int8 projections with --quant int8
-        eng = LLMEngine(cfg, backend="native", device=dev, max_batch=per_rank, max_model_len=max_len,
+        eng = LLMEngine(cfg, backend=backend, device=dev, max_batch=per_rank, max_model_len=max_len,
                         max_prefill_tokens=a.prefill_tokens, expert_parallel=not tp_attn,
                         tensor_parallel=tp_attn, seed=0,
                         quantization=None if a.quant == "none" else a.quant)
@@ -127,7 +132,7 @@ def main(argv=None):
     check_status(dev)
     if rank == 0:
         print(json.dumps({"config": "qwen3-next hybrid (3 DeltaNet : 1 gated attention, 512 experts top-10 + shared)",
-                          "quant": a.quant, "batch": a.batch, "prompt_len": a.prompt_len,
+                          "impl": a.impl, "quant": a.quant, "batch": a.batch, "prompt_len": a.prompt_len,
                           "layers": cfg.num_hidden_layers, "n_gpus": world,
                           "parallelism": f"ep{world}+{a.attn}_attn{world}" if world > 1 else "single",
                           "weights_init_s": round(init_s, 1), "prefill_s": round(prefill_s, 3),
